@@ -1,0 +1,84 @@
+"""The CPU oracle against fixtures produced by the reference's own code (tests/golden/make_golden.py)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import moe_oracle as O
+
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    return np.load(os.path.join(G, name))
+
+
+def test_e4m3_encode_matches_torch():
+    d = load("e4m3_golden.npz")
+    assert np.array_equal(O.e4m3_encode(d["values"]), d["codes"])
+
+
+@pytest.mark.parametrize("case", ["a", "b", "c", "d"])
+def test_quantize_matches_engine_fp4(case):
+    d = load("quant_golden.npz")
+    x, g = d[f"{case}_x"], d[f"{case}_g"]
+    assert O.global_scale_from_amax(d[f"{case}_amax"]) == g
+    packed, s8 = O.quantize_rows(x, g)
+    assert np.array_equal(packed, d[f"{case}_packed"])
+    assert np.array_equal(O.to_blocked(s8), d[f"{case}_sf"])
+
+
+def test_swizzle_roundtrip():
+    rng = np.random.default_rng(0)
+    s = rng.integers(0, 255, size=(300, 44), dtype=np.uint8)
+    flat = O.to_blocked(s)
+    assert flat.size == 3 * 11 * 512
+    assert np.array_equal(O.from_blocked(flat, 300, 44), s)
+
+
+@pytest.mark.parametrize("name", ["e128k8", "e64k4"])
+def test_route_matches_vllm_torch(name):
+    d = load("route_golden.npz")
+    k = d[f"{name}_ids"].shape[1]
+    w, ids = O.route(d[f"{name}_logits"], k, d[f"{name}_scale"])
+    assert np.array_equal(ids, d[f"{name}_ids"])                 # bit-exact routing indices
+    np.testing.assert_allclose(w, d[f"{name}_w"], rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("act", ["gelu_tanh", "silu"])
+def test_layer_matches_reference_composition(act):
+    d = load("layer_golden.npz")
+    p = act + "_"
+    x, ids, w = d[p + "x"], d[p + "topk_ids"], d[p + "topk_w"]
+    wr, idr = O.route(d[p + "logits"], ids.shape[1])
+    assert np.array_equal(idr, ids)
+    r = O.moe_forward(x, w, ids, d[p + "w1_fp4"], d[p + "w1_sf"], d[p + "w1_alphas"], d[p + "w2_fp4"],
+                      d[p + "w2_sf"], d[p + "w2_alphas"], d[p + "a1_gscale"], d[p + "a2_gscale"], act)
+    # the routed input rows quantise to exactly the reference's bytes (engine/fp4.py with the same scale)
+    T, k = ids.shape
+    cm = r["plan"]["c_map"].reshape(T, k)
+    assert np.array_equal(r["rep_fp4"][cm], d[p + "rep_rows_packed"])
+    # output within the north-star tolerance of the reference composition (bf16 layer output)
+    ref = d[p + "out"]
+    diff = np.abs(r["out"] - ref)
+    assert diff.max() <= 2e-2
+    assert np.linalg.norm(r["out"] - ref) <= 1e-2 * np.linalg.norm(ref)
+    c3 = r["c3"][cm]
+    np.testing.assert_allclose(c3, d[p + "c3"], atol=2e-2, rtol=0)
+
+
+def test_plan_canonical_order():
+    ids = np.array([[3, 1], [1, 0], [3, 0], [2, 1]], dtype=np.int32)
+    pl = O.plan(ids, 4)
+    assert pl["counts"].tolist() == [2, 3, 1, 2]
+    assert pl["expert_offsets"].tolist() == [0, 2, 5, 6, 8]
+    assert pl["blockscale_offsets"].tolist() == [0, 128, 256, 384, 512]
+    # inside an expert, slots follow token order
+    assert pl["a_map"].tolist() == [1, 2, 0, 1, 3, 3, 0, 2]
+    assert pl["c_map"].tolist() == [6, 2, 3, 0, 7, 1, 5, 4]
+
+
+def test_combine_order_top8():
+    assert O.combine_order(8) == [[0, 4], [1, 5], [2, 6], [3, 7]]
+    assert O.combine_order(4) == [[0], [1], [2], [3]]
+    assert O.combine_order(2) == [[0], [1]]
