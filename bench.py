@@ -1,0 +1,391 @@
+"""Benchmark of the B200 NVFP4 prefill MoE layer (BASELINE.json metric: MoE-layer tokens/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg1|cfg5_*]
+
+One step = one pass of the layer over one packed batch: Gemma-4 routing of the fp32 router logits, routing data,
+permute + NVFP4 quantisation, w13 grouped GEMM with fused GELU-tanh*up + re-quantisation, w2 grouped GEMM,
+weighted combine. Default workload = BASELINE config 2 (26B-A4B-shaped layer: hidden 2816, 128 experts, top-8,
+inter 704, 32 packed sequences of lengths U[256, 2048], ~37k tokens) on one B200. Inputs are seeded synthetic
+data of that shape (activations N(0,1) bf16, weights N(0,0.02) quantised to NVFP4 on the device).
+
+`value` times the kernels with the inputs resident in HBM (CUDA events, max over ranks); `e2e` times the public
+API call (reax_engine_b200.route + run_moe_nvfp4) with pinned host inputs copied in and the output copied back
+every step. `--impl reference` times the reference path's CPU restatement (oracle/moe_oracle.py, numpy) on the
+host cores on a bounded token sample. With torchrun (N > 1) each rank runs the expert-parallel layer
+(reax_engine_b200.ep) on its own 65,536-token batch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
+NOMINAL_FP4_TFLOPS = 9000.0
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm_gbs=d["hbm_gbs"], bf16=d["bf16_tflops"], bf16_sus=d.get("bf16_tflops_sustained"),
+                    source="measured")
+    return dict(hbm_gbs=6650.0, bf16=1590.0, bf16_sus=1400.0, source="fallback")
+
+
+def workload(name: str):
+    from moe_cases import packed_lengths
+    if name == "cfg2":
+        lens = packed_lengths(32, 256, 2048, seed=0)
+        return dict(name="cfg2: 26B-A4B-shaped MoE layer, 32 packed seqs U[256,2048]", T=sum(lens), H=2816, E=128,
+                    k=8, I=704, act="gelu_tanh", skew=None, lens=lens)
+    if name == "cfg1":
+        lens = [64, 96, 160, 192]
+        return dict(name="cfg1: H2048 E64 top4 I1024 SiLU, 4 packed seqs", T=512, H=2048, E=64, k=4, I=1024,
+                    act="silu", skew=None, lens=lens)
+    if name.startswith("cfg5_"):
+        T = int(name.split("_")[1])
+        return dict(name=f"cfg5: skewed Zipf routing T={T}", T=T, H=2816, E=128, k=8, I=704, act="gelu_tanh",
+                    skew=2.0, lens=[T])
+    if name == "cfg4":
+        return dict(name="cfg4: expert-parallel layer, 65536 tokens/rank", T=65536, H=2816, E=128, k=8, I=704,
+                    act="gelu_tanh", skew=None, lens=[65536])
+    raise ValueError(name)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_inputs(wl: dict, device, seed: int = 0):
+    """Seeded synthetic inputs of the workload's shapes, generated on the device."""
+    import torch
+
+    import reax_engine_b200 as R
+    from moe_cases import zipf_bias
+    T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(T, H, generator=g, device=device).bfloat16()
+    if wl["skew"] is None:
+        gate = torch.randn(E, H, generator=g, device=device) * 0.02
+        logits = x.float() @ gate.t()
+    else:
+        logits = torch.randn(T, E, generator=g, device=device) + zipf_bias(E, wl["skew"], seed).to(device)[None]
+    w1 = torch.randn(E, 2 * I, H, generator=g, device=device) * 0.02
+    w1q, w1s, w1g = R.quantize_weights(w1)
+    del w1
+    w2 = torch.randn(E, H, I, generator=g, device=device) * 0.02
+    w2q, w2s, w2g = R.quantize_weights(w2)
+    del w2
+    a1_g = float(x.float().abs().max()) / 2688.0
+    a2_g = 8.0 / 2688.0
+    inp = dict(x=x, logits=logits, w1q=w1q, w1s=w1s, w2q=w2q, w2s=w2s,
+               a1_gscale=torch.full((E,), 1.0 / a1_g, device=device),
+               a2_gscale=torch.full((E,), 1.0 / a2_g, device=device),
+               w1_alphas=(w1g * a1_g).float(), w2_alphas=(w2g * a2_g).float())
+    inp["w1p"], inp["w1p_sf"] = R.prepack_w13(w1q, w1s, I)
+    torch.cuda.synchronize(device)
+    return inp
+
+
+def cpu_sample(wl: dict, inp_cpu: dict, n_tokens: int, reps: int = 1):
+    """Time the oracle (reference CPU restatement) on the first n_tokens of the workload. Returns tokens/s."""
+    from oracle import moe_oracle as O
+    n = min(n_tokens, wl["T"])
+    x = inp_cpu["x"][:n]
+    logits = inp_cpu["logits"][:n]
+    wcache: dict = {}
+    # untimed: dequantise the touched experts' weights once (model-load work for a CPU engine)
+    w, ids = O.route(logits, wl["k"])
+    for e in np.unique(ids):
+        wcache[(id(inp_cpu["w1q"]), int(e))] = O.expert_weights(inp_cpu["w1q"], inp_cpu["w1s"], int(e))
+        wcache[(id(inp_cpu["w2q"]), int(e))] = O.expert_weights(inp_cpu["w2q"], inp_cpu["w2s"], int(e))
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        w, ids = O.route(logits, wl["k"])
+        O.moe_forward(x, w, ids, inp_cpu["w1q"], inp_cpu["w1s"], inp_cpu["w1_alphas"], inp_cpu["w2q"],
+                      inp_cpu["w2s"], inp_cpu["w2_alphas"], inp_cpu["a1_gscale"], inp_cpu["a2_gscale"], wl["act"],
+                      wcache)
+        times.append(time.perf_counter() - t0)
+    return n / statistics.median(times), n, statistics.median(times)
+
+
+def to_cpu_inputs(inp: dict) -> dict:
+    return dict(x=inp["x"].float().cpu().numpy(), logits=inp["logits"].cpu().numpy(),
+                w1q=inp["w1q"].cpu().numpy(), w1s=inp["w1s"].cpu().numpy(), w2q=inp["w2q"].cpu().numpy(),
+                w2s=inp["w2s"].cpu().numpy(), a1_gscale=inp["a1_gscale"].cpu().numpy(),
+                a2_gscale=inp["a2_gscale"].cpu().numpy(), w1_alphas=inp["w1_alphas"].cpu().numpy(),
+                w2_alphas=inp["w2_alphas"].cpu().numpy())
+
+
+def run_reference(args, wl: dict) -> None:
+    """The reference arm: the reference path's CPU restatement (numpy oracle), all host cores, bounded samples."""
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    dev = torch.device("cuda:0") if torch.cuda.is_available() else None
+    if dev is not None:
+        inp = build_inputs(wl, dev)
+        cpu = to_cpu_inputs(inp)
+        del inp
+        torch.cuda.empty_cache()
+    else:
+        raise SystemExit("reference arm needs the same seeded inputs (generated on the GPU)")
+    sample = 256
+    for _ in range(args.warmup):
+        cpu_sample(wl, cpu, 32)
+    rates = []
+    for _ in range(args.steps):
+        r, n, t = cpu_sample(wl, cpu, sample)
+        rates.append(r)
+    v = statistics.median(rates)
+    line = dict(metric=METRIC, value=v, unit="tokens/s", n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                ms_per_step=1000.0 * wl["T"] / v, higher_is_better=True, scaling="weak", vs_baseline=None,
+                dtype="fp32 (dequantised NVFP4)", data="synthetic",
+                config=dict(workload=wl["name"], tokens=wl["T"], hidden=wl["H"], experts=wl["E"], topk=wl["k"],
+                            inter=wl["I"]),
+                impl="reference",
+                cpu_baseline=dict(value=v, unit="tokens/s", cores=os.cpu_count(), kind="port",
+                                  sample=f"first {sample} tokens of the workload per step, numpy oracle "
+                                         f"(oracle/moe_oracle.py), expert weights pre-dequantised"),
+                e2e=dict(value=v, unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, wl: dict) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import reax_engine_b200 as R
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    inp = build_inputs(wl, dev, seed=rank)
+    T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
+    st = R.Stages(T, H, I, E, k, wl["act"], dev)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    s = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        w, ids = R.route(None, inp["logits"], k)
+        if ev is not None: ev[0].record(s)
+        st.plan(ids)
+        if ev is not None: ev[1].record(s)
+        st.permute_quant(inp["x"], inp["a1_gscale"])
+        if ev is not None: ev[2].record(s)
+        st.gemm_w13(inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"])
+        if ev is not None: ev[3].record(s)
+        st.gemm_w2(inp["w2q"], inp["w2s"], inp["w2_alphas"])
+        if ev is not None: ev[4].record(s)
+        st.combine(w, out)
+        if ev is not None: ev[5].record(s)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if st.status() != 0:
+        raise SystemExit(f"device status {st.status()} after warm-up")
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index) as clk:
+        start.record(s)
+        for i in range(args.steps):
+            step(evs[i])
+        stop.record(s)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(stop)
+    names = ["route", "plan", "permute_quant", "gemm_w13", "gemm_w2", "combine"]
+    per = {n: [] for n in names}
+    for i in range(args.steps):
+        prev = start if i == 0 else evs[i - 1][5]
+        marks = [prev] + evs[i]
+        for j, n in enumerate(names):
+            per[n].append(marks[j].elapsed_time(marks[j + 1]))
+    per_ms = {n: statistics.mean(v) for n, v in per.items()}
+    t_max = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms = float(t_max.item())
+    ms_step = ms / args.steps
+    value = world * T * args.steps / (ms / 1000.0)
+
+    # ---- end to end through the public API, pinned host buffers in, output back
+    x_h = inp["x"].cpu().pin_memory()
+    lg_h = inp["logits"].cpu().pin_memory()
+    out_h = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty_like(inp["x"])
+    lg_d = torch.empty_like(inp["logits"])
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        lg_d.copy_(lg_h, non_blocking=True)
+        w, ids = R.route(None, lg_d, k)
+        R.run_moe_nvfp4(out, x_d, inp["a1_gscale"], inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"],
+                        inp["w2q"], inp["w2s"], inp["w2_alphas"], w, ids, wl["act"], w1_prepacked=True)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    e0.record(s)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(s)
+    torch.cuda.synchronize(dev)
+    ems = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
+
+    # ---- roofline of the dominant kernel and per-kernel figures
+    peaks = load_peaks()
+    slots = T * k
+    fp4_peak = 4.0 * peaks["bf16"]
+    flops = {"gemm_w13": 2.0 * slots * H * 2 * I, "gemm_w2": 2.0 * slots * I * H}
+    hbm = {"route": T * E * 4 + T * k * 8, "plan": T * k * 4,
+           "permute_quant": T * H * 2 + slots * (H // 2 + H // 16) + slots * 4,
+           "combine": slots * H * 2 + slots * 8 + T * H * 2}
+    kernels = {}
+    for n in names:
+        t = per_ms[n] / 1000.0
+        if n in flops:
+            a = flops[n] / t / 1e12
+            kernels[n] = dict(ms=per_ms[n], achieved=a, unit="TFLOP/s", frac=a / fp4_peak)
+        else:
+            a = hbm[n] / t / 1e9
+            kernels[n] = dict(ms=per_ms[n], achieved=a, unit="GB/s", frac=a / peaks["hbm_gbs"])
+    dom = max(names, key=lambda n: per_ms[n])
+    kd = kernels[dom]
+    roof = dict(kernel=dom, bound="tensor" if dom in flops else "hbm", achieved=kd["achieved"],
+                peak=fp4_peak if dom in flops else peaks["hbm_gbs"], unit=kd["unit"], frac=kd["frac"], traffic=None,
+                peak_basis=("4 x measured cuBLAS bf16 dense (nominal dense FP4:BF16 = 4:1; "
+                            f"{peaks['source']} bf16 {peaks['bf16']} TFLOP/s), nominal FP4 9000")
+                if dom in flops else f"{peaks['source']} HBM copy bandwidth")
+    layer_flop = flops["gemm_w13"] + flops["gemm_w2"]
+    layer = dict(tflops=layer_flop / (ms_step / 1000.0) / 1e12,
+                 frac_fp4=layer_flop / (ms_step / 1000.0) / 1e12 / fp4_peak)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu_in = to_cpu_inputs(inp)
+        rate, n, t = cpu_sample(wl, cpu_in, args.cpu_tokens)
+        cpu = dict(value=rate, unit="tokens/s", cores=os.cpu_count(), kind="port",
+                   sample=f"first {n} tokens of the workload, numpy oracle, {t:.2f} s")
+    launches_per_step = 7   # route, count, plan, permute_quant, gemm_w13, gemm_w2, combine
+    line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
+                ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
+                data="synthetic",
+                config=dict(workload=wl["name"], tokens=T, hidden=H, experts=E, topk=k, inter=I,
+                            activation=wl["act"], parallelism="replicas" if world > 1 else "single",
+                            l2="inputs larger than L2 (x %.0f MB, weights %.0f MB); no flush" % (
+                                T * H * 2 / 1e6, (inp["w1q"].numel() + inp["w1s"].numel() + inp["w2q"].numel() +
+                                                  inp["w2s"].numel()) / 1e6)),
+                e2e=dict(value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * H * 2 + T * E * 4,
+                         d2h_bytes_per_step=T * H * 2),
+                gpu_launches=launches_per_step * args.steps, roofline=roof, layer=layer, kernels=kernels,
+                cpu_baseline=cpu, clocks=clk.summary())
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default=None)
+    ap.add_argument("--cpu-tokens", type=int, default=256)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    wl = workload(args.workload or ("cfg4" if world > 1 else "cfg2"))
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

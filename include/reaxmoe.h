@@ -1,0 +1,162 @@
+/*
+ * reaxmoe.h -- C ABI of the B200 (sm_100a) NVFP4 prefill MoE layer.
+ *
+ * One entry point per stage of the reference's MoE operator, plus the whole layer. All pointers are device
+ * pointers unless stated; every call is asynchronous on the given CUDA stream (passed as void*, i.e. a
+ * cudaStream_t; NULL = the legacy default stream), allocates nothing, performs no host synchronisation and
+ * returns an int status: 0 = ok, > 0 = one of the REAXMOE_ERR_* codes below. The text of the last error of
+ * the calling thread is available from reaxmoe_last_error().
+ *
+ * Reference interfaces replaced (paths are within the reference project):
+ *   - vLLM run_cutlass_moe_fp4(output, a, a1_gscale, w1_fp4, w1_blockscale, w1_alphas, a2_gscale, w2_fp4,
+ *     w2_blockscale, w2_alphas, topk_weights, topk_ids, activation, workspace13, workspace2, m, n, k, e,
+ *     ...), as patched by champions/uid240/opt/blink/blink_moe.py:434-567 (stock body:
+ *     vllm/model_executor/layers/fused_moe/experts/cutlass_moe.py:481-664)      -> reaxmoe_forward
+ *   - Gemma-4 routing function (vllm/model_executor/models/gemma4.py:95-203, called from
+ *     gemma4.py:332-345)                                                          -> reaxmoe_route
+ *   - get_cutlass_moe_mm_data / blink _fplan (champions/uid240/opt/blink/blink_moe.py:271-299)
+ *                                                                                 -> reaxmoe_plan
+ *   - scaled_fp4_experts_quant of the m rows + _tscatter (blink_moe.py:301-323, :402-421)
+ *                                                                                 -> reaxmoe_permute_quant
+ *   - w13 grouped GEMM + gelu_tanh/silu * up + NVFP4 quant (blink_moegemm.cu:472-934 MODE 1,
+ *     engine/fp4_triton.py:54-65, :161-167)                                       -> reaxmoe_gemm_w13
+ *   - w2 grouped GEMM (blink_moegemm.cu:1173-1197, bmoe69.cu:1186-1189)           -> reaxmoe_gemm_w2
+ *   - combine / unpermute _tail (blink_moe.py:168-198, :423-428)                  -> reaxmoe_combine
+ *   - engine/fp4.py::quantize_nvfp4 (values, e4m3 block scales, 128x4 atoms, engine/fp4.py:16-52) and
+ *     engine/fp4_triton.py::nvfp4_quant_static (:129-135)                         -> reaxmoe_quantize
+ *   - int nv4_gemm(...) / size_t nv4_ws(...) C-ABI convention
+ *     (champions/uid240/opt/reax/engine/nv4_dispatch.cu:11-26)                    -> status codes, workspace query
+ *
+ * Data formats (engine/fp4.py layout):
+ *   NVFP4 matrix [R, K]: packed e2m1 bytes [R, K/2] (low nibble = even column) + e4m3 block scales (one per
+ *   16 elements) in 128x4 atoms: byte (r, kb) lives at ((r/128)*(K/64) + kb/4)*512 + (r%32)*16 + ((r%128)/32)*4
+ *   + kb%4. Weights are stacked per expert: w_fp4 [E, N, K/2], w_sf [E][N/128][K/64][512].
+ *   Global scales: a*_gscale are QUANT-side (1 / dequant scale, vLLM convention); w*_alphas[e] = weight
+ *   dequant scale x input dequant scale.
+ *   Routed rows (vLLM layout): slot s of expert e is row expert_offsets[e] + i; its scale row is
+ *   blockscale_offsets[e] + i (each expert's scale rows start on a 128-row atom).
+ *   Slot order inside an expert is canonical: by (token, k-index) ascending.
+ */
+#ifndef REAXMOE_H
+#define REAXMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  REAXMOE_OK = 0,
+  REAXMOE_ERR_BAD_SHAPE = 1,       /* a size breaks a precondition (see reaxmoe_problem) */
+  REAXMOE_ERR_MISALIGNED = 2,      /* a pointer is not 16-byte aligned */
+  REAXMOE_ERR_TOO_MANY_EXPERTS = 3,/* experts > 256 or topk > 16 or topk > experts */
+  REAXMOE_ERR_DEVICE_TIMEOUT = 4,  /* a bounded device wait expired (read back by reaxmoe_read_status) */
+  REAXMOE_ERR_WORKSPACE = 5,       /* workspace NULL or smaller than reaxmoe_workspace_size() */
+  REAXMOE_ERR_CUDA = 6,            /* a CUDA runtime / driver call failed */
+  REAXMOE_ERR_NULL = 7,            /* a required pointer is NULL */
+  REAXMOE_ERR_BAD_EXPERT_ID = 8,   /* a routed expert id outside [0, experts) (device-detected) */
+  REAXMOE_ERR_UNSUPPORTED = 9      /* e.g. no sm_100 device */
+};
+
+enum { REAXMOE_ACT_SILU = 0, REAXMOE_ACT_GELU_TANH = 1 };
+
+/* Layer shape. vLLM names in brackets. Preconditions: hidden [k] % 128 == 0 and >= 256; inter [n] % 64 == 0
+ * and >= 256; 1 <= experts [e] <= 256; 1 <= topk <= min(16, experts); tokens [m] >= 0. */
+typedef struct reaxmoe_problem {
+  int32_t tokens;
+  int32_t hidden;
+  int32_t inter;
+  int32_t experts;
+  int32_t topk;
+  int32_t activation; /* REAXMOE_ACT_* */
+} reaxmoe_problem;
+
+typedef struct reaxmoe_forward_args {
+  reaxmoe_problem p;
+  const void* a;              /* [tokens, hidden] bf16 */
+  const float* a1_gscale;     /* [experts] quant-side input scale of w13 */
+  const void* w1_fp4;         /* [experts, 2*inter, hidden/2] u8, gate/up INTERLEAVED (reaxmoe_prepack_w13) */
+  const void* w1_sf;          /* [experts][2*inter/128][hidden/64][512] e4m3, interleaved like w1_fp4 */
+  const float* w1_alphas;     /* [experts] */
+  const float* a2_gscale;     /* [experts] quant-side scale of the intermediate */
+  const void* w2_fp4;         /* [experts, hidden, inter/2] u8 */
+  const void* w2_sf;          /* [experts][hidden/128][inter/64][512] e4m3 */
+  const float* w2_alphas;     /* [experts] */
+  const float* topk_weights;  /* [tokens, topk] fp32 */
+  const int32_t* topk_ids;    /* [tokens, topk] int32 */
+  void* output;               /* [tokens, hidden] bf16, written (not accumulated) */
+} reaxmoe_forward_args;
+
+/* Bytes of workspace reaxmoe_forward needs for this problem (0 on a bad shape). */
+size_t reaxmoe_workspace_size(const reaxmoe_problem* p);
+
+/* The whole layer: plan -> permute_quant -> gemm_w13 -> gemm_w2 -> combine
+ * (run_cutlass_moe_fp4, cutlass_moe.py:481-664; blink_moe.py:434-567). */
+int reaxmoe_forward(const reaxmoe_forward_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Gemma-4 routing: ids = top-k of logits (descending, ties to the lower expert id), weights = softmax over all
+ * experts renormalised over the top-k, times per_expert_scale[id] (NULL = 1). logits [tokens, experts] fp32;
+ * ids [tokens, topk] int32; weights [tokens, topk] fp32. (gemma4.py:183-203) */
+int reaxmoe_route(const float* logits, const float* per_expert_scale, int32_t tokens, int32_t experts,
+                  int32_t topk, int32_t* topk_ids, float* topk_weights, void* stream);
+
+/* Routing data (get_cutlass_moe_mm_data; blink_moe.py:271-299). Writes, inside the workspace, the per-expert
+ * counts, expert_offsets[E+1], blockscale_offsets[E+1] and GEMM tile tables, and copies them out to the
+ * optional (NULL-able) host-visible-or-device arrays given. */
+int reaxmoe_plan(const reaxmoe_problem* p, const int32_t* topk_ids, void* workspace, size_t workspace_bytes,
+                 int32_t* expert_offsets, int32_t* blockscale_offsets, int32_t* problem_sizes1,
+                 int32_t* problem_sizes2, void* stream);
+
+/* Quantise every token row once per distinct expert scale and scatter it to its top-k slots (FP4 rows +
+ * swizzled scales) in the canonical order; writes c_map[t*topk + j] = slot (blink_moe.py:301-323). Needs the
+ * plan of the same workspace. rep_fp4 [tokens*topk, hidden/2]; rep_sf scale atoms over blockscale_offsets. */
+int reaxmoe_permute_quant(const reaxmoe_problem* p, const void* a, const float* a1_gscale, const int32_t* topk_ids,
+                          void* workspace, size_t workspace_bytes, void* rep_fp4, void* rep_sf, int32_t* c_map,
+                          void* stream);
+
+/* Grouped NVFP4 GEMM w13 with the fused activation(gate) * up and NVFP4 re-quantisation epilogue
+ * (blink_moegemm.cu:472-934 MODE 1). Needs the plan of the same workspace. */
+int reaxmoe_gemm_w13(const reaxmoe_problem* p, const void* rep_fp4, const void* rep_sf, const void* w1_fp4,
+                     const void* w1_sf, const float* w1_alphas, const float* a2_gscale, void* workspace,
+                     size_t workspace_bytes, void* int_fp4, void* int_sf, void* stream);
+
+/* Grouped NVFP4 GEMM w2: c3[slot] = bf16(alpha_e * int[slot] . w2_e^T) (blink_moegemm.cu:1173-1197). */
+int reaxmoe_gemm_w2(const reaxmoe_problem* p, const void* int_fp4, const void* int_sf, const void* w2_fp4,
+                    const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes, void* c3,
+                    void* stream);
+
+/* out[t] = bf16( sum_j bf16(c3[c_map[t*topk+j]] * bf16(w[t, j])) ), fp32 sums in the canonical order
+ * ((s0 + s1) + s2) + s3 of 4 strided partial sums (blink_moe.py:168-198, ORDER 1 for top-8). */
+int reaxmoe_combine(const reaxmoe_problem* p, const void* c3, const int32_t* c_map, const float* topk_weights,
+                    void* output, void* stream);
+
+/* NVFP4 quantisation of rows (engine/fp4.py::quantize_nvfp4 numerics with a given scale; fp4_triton.py
+ * nvfp4_quant_static). x [rows, cols] bf16 (x_is_fp32 = 0) or fp32 (1); rows are grouped by group_rows
+ * (e.g. one expert's N rows), group g quantised with dequant scale 1 / gscale[g]; packed [rows, cols/2];
+ * scales in 128x4 atoms, each group starting on its own atom row: scale row = (r / group_rows) *
+ * ceil128(group_rows) + r % group_rows. cols % 64 == 0. */
+int reaxmoe_quantize(const void* x, int32_t x_is_fp32, int64_t rows, int32_t cols, int32_t group_rows,
+                     const float* gscale, void* packed, void* scales, void* stream);
+
+/* One-time re-layout of w13 for the fused gate/up epilogue: output row block b (128 rows) = gate rows
+ * [64b, 64b+64) then up rows inter + [64b, 64b+64); scales move with their rows. In-place is NOT allowed. */
+int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, int32_t inter, int32_t hidden,
+                        void* w1p_fp4, void* w1p_sf, void* stream);
+
+/* Synchronises `stream`, returns the device status word of the workspace (0 = ok, else REAXMOE_ERR_*) and
+ * clears it when `clear` != 0. Not for the hot path. */
+int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream);
+
+/* Copies the last error text of the calling thread into buf (NUL-terminated); returns its full length. */
+size_t reaxmoe_last_error(char* buf, size_t len);
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int32_t reaxmoe_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REAXMOE_H */

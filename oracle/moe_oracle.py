@@ -162,12 +162,22 @@ def from_blocked(flat: np.ndarray, rows: int, k16: int, row0: int = 0) -> np.nda
     return np.asarray(flat, dtype=np.uint8)[swizzle_offset(r, c, k16)]
 
 
+_BYTE_LUT = None
+
+
+def _byte_lut() -> np.ndarray:
+    """[256, 2] float32: the two e2m1 values of a packed byte (low nibble first)."""
+    global _BYTE_LUT
+    if _BYTE_LUT is None:
+        b = np.arange(256, dtype=np.uint8)
+        _BYTE_LUT = np.stack([e2m1_decode(b & 0xF), e2m1_decode(b >> 4)], axis=-1).astype(np.float32)
+    return _BYTE_LUT
+
+
 def dequant(packed: np.ndarray, s8: np.ndarray) -> np.ndarray:
     """packed [R, K/2], unswizzled scales [R, K/16] -> exact float32 values e2m1 * e4m3 (no global scale)."""
     R = packed.shape[0]
-    lo, hi = packed & 0xF, packed >> 4
-    codes = np.stack([lo, hi], axis=-1).reshape(R, -1)
-    v = e2m1_decode(codes).reshape(R, -1, 16)
+    v = _byte_lut()[np.asarray(packed, dtype=np.uint8)].reshape(R, -1, 16)
     return (v * e4m3_decode(s8)[..., None]).reshape(R, -1).astype(np.float32)
 
 
@@ -285,7 +295,7 @@ def expert_weights(w_fp4: np.ndarray, w_sf: np.ndarray, e: int) -> np.ndarray:
 
 
 def grouped_gemm(a_fp4: np.ndarray, a_sf: np.ndarray, w_fp4: np.ndarray, w_sf: np.ndarray, alphas: np.ndarray,
-                 pl: dict) -> np.ndarray:
+                 pl: dict, wcache: dict | None = None) -> np.ndarray:
     """out[slots of e] = bf16(alpha_e * (dequant(A_e) @ dequant(W_e)^T)) with fp32 accumulation
     (CUTLASS epilogue alpha * acc, beta = 0, then cvt.rn to bf16: ``blink_moegemm.cu:193-200``)."""
     E = pl["counts"].shape[0]
@@ -300,7 +310,13 @@ def grouped_gemm(a_fp4: np.ndarray, a_sf: np.ndarray, w_fp4: np.ndarray, w_sf: n
         r0 = int(eoff[e])
         s8 = from_blocked(a_sf, m, K // 16, int(boff[e]))
         a = dequant(a_fp4[r0:r0 + m], s8)
-        w = expert_weights(w_fp4, w_sf, e)
+        if wcache is not None:
+            key = (id(w_fp4), e)
+            if key not in wcache:
+                wcache[key] = expert_weights(w_fp4, w_sf, e)
+            w = wcache[key]
+        else:
+            w = expert_weights(w_fp4, w_sf, e)
         acc = (a @ w.T).astype(np.float32)
         out[r0:r0 + m] = bf16_round(np.float32(alphas[e]) * acc)
     return out
@@ -347,7 +363,7 @@ def combine(c3: np.ndarray, c_map: np.ndarray, topk_weights: np.ndarray) -> np.n
 
 
 def moe_forward(x, topk_weights, topk_ids, w1_fp4, w1_sf, w1_alphas, w2_fp4, w2_sf, w2_alphas, a1_gscale,
-                a2_gscale, activation: str = "gelu_tanh") -> dict:
+                a2_gscale, activation: str = "gelu_tanh", wcache: dict | None = None) -> dict:
     """The whole layer (stock ``run_cutlass_moe_fp4`` semantics). x: [T, H] float32 holding bf16 values;
     w1_fp4 [E, 2I, H/2] (gate rows [0, I), up rows [I, 2I)), w1_sf [E, swizzled bytes];
     w2_fp4 [E, H, I/2]. Returns every intermediate and the output (float32 holding bf16 values)."""
@@ -356,9 +372,9 @@ def moe_forward(x, topk_weights, topk_ids, w1_fp4, w1_sf, w1_alphas, w2_fp4, w2_
     inter = w2_fp4.shape[2] * 2
     pl = plan(topk_ids, E)
     rep_fp4, rep_sf = permute_quant(x, topk_ids, a1_gscale, pl)
-    c1 = grouped_gemm(rep_fp4, rep_sf, w1_fp4, w1_sf, w1_alphas, pl)
+    c1 = grouped_gemm(rep_fp4, rep_sf, w1_fp4, w1_sf, w1_alphas, pl, wcache)
     int_fp4, int_sf, h = act_quant(c1, a2_gscale, activation, pl, inter)
-    c3 = grouped_gemm(int_fp4, int_sf, w2_fp4, w2_sf, w2_alphas, pl)
+    c3 = grouped_gemm(int_fp4, int_sf, w2_fp4, w2_sf, w2_alphas, pl, wcache)
     out = combine(c3, pl["c_map"], topk_weights)
     return dict(plan=pl, rep_fp4=rep_fp4, rep_sf=rep_sf, c1=c1, h=h, int_fp4=int_fp4, int_sf=int_sf, c3=c3,
                 out=out)

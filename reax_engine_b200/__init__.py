@@ -1,0 +1,12 @@
+"""reax_engine_b200 -- B200-native (sm_100a) NVFP4 prefill MoE layer of the REAX decision engine.
+
+Public API (mirrors the reference's operator interfaces; see ``moe.py``):
+    route, run_moe_nvfp4, quantize_nvfp4, quantize_weights, prepack_w13, workspace_size, Stages, MoEActivation
+    ep (expert-parallel layer over torch.distributed / NCCL)
+"""
+from ._lib import ReaxMoEError, lib  # noqa: F401
+from .moe import (MoEActivation, Stages, Workspace, prepack_w13, quantize_nvfp4, quantize_weights,  # noqa: F401
+                  read_status, route, run_moe_nvfp4, workspace_size)
+
+__all__ = ["ReaxMoEError", "MoEActivation", "Stages", "Workspace", "prepack_w13", "quantize_nvfp4",
+           "quantize_weights", "read_status", "route", "run_moe_nvfp4", "workspace_size", "lib"]

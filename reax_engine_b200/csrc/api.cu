@@ -1,0 +1,401 @@
+// api.cu -- the extern "C" entry points of include/reaxmoe.h: argument checks, workspace layout and the
+// launch sequence of the layer. No allocation, no host synchronisation on the forward path.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace reaxmoe {
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+static int cuda_check(const char* what) {
+  const cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) return fail(REAXMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return 0;
+}
+
+static int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int check_problem(const reaxmoe_problem* p) {
+  if (p == nullptr) return fail(REAXMOE_ERR_NULL, "problem is NULL");
+  if (p->experts < 1 || p->experts > kMaxExperts)
+    return fail(REAXMOE_ERR_TOO_MANY_EXPERTS, "experts=%d outside [1, %d]", p->experts, kMaxExperts);
+  if (p->topk < 1 || p->topk > kMaxTopk || p->topk > p->experts)
+    return fail(REAXMOE_ERR_TOO_MANY_EXPERTS, "topk=%d outside [1, min(%d, experts)]", p->topk, kMaxTopk);
+  if (p->hidden < 256 || p->hidden % 128 != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "hidden=%d must be a multiple of 128 and >= 256", p->hidden);
+  if (p->inter < 256 || p->inter % 64 != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "inter=%d must be a multiple of 64 and >= 256", p->inter);
+  if (p->tokens < 0) return fail(REAXMOE_ERR_BAD_SHAPE, "tokens=%d < 0", p->tokens);
+  if ((int64_t)p->tokens * p->topk > (int64_t)1 << 30)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "tokens*topk=%lld too large", (long long)p->tokens * p->topk);
+  if (p->activation != REAXMOE_ACT_SILU && p->activation != REAXMOE_ACT_GELU_TANH)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "activation=%d unknown", p->activation);
+  return 0;
+}
+
+// Workspace regions, each 256-byte aligned.
+struct Layout {
+  size_t status, seg_counts, seg_base, counts, eoff, boff, tile_prefix, c_map, rep_fp4, rep_sf, int_fp4, int_sf, c3,
+      total;
+};
+
+static size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static Layout layout(const reaxmoe_problem* p) {
+  Layout L;
+  const int64_t m = p->tokens, k = p->topk, E = p->experts, H = p->hidden, I = p->inter;
+  const int64_t slots = m * k;
+  const int64_t nseg = ceil_div64(m, kSegTokens);
+  const int64_t sfblk = sf_row_blocks(slots, (int)E);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = up256(off + bytes);
+    return o;
+  };
+  L.status = take(64);
+  L.seg_counts = take((size_t)nseg * E * 4);
+  L.seg_base = take((size_t)nseg * E * 4);
+  L.counts = take((size_t)E * 4);
+  L.eoff = take((size_t)(E + 1) * 4);
+  L.boff = take((size_t)(E + 1) * 4);
+  L.tile_prefix = take((size_t)(E + 1) * 4);
+  L.c_map = take((size_t)slots * 4);
+  L.rep_fp4 = take((size_t)slots * (H / 2));
+  L.rep_sf = take((size_t)sfblk * (H / 64) * 512);
+  L.int_fp4 = take((size_t)slots * (I / 2));
+  L.int_sf = take((size_t)sfblk * (I / 64) * 512);
+  L.c3 = take((size_t)slots * H * 2);
+  L.total = off;
+  return L;
+}
+
+struct WS {
+  int* status;
+  int* seg_counts;
+  int* seg_base;
+  int* counts;
+  int* eoff;
+  int* boff;
+  int* tile_prefix;
+  int* c_map;
+  uint8_t* rep_fp4;
+  uint8_t* rep_sf;
+  uint8_t* int_fp4;
+  uint8_t* int_sf;
+  __nv_bfloat16* c3;
+};
+
+static WS carve(void* ws, const Layout& L) {
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  WS w;
+  w.status = reinterpret_cast<int*>(b + L.status);
+  w.seg_counts = reinterpret_cast<int*>(b + L.seg_counts);
+  w.seg_base = reinterpret_cast<int*>(b + L.seg_base);
+  w.counts = reinterpret_cast<int*>(b + L.counts);
+  w.eoff = reinterpret_cast<int*>(b + L.eoff);
+  w.boff = reinterpret_cast<int*>(b + L.boff);
+  w.tile_prefix = reinterpret_cast<int*>(b + L.tile_prefix);
+  w.c_map = reinterpret_cast<int*>(b + L.c_map);
+  w.rep_fp4 = b + L.rep_fp4;
+  w.rep_sf = b + L.rep_sf;
+  w.int_fp4 = b + L.int_fp4;
+  w.int_sf = b + L.int_sf;
+  w.c3 = reinterpret_cast<__nv_bfloat16*>(b + L.c3);
+  return w;
+}
+
+static int check_ws(const reaxmoe_problem* p, void* ws, size_t bytes, Layout* L) {
+  *L = layout(p);
+  if (ws == nullptr) return fail(REAXMOE_ERR_WORKSPACE, "workspace is NULL");
+  if (!aligned16(ws)) return fail(REAXMOE_ERR_MISALIGNED, "workspace not 16-byte aligned");
+  if (bytes < L->total)
+    return fail(REAXMOE_ERR_WORKSPACE, "workspace %zu bytes < required %zu", bytes, L->total);
+  return 0;
+}
+
+static unsigned long long device_timeout_ns() {
+  const char* s = getenv("REAXMOE_WAIT_TIMEOUT_NS");
+  if (s != nullptr && *s) return strtoull(s, nullptr, 10);
+  return 4000000000ull;  // 4 s: far above any legitimate intra-CTA wait
+}
+
+static int do_plan(const reaxmoe_problem* p, const int32_t* ids, const WS& w, int32_t* ps1, int32_t* ps2,
+                   cudaStream_t s) {
+  const int nseg = (int)ceil_div64(p->tokens, kSegTokens);
+  cudaMemsetAsync(w.status, 0, sizeof(int), s);
+  launch_count(ids, p->tokens, p->topk, p->experts, w.seg_counts, w.status, s);
+  launch_plan(w.seg_counts, nseg, p->experts, w.seg_base, w.counts, w.eoff, w.boff, w.tile_prefix, ps1, ps2,
+              2 * p->inter, p->hidden, p->hidden, p->inter, s);
+  return cuda_check("plan");
+}
+
+static GemmLaunch w13_launch(const reaxmoe_problem* p, const WS& w, const void* rep_fp4, const void* rep_sf,
+                             const void* w1, const void* w1_sf, const float* alphas, const float* a2_gscale,
+                             void* int_fp4, void* int_sf) {
+  GemmLaunch g;
+  memset(&g, 0, sizeof(g));
+  g.mode = 1;
+  g.act = p->activation;
+  g.a = rep_fp4;
+  g.slots = (int64_t)p->tokens * p->topk;
+  g.a_sf = rep_sf;
+  g.b = w1;
+  g.b_sf = w1_sf;
+  g.alphas = alphas;
+  g.E = p->experts;
+  g.N = 2 * p->inter;
+  g.K = p->hidden;
+  g.counts = w.counts;
+  g.eoff = w.eoff;
+  g.boff = w.boff;
+  g.tile_prefix = w.tile_prefix;
+  g.q_out = int_fp4;
+  g.q_sf = int_sf;
+  g.q_gscale = a2_gscale;
+  g.status = w.status;
+  g.timeout_ns = device_timeout_ns();
+  return g;
+}
+
+static GemmLaunch w2_launch(const reaxmoe_problem* p, const WS& w, const void* int_fp4, const void* int_sf,
+                            const void* w2, const void* w2_sf, const float* alphas, void* c3) {
+  GemmLaunch g;
+  memset(&g, 0, sizeof(g));
+  g.mode = 0;
+  g.a = int_fp4;
+  g.slots = (int64_t)p->tokens * p->topk;
+  g.a_sf = int_sf;
+  g.b = w2;
+  g.b_sf = w2_sf;
+  g.alphas = alphas;
+  g.E = p->experts;
+  g.N = p->hidden;
+  g.K = p->inter;
+  g.counts = w.counts;
+  g.eoff = w.eoff;
+  g.boff = w.boff;
+  g.tile_prefix = w.tile_prefix;
+  g.out = c3;
+  g.status = w.status;
+  g.timeout_ns = device_timeout_ns();
+  return g;
+}
+
+}  // namespace reaxmoe
+
+using namespace reaxmoe;
+
+extern "C" {
+
+int32_t reaxmoe_version(void) { return 100; }
+
+size_t reaxmoe_last_error(char* buf, size_t len) {
+  if (buf != nullptr && len > 0) {
+    const size_t n = g_last_error.size() < len - 1 ? g_last_error.size() : len - 1;
+    memcpy(buf, g_last_error.data(), n);
+    buf[n] = '\0';
+  }
+  return g_last_error.size();
+}
+
+size_t reaxmoe_workspace_size(const reaxmoe_problem* p) {
+  if (check_problem(p)) return 0;
+  return layout(p).total;
+}
+
+int reaxmoe_route(const float* logits, const float* per_expert_scale, int32_t tokens, int32_t experts, int32_t topk,
+                  int32_t* topk_ids, float* topk_weights, void* stream) {
+  if (experts < 1 || experts > kMaxExperts || topk < 1 || topk > kMaxTopk || topk > experts)
+    return fail(REAXMOE_ERR_TOO_MANY_EXPERTS, "route: experts=%d topk=%d unsupported", experts, topk);
+  if (tokens < 0) return fail(REAXMOE_ERR_BAD_SHAPE, "route: tokens=%d < 0", tokens);
+  if (tokens == 0) return 0;
+  if (logits == nullptr || topk_ids == nullptr || topk_weights == nullptr)
+    return fail(REAXMOE_ERR_NULL, "route: NULL pointer");
+  launch_route(logits, per_expert_scale, tokens, experts, topk, topk_ids, topk_weights,
+               static_cast<cudaStream_t>(stream));
+  return cuda_check("route");
+}
+
+int reaxmoe_plan(const reaxmoe_problem* p, const int32_t* topk_ids, void* workspace, size_t workspace_bytes,
+                 int32_t* expert_offsets, int32_t* blockscale_offsets, int32_t* problem_sizes1,
+                 int32_t* problem_sizes2, void* stream) {
+  int rc = check_problem(p);
+  if (rc) return rc;
+  Layout L;
+  if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
+  if (p->tokens == 0) return 0;
+  if (topk_ids == nullptr) return fail(REAXMOE_ERR_NULL, "plan: topk_ids is NULL");
+  const WS w = carve(workspace, L);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = do_plan(p, topk_ids, w, problem_sizes1, problem_sizes2, s))) return rc;
+  const size_t n = (size_t)(p->experts + 1) * 4;
+  if (expert_offsets != nullptr) cudaMemcpyAsync(expert_offsets, w.eoff, n, cudaMemcpyDefault, s);
+  if (blockscale_offsets != nullptr) cudaMemcpyAsync(blockscale_offsets, w.boff, n, cudaMemcpyDefault, s);
+  return cuda_check("plan copy-out");
+}
+
+int reaxmoe_permute_quant(const reaxmoe_problem* p, const void* a, const float* a1_gscale, const int32_t* topk_ids,
+                          void* workspace, size_t workspace_bytes, void* rep_fp4, void* rep_sf, int32_t* c_map,
+                          void* stream) {
+  int rc = check_problem(p);
+  if (rc) return rc;
+  Layout L;
+  if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
+  if (p->tokens == 0) return 0;
+  if (!a || !a1_gscale || !topk_ids || !rep_fp4 || !rep_sf || !c_map)
+    return fail(REAXMOE_ERR_NULL, "permute_quant: NULL pointer");
+  if (!aligned16(a) || !aligned16(rep_fp4) || !aligned16(rep_sf))
+    return fail(REAXMOE_ERR_MISALIGNED, "permute_quant: a, rep_fp4 and rep_sf must be 16-byte aligned");
+  const WS w = carve(workspace, L);
+  launch_permute_quant(static_cast<const __nv_bfloat16*>(a), a1_gscale, topk_ids, w.seg_base, w.eoff, w.boff,
+                       p->tokens, p->hidden, p->experts, p->topk, static_cast<uint8_t*>(rep_fp4),
+                       static_cast<uint8_t*>(rep_sf), c_map, static_cast<cudaStream_t>(stream));
+  return cuda_check("permute_quant");
+}
+
+int reaxmoe_gemm_w13(const reaxmoe_problem* p, const void* rep_fp4, const void* rep_sf, const void* w1_fp4,
+                     const void* w1_sf, const float* w1_alphas, const float* a2_gscale, void* workspace,
+                     size_t workspace_bytes, void* int_fp4, void* int_sf, void* stream) {
+  int rc = check_problem(p);
+  if (rc) return rc;
+  Layout L;
+  if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
+  if (p->tokens == 0) return 0;
+  if (!rep_fp4 || !rep_sf || !w1_fp4 || !w1_sf || !w1_alphas || !a2_gscale || !int_fp4 || !int_sf)
+    return fail(REAXMOE_ERR_NULL, "gemm_w13: NULL pointer");
+  if (!aligned16(rep_fp4) || !aligned16(rep_sf) || !aligned16(w1_fp4) || !aligned16(w1_sf) || !aligned16(int_fp4))
+    return fail(REAXMOE_ERR_MISALIGNED, "gemm_w13: operands must be 16-byte aligned");
+  const WS w = carve(workspace, L);
+  const GemmLaunch g = w13_launch(p, w, rep_fp4, rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, int_fp4, int_sf);
+  if ((rc = launch_grouped_gemm(g, num_sms(), static_cast<cudaStream_t>(stream))))
+    return fail(rc, "gemm_w13 launch failed: %s", cudaGetErrorString(cudaPeekAtLastError()));
+  return cuda_check("gemm_w13");
+}
+
+int reaxmoe_gemm_w2(const reaxmoe_problem* p, const void* int_fp4, const void* int_sf, const void* w2_fp4,
+                    const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes, void* c3,
+                    void* stream) {
+  int rc = check_problem(p);
+  if (rc) return rc;
+  Layout L;
+  if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
+  if (p->tokens == 0) return 0;
+  if (!int_fp4 || !int_sf || !w2_fp4 || !w2_sf || !w2_alphas || !c3) return fail(REAXMOE_ERR_NULL, "gemm_w2: NULL pointer");
+  if (!aligned16(int_fp4) || !aligned16(int_sf) || !aligned16(w2_fp4) || !aligned16(w2_sf) || !aligned16(c3))
+    return fail(REAXMOE_ERR_MISALIGNED, "gemm_w2: operands must be 16-byte aligned");
+  const WS w = carve(workspace, L);
+  const GemmLaunch g = w2_launch(p, w, int_fp4, int_sf, w2_fp4, w2_sf, w2_alphas, c3);
+  if ((rc = launch_grouped_gemm(g, num_sms(), static_cast<cudaStream_t>(stream))))
+    return fail(rc, "gemm_w2 launch failed: %s", cudaGetErrorString(cudaPeekAtLastError()));
+  return cuda_check("gemm_w2");
+}
+
+int reaxmoe_combine(const reaxmoe_problem* p, const void* c3, const int32_t* c_map, const float* topk_weights,
+                    void* output, void* stream) {
+  int rc = check_problem(p);
+  if (rc) return rc;
+  if (p->tokens == 0) return 0;
+  if (!c3 || !c_map || !topk_weights || !output) return fail(REAXMOE_ERR_NULL, "combine: NULL pointer");
+  if (!aligned16(c3) || !aligned16(output)) return fail(REAXMOE_ERR_MISALIGNED, "combine: misaligned");
+  launch_combine(static_cast<const __nv_bfloat16*>(c3), c_map, topk_weights, p->tokens, p->hidden, p->topk,
+                 static_cast<__nv_bfloat16*>(output), num_sms(), static_cast<cudaStream_t>(stream));
+  return cuda_check("combine");
+}
+
+int reaxmoe_forward(const reaxmoe_forward_args* args, void* workspace, size_t workspace_bytes, void* stream) {
+  if (args == nullptr) return fail(REAXMOE_ERR_NULL, "forward: args is NULL");
+  const reaxmoe_problem* p = &args->p;
+  int rc = check_problem(p);
+  if (rc) return rc;
+  Layout L;
+  if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
+  if (p->tokens == 0) return 0;
+  if (!args->a || !args->a1_gscale || !args->w1_fp4 || !args->w1_sf || !args->w1_alphas || !args->a2_gscale ||
+      !args->w2_fp4 || !args->w2_sf || !args->w2_alphas || !args->topk_weights || !args->topk_ids || !args->output)
+    return fail(REAXMOE_ERR_NULL, "forward: NULL pointer in args");
+  if (!aligned16(args->a) || !aligned16(args->w1_fp4) || !aligned16(args->w1_sf) || !aligned16(args->w2_fp4) ||
+      !aligned16(args->w2_sf) || !aligned16(args->output))
+    return fail(REAXMOE_ERR_MISALIGNED, "forward: activations, weights and output must be 16-byte aligned");
+  const WS w = carve(workspace, L);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = do_plan(p, args->topk_ids, w, nullptr, nullptr, s))) return rc;
+  launch_permute_quant(static_cast<const __nv_bfloat16*>(args->a), args->a1_gscale, args->topk_ids, w.seg_base,
+                       w.eoff, w.boff, p->tokens, p->hidden, p->experts, p->topk, w.rep_fp4, w.rep_sf, w.c_map, s);
+  if ((rc = cuda_check("permute_quant"))) return rc;
+  const int sms = num_sms();
+  GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, args->w1_fp4, args->w1_sf, args->w1_alphas, args->a2_gscale,
+                             w.int_fp4, w.int_sf);
+  if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "forward: gemm_w13 launch failed");
+  GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, args->w2_fp4, args->w2_sf, args->w2_alphas, w.c3);
+  if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "forward: gemm_w2 launch failed");
+  launch_combine(w.c3, w.c_map, args->topk_weights, p->tokens, p->hidden, p->topk,
+                 static_cast<__nv_bfloat16*>(args->output), sms, s);
+  return cuda_check("forward");
+}
+
+int reaxmoe_quantize(const void* x, int32_t x_is_fp32, int64_t rows, int32_t cols, int32_t group_rows,
+                     const float* gscale, void* packed, void* scales, void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 64 != 0 || group_rows <= 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "quantize: rows=%lld cols=%d group_rows=%d", (long long)rows, cols, group_rows);
+  if (rows == 0) return 0;
+  if (!x || !gscale || !packed || !scales) return fail(REAXMOE_ERR_NULL, "quantize: NULL pointer");
+  if (!aligned16(x) || !aligned16(packed) || !aligned16(scales))
+    return fail(REAXMOE_ERR_MISALIGNED, "quantize: pointers must be 16-byte aligned");
+  launch_quantize(x, x_is_fp32 != 0, rows, cols, group_rows, gscale, static_cast<uint8_t*>(packed),
+                  static_cast<uint8_t*>(scales), static_cast<cudaStream_t>(stream));
+  return cuda_check("quantize");
+}
+
+int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, int32_t inter, int32_t hidden,
+                        void* w1p_fp4, void* w1p_sf, void* stream) {
+  if (experts < 1 || inter < 64 || inter % 64 != 0 || hidden < 128 || hidden % 128 != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "prepack_w13: experts=%d inter=%d hidden=%d", experts, inter, hidden);
+  if (!w1_fp4 || !w1_sf || !w1p_fp4 || !w1p_sf) return fail(REAXMOE_ERR_NULL, "prepack_w13: NULL pointer");
+  if (w1_fp4 == w1p_fp4 || w1_sf == w1p_sf) return fail(REAXMOE_ERR_BAD_SHAPE, "prepack_w13: in-place not allowed");
+  if (!aligned16(w1_fp4) || !aligned16(w1p_fp4)) return fail(REAXMOE_ERR_MISALIGNED, "prepack_w13: misaligned");
+  launch_prepack_w13(static_cast<const uint8_t*>(w1_fp4), static_cast<const uint8_t*>(w1_sf), experts, inter, hidden,
+                     static_cast<uint8_t*>(w1p_fp4), static_cast<uint8_t*>(w1p_sf), static_cast<cudaStream_t>(stream));
+  return cuda_check("prepack_w13");
+}
+
+int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream) {
+  if (workspace == nullptr || workspace_bytes < 64) return fail(REAXMOE_ERR_WORKSPACE, "read_status: bad workspace");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  if (cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return fail(REAXMOE_ERR_CUDA, "read_status: %s", cudaGetErrorString(cudaGetLastError()));
+  if (clear && v != 0) {
+    const int zero = 0;
+    cudaMemcpyAsync(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice, s);
+    cudaStreamSynchronize(s);
+  }
+  return v;
+}
+
+}  // extern "C"

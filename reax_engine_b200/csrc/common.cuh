@@ -1,0 +1,93 @@
+// common.cuh -- shared device helpers of the NVFP4 MoE library (sm_100a).
+//
+// NVFP4 numerics follow the reference's quantiser (engine/fp4.py:27-52, engine/fp4_triton.py:16-27):
+//   s  = e4m3_rn(min(bamax / (6 g), 448)),  sf = max(float(s) * g, 1e-30),  q = x / sf  (IEEE division),
+//   code = index of q on the e2m1 grid, ties to the even index, sign bit = (q < 0).
+// All float operations that the oracle reproduces use explicit _rn intrinsics so that nvcc cannot contract
+// them into FMAs.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/reaxmoe.h"
+
+namespace reaxmoe {
+
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopk = 16;
+constexpr int kSegTokens = 128;   // tokens per routing segment (count / permute CTA)
+
+__host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Scale-atom row blocks needed for S routed slots over E experts: sum_e ceil(count_e / 128) <= S/128 + E.
+__host__ __device__ inline int64_t sf_row_blocks(int64_t slots, int experts) { return slots / 128 + experts + 1; }
+
+// Byte offset of scale (row, 16-element block kb) in the 128x4 atom layout of a matrix with K/64 atom columns
+// (engine/fp4.py:16-24; engine/fp4_triton.py:38-39).
+__host__ __device__ inline int64_t sf_offset(int64_t row, int kb, int k64) {
+  return ((row >> 7) * k64 + (kb >> 2)) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 + (kb & 3);
+}
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// e4m3 (fn) round-to-nearest-even of a value in [0, 448] (torch .to(float8_e4m3fn) at engine/fp4.py:47).
+__device__ __forceinline__ uint32_t e4m3_rn(float x) {
+  return (uint32_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// e2m1 code of q (already divided by the block scale): thresholds at the grid midpoints, ties to the even
+// index (engine/fp4.py:27-36; the same comparisons as engine/fp4_triton.py:24-26).
+__device__ __forceinline__ uint32_t e2m1_code(float q) {
+  const float a = fabsf(q);
+  uint32_t idx = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) + (a >= 3.5f) + (a > 5.0f);
+  return idx | ((q < 0.0f) ? 8u : 0u);
+}
+
+// Quantise one 16-element block with dequant-side global scale g. Returns the e4m3 scale byte; writes the
+// 8 packed bytes (element 2i in the low nibble of byte i) into lo/hi words.
+__device__ __forceinline__ uint32_t quant_block16(const float (&v)[16], float g, uint32_t& lo, uint32_t& hi) {
+  float bamax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(v[i]));
+  const float s = fminf(__fdiv_rn(bamax, __fmul_rn(6.0f, g)), 448.0f);
+  const uint32_t s8 = e4m3_rn(s);
+  const float sf = fmaxf(__fmul_rn(e4m3_to_f32(s8), g), 1e-30f);
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t c = e2m1_code(__fdiv_rn(v[i], sf));
+    w[i >> 3] |= c << ((i & 7) * 4);
+  }
+  lo = w[0];
+  hi = w[1];
+  return s8;
+}
+
+// Unpack 8 bf16 (one uint4) to floats.
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const uint32_t l = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return l | (h << 16);
+}
+
+// Device status word: first error wins.
+__device__ __forceinline__ void set_status(int* status, int code) {
+  if (status != nullptr) atomicCAS(status, 0, code);
+}
+
+}  // namespace reaxmoe

@@ -1,0 +1,499 @@
+// gemm_sm100.cu -- persistent grouped NVFP4 GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Replaces the reference's sm_120a grouped GEMMs (champions/uid240/opt/blink/blink_moegemm.cu:472-934 "bmoe"
+// MODE 0/1 and bmoe69.cu variant 11) and the stock vLLM cutlass_fp4_moe_mm + activation + quant chain
+// (vllm/model_executor/layers/fused_moe/experts/cutlass_moe.py:609-648). Same arithmetic per output element:
+//   acc = sum over K of e2m1(A) * e4m3(sfA) * e2m1(B) * e4m3(sfB)   (block-scaled MMA, fp32 accumulation)
+//   mode 0 (w2):  out = bf16(alpha_e * acc)
+//   mode 1 (w13): gate/up = bf16(alpha_e * acc); h = bf16(bf16(act(gate)) * up); NVFP4 quant of h with the
+//                 expert's intermediate scale (engine/fp4.py numerics) -> FP4 rows + 128x4 scale atoms.
+//
+// Design (one CTA per SM, persistent over a static list of (expert, 128-row m-tile, 128-col n-tile) units):
+//   warp 0      TMA producer: A (routed FP4 rows) and B (expert weights) tiles by 2D TMA with 128-byte
+//               swizzle, the matching 512-byte scale atoms by 1D bulk copies, into a STAGES-deep smem ring.
+//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.cp (scale atoms smem -> TMEM,
+//               32x128b.warpx4) and tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=128, K=64 per
+//               instruction) into a double-buffered fp32 accumulator, and tcgen05.commit to free the stage.
+//   warps 2..9  epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane TMEM quarter and half of the
+//               columns), release it to the MMA warp at once, then convert / activate / quantise and store.
+// Every mbarrier wait is bounded (globaltimer); on expiry the CTA records REAXMOE_ERR_DEVICE_TIMEOUT in the
+// status word, raises a CTA-wide abort flag, drains its own in-flight copies and MMAs, frees TMEM and returns.
+// No TMA multicast and no clusters: the same kernel runs on every rank of the expert-parallel path.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace reaxmoe {
+namespace gemm {
+
+constexpr int BM = 128;                 // rows per tile (MMA M)
+constexpr int BN = 128;                 // cols per tile (MMA N); mode 1: 64 gate + 64 up columns
+constexpr int KSTEP = 64;               // K per tcgen05.mma (FP4)
+constexpr int KSTAGE = 256;             // K per pipeline stage = one 128-byte swizzle row of FP4
+constexpr int KPS = KSTAGE / KSTEP;     // MMAs (and scale atoms) per stage
+constexpr int A_BYTES = BM * KSTAGE / 2;
+constexpr int B_BYTES = BN * KSTAGE / 2;
+constexpr int SF_BYTES = KPS * 512;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 2 * SF_BYTES;
+constexpr int STAGES = 5;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int THREADS = (2 + NUM_EPI_WARPS) * 32;
+constexpr int TMEM_COLS = 512;
+constexpr int SFA_COL = 2 * BN;         // after the two accumulators
+constexpr int SFB_COL = SFA_COL + 4 * KPS;
+constexpr int SMEM_TABLE_INTS = 4 * (kMaxExperts + 1);
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + SMEM_TABLE_INTS * 4;
+static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned for the 128B swizzle");
+static_assert(SFB_COL + 4 * KPS <= TMEM_COLS, "TMEM budget");
+
+// Instruction descriptor of tcgen05.mma.kind::mxf4nvf4 (block-scaled): A/B = e2m1 (MXF4 format 1) at bits
+// [7,10) / [10,13), K-major both, N >> 3 at [17,23), scale type ue4m3 (0) at bit 23, M >> 4 at [24,29),
+// scale-factor ids 0, dense K = 64.
+constexpr uint32_t IDESC = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+struct Params {
+  CUtensorMap tmA;  // [slots, K/2] u8, box 128 x 128 rows, 128B swizzle
+  CUtensorMap tmB;  // [E*N, K/2] u8, same box
+  const uint8_t* sfA;
+  const uint8_t* sfB;
+  const float* alphas;
+  const int* counts;
+  const int* eoff;
+  const int* boff;
+  const int* tile_prefix;
+  __nv_bfloat16* out;
+  uint8_t* q_out;
+  uint8_t* q_sf;
+  const float* q_gscale;
+  int* status;
+  unsigned long long timeout_ns;
+  int E, N, K, n_tiles, k_chunks;
+};
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void tc_mma_fp4(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
+                                           uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+// 32 lanes x 32 columns of 32-bit: thread i of the warp gets lane (quarter*32 + i), columns [col, col+32).
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm_100 format, version 1 at bits [46,48)): start >> 4 at [0,14),
+// leading byte offset >> 4 at [16,30), stride byte offset >> 4 at [32,46), layout at [61,64).
+// A/B tiles: K-major, 128-byte swizzle, 8-row core-matrix groups 1024 bytes apart (SBO), LBO unused (1).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Scale atoms for tcgen05.cp 32x128b: no swizzle, 32 rows x 16 bytes, 8-row core matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (8ull << 32) | (1ull << 46);
+}
+
+// Bounded wait. Returns false if the CTA aborted or the deadline passed (then records the timeout).
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                             unsigned long long timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 31u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > timeout_ns) {
+        *abort_flag = 1;
+        set_status(status, REAXMOE_ERR_DEVICE_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+// Drain wait: ignores the abort flag, short deadline; used only to let in-flight async work land.
+__device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > 20000000ull) return;  // 20 ms
+  }
+}
+
+struct Unit {
+  int e, mt, nt, row0, rows, sfblk;
+};
+
+__device__ __forceinline__ Unit decode(int u, int n_tiles, int E, const int* s_tp, const int* s_cnt,
+                                       const int* s_eoff, const int* s_boff) {
+  const int gm = u / n_tiles;
+  Unit r;
+  r.nt = u - gm * n_tiles;
+  int lo = 0, hi = E;  // largest e < E with s_tp[e] <= gm
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (s_tp[mid] <= gm) lo = mid; else hi = mid;
+  }
+  r.e = lo;
+  r.mt = gm - s_tp[lo];
+  r.row0 = s_eoff[lo] + r.mt * BM;
+  r.rows = min(BM, s_cnt[lo] - r.mt * BM);
+  r.sfblk = (s_boff[lo] >> 7) + r.mt;
+  return r;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f, kKappa = 0.044715f;
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(kBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+template <int MODE, int ACT>
+__global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* accf = bars + 2 * STAGES;
+  uint64_t* acce = accf + 2;
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  int* s_tp = reinterpret_cast<int*>(smem + STAGES * STAGE_BYTES + 256);
+  int* s_cnt = s_tp + (kMaxExperts + 1);
+  int* s_eoff = s_cnt + (kMaxExperts + 1);
+  int* s_boff = s_eoff + (kMaxExperts + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int E = p.E;
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    s_tp[i] = p.tile_prefix[i];
+    if (i < E) {
+      s_cnt[i] = p.counts[i];
+      s_eoff[i] = p.eoff[i];
+      s_boff[i] = p.boff[i];
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&accf[b]), 1);
+      mbar_init(smem_u32(&acce[b]), NUM_EPI_WARPS);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int n_tiles = p.n_tiles;
+  const int total_units = s_tp[E] * n_tiles;
+  const int k_chunks = p.k_chunks;
+  const int k_stages = (k_chunks + KPS - 1) / KPS;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long fills = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        const Unit U = decode(u, n_tiles, E, s_tp, s_cnt, s_eoff, s_boff);
+        const int brow = U.e * p.N + U.nt * BN;
+        const uint8_t* sfa = p.sfA + (size_t)U.sfblk * k_chunks * 512;
+        const uint8_t* sfb = p.sfB + ((size_t)U.e * (p.N / 128) + U.nt) * k_chunks * 512;
+        for (int ks = 0; ks < k_stages; ++ks) {
+          const int kc0 = ks * KPS;
+          const int nk = min(KPS, k_chunks - kc0);
+          if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + stage * STAGE_BYTES;
+          const uint32_t bar = smem_u32(&full[stage]);
+          mbar_expect_tx(bar, (uint32_t)(A_BYTES + B_BYTES + 2 * nk * 512));
+          tma_load_2d(smem_u32(st), &p.tmA, bar, kc0 * (KSTEP / 2), U.row0);
+          tma_load_2d(smem_u32(st + A_BYTES), &p.tmB, bar, kc0 * (KSTEP / 2), brow);
+          bulk_load(smem_u32(st + A_BYTES + B_BYTES), sfa + (size_t)kc0 * 512, (uint32_t)(nk * 512), bar);
+          bulk_load(smem_u32(st + A_BYTES + B_BYTES + SF_BYTES), sfb + (size_t)kc0 * 512, (uint32_t)(nk * 512), bar);
+          ++fills;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // let the last fills of every stage land before the CTA may exit (only matters after an abort)
+      for (long f = fills - 1; f >= 0 && f >= fills - STAGES; --f)
+        wait_drain(smem_u32(&full[f % STAGES]), (uint32_t)((f / STAGES) & 1));
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        if (!wait_bounded(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, p.status, p.timeout_ns)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
+        for (int ks = 0; ks < k_stages; ++ks) {
+          const int nk = min(KPS, k_chunks - ks * KPS);
+          if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag, p.status, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_s = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_s = a_s + A_BYTES;
+          const uint32_t sfa_s = b_s + B_BYTES;
+          const uint32_t sfb_s = sfa_s + SF_BYTES;
+          for (int kk = 0; kk < nk; ++kk) {
+            tc_cp_sf(tmem + SFA_COL + 4 * kk, desc_sf(sfa_s + kk * 512));
+            tc_cp_sf(tmem + SFB_COL + 4 * kk, desc_sf(sfb_s + kk * 512));
+            tc_mma_fp4(d_tmem, desc_sw128(a_s + kk * (KSTEP / 2)), desc_sw128(b_s + kk * (KSTEP / 2)), IDESC,
+                       tmem + SFA_COL + 4 * kk, tmem + SFB_COL + 4 * kk, (ks | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&accf[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // all tcgen05 work of this thread has completed once this commit arrives
+      tc_commit(smem_u32(drain));
+      wait_drain(smem_u32(drain), 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue warps
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int sub = (warp - 2) >> 2;        // which half of the tile's columns
+    const int r = q * 32 + lane;            // row inside the tile
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+      const Unit U = decode(u, n_tiles, E, s_tp, s_cnt, s_eoff, s_boff);
+      if (!wait_bounded(smem_u32(&accf[acc]), acc_phase, abort_flag, p.status, p.timeout_ns)) break;
+      tc_fence_after();
+      const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      uint32_t x0[32], x1[32];
+      if constexpr (MODE == 0) {
+        tc_ld_32x32b_x32(t_base + sub * 64, x0);
+        tc_ld_32x32b_x32(t_base + sub * 64 + 32, x1);
+      } else {
+        tc_ld_32x32b_x32(t_base + sub * 32, x0);        // gate columns
+        tc_ld_32x32b_x32(t_base + 64 + sub * 32, x1);   // up columns
+      }
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+      if (r >= U.rows) continue;
+      const float alpha = p.alphas[U.e];
+      const int64_t row = (int64_t)U.row0 + r;
+      if constexpr (MODE == 0) {
+        uint4* dst = reinterpret_cast<uint4*>(p.out + row * p.N + U.nt * BN + sub * 64);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint4 o;
+          o.x = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x0[8 * i + 0])), __fmul_rn(alpha, __uint_as_float(x0[8 * i + 1])));
+          o.y = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x0[8 * i + 2])), __fmul_rn(alpha, __uint_as_float(x0[8 * i + 3])));
+          o.z = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x0[8 * i + 4])), __fmul_rn(alpha, __uint_as_float(x0[8 * i + 5])));
+          o.w = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x0[8 * i + 6])), __fmul_rn(alpha, __uint_as_float(x0[8 * i + 7])));
+          dst[i] = o;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint4 o;
+          o.x = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x1[8 * i + 0])), __fmul_rn(alpha, __uint_as_float(x1[8 * i + 1])));
+          o.y = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x1[8 * i + 2])), __fmul_rn(alpha, __uint_as_float(x1[8 * i + 3])));
+          o.z = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x1[8 * i + 4])), __fmul_rn(alpha, __uint_as_float(x1[8 * i + 5])));
+          o.w = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x1[8 * i + 6])), __fmul_rn(alpha, __uint_as_float(x1[8 * i + 7])));
+          dst[4 + i] = o;
+        }
+      } else {
+        const float g = __fdiv_rn(1.0f, p.q_gscale[U.e]);
+        const int inter = p.N / 2;
+        uint32_t w[4];
+        uint32_t sbytes = 0u;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          float h[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float gate = bf16r(__fmul_rn(alpha, __uint_as_float(x0[16 * b + i])));
+            const float up = bf16r(__fmul_rn(alpha, __uint_as_float(x1[16 * b + i])));
+            const float a = bf16r(ACT == REAXMOE_ACT_GELU_TANH ? gelu_tanh(gate) : silu(gate));
+            h[i] = bf16r(__fmul_rn(a, up));
+          }
+          sbytes |= quant_block16(h, g, w[2 * b], w[2 * b + 1]) << (8 * b);
+        }
+        *reinterpret_cast<uint4*>(p.q_out + row * (inter / 2) + U.nt * 32 + sub * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        const int64_t sfrow = (int64_t)U.sfblk * 128 + r;
+        *reinterpret_cast<uint16_t*>(p.q_sf + sf_offset(sfrow, U.nt * 4 + sub * 2, inter / 64)) = (uint16_t)sbytes;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+static int make_map(CUtensorMap* tm, const void* base, int64_t rows, int row_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return REAXMOE_ERR_CUDA;
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {128u, 128u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : REAXMOE_ERR_CUDA;
+}
+
+template <int MODE, int ACT>
+static int launch_t(const Params& prm, int grid, cudaStream_t s) {
+  auto kfn = grouped_gemm_kernel<MODE, ACT>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+    return REAXMOE_ERR_CUDA;
+  kfn<<<grid, THREADS, SMEM_BYTES, s>>>(prm);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
+}
+
+}  // namespace gemm
+
+int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
+  using namespace gemm;
+  if (g.slots == 0) return 0;
+  Params prm;
+  memset(&prm, 0, sizeof(prm));
+  int rc = make_map(&prm.tmA, g.a, g.slots, g.K / 2);
+  if (rc) return rc;
+  rc = make_map(&prm.tmB, g.b, (int64_t)g.E * g.N, g.K / 2);
+  if (rc) return rc;
+  prm.sfA = static_cast<const uint8_t*>(g.a_sf);
+  prm.sfB = static_cast<const uint8_t*>(g.b_sf);
+  prm.alphas = g.alphas;
+  prm.counts = g.counts;
+  prm.eoff = g.eoff;
+  prm.boff = g.boff;
+  prm.tile_prefix = g.tile_prefix;
+  prm.out = static_cast<__nv_bfloat16*>(g.out);
+  prm.q_out = static_cast<uint8_t*>(g.q_out);
+  prm.q_sf = static_cast<uint8_t*>(g.q_sf);
+  prm.q_gscale = g.q_gscale;
+  prm.status = g.status;
+  prm.timeout_ns = g.timeout_ns;
+  prm.E = g.E;
+  prm.N = g.N;
+  prm.K = g.K;
+  prm.n_tiles = g.N / BN;
+  prm.k_chunks = g.K / KSTEP;
+  const int64_t max_units = (g.slots / BM + g.E + 1) * (int64_t)prm.n_tiles;
+  const int grid = (int)(max_units < num_sms ? max_units : num_sms);
+  if (g.mode == 0) return launch_t<0, 0>(prm, grid, s);
+  if (g.act == REAXMOE_ACT_GELU_TANH) return launch_t<1, REAXMOE_ACT_GELU_TANH>(prm, grid, s);
+  return launch_t<1, REAXMOE_ACT_SILU>(prm, grid, s);
+}
+
+}  // namespace reaxmoe

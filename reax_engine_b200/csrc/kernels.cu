@@ -1,0 +1,466 @@
+// kernels.cu -- routing, routing data, permute+quantise, combine, NVFP4 quantisation and w13 prepack kernels.
+//
+// All of these are HBM- or latency-bound integer/byte work: 128-bit loads and stores where the layout allows,
+// warp shuffles for reductions, no tensor cores.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace reaxmoe {
+
+// ------------------------------------------------------------------------------------------------------
+// K1 route: Gemma-4 routing (vllm/model_executor/models/gemma4.py:183-203; Triton form :95-175).
+// One warp per token; lane l holds logits [l*V, l*V + V). Top-k by a total order on (logit, -index): the
+// larger logit wins, equal logits go to the lower expert id. -0.0 and +0.0 compare equal.
+// w_j = e_j / (e_0 + ... + e_{k-1}) * scale[id_j] with e_j = exp(l_j - l_max): softmax over all experts,
+// masked to the top-k and renormalised (the all-expert denominator cancels).
+// ------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t sortable_key(float v) {
+  uint32_t u = __float_as_uint(v);
+  if (u == 0x80000000u) u = 0u;  // -0.0 ties with +0.0
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int V>
+__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, const float* __restrict__ scale,
+                                                    int T, int E, int K, int* __restrict__ ids,
+                                                    float* __restrict__ weights) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const float* row = logits + t * E;
+  float v[V];
+  uint64_t key[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int idx = lane * V + i;
+    v[i] = idx < E ? row[idx] : 0.0f;
+    key[i] = idx < E ? ((uint64_t)sortable_key(v[i]) << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)idx) : 0ull;
+  }
+  int my_id = 0;
+  float my_val = 0.0f, top_val = 0.0f;
+  for (int j = 0; j < K; ++j) {
+    uint64_t best = 0ull;
+#pragma unroll
+    for (int i = 0; i < V; ++i) best = key[i] > best ? key[i] : best;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const uint64_t o = __shfl_xor_sync(0xffffffffu, best, off);
+      best = o > best ? o : best;
+    }
+    const int id = (int)(0xFFFFFFFFu - (uint32_t)best);
+    const int owner = id / V;
+    float val = 0.0f;
+    if (lane == owner) {
+#pragma unroll
+      for (int i = 0; i < V; ++i)
+        if (lane * V + i == id) { val = v[i]; key[i] = 0ull; }
+    }
+    val = __shfl_sync(0xffffffffu, val, owner);
+    if (j == 0) top_val = val;
+    if (lane == j) { my_id = id; my_val = val; }
+  }
+  const float ex = (lane < K) ? expf(my_val - top_val) : 0.0f;
+  float denom = 0.0f;
+  for (int j = 0; j < K; ++j) denom = __fadd_rn(denom, __shfl_sync(0xffffffffu, ex, j));
+  if (lane < K) {
+    float w = __fdiv_rn(ex, denom);
+    if (scale != nullptr) w = __fmul_rn(w, scale[my_id]);
+    ids[t * K + lane] = my_id;
+    weights[t * K + lane] = w;
+  }
+}
+
+int launch_route(const float* logits, const float* scale, int T, int E, int K, int* ids, float* w,
+                 cudaStream_t s) {
+  if (T == 0) return 0;
+  const int warps_per_block = 8;
+  const dim3 grid((unsigned)ceil_div64(T, warps_per_block));
+  if (E <= 32) route_kernel<1><<<grid, 256, 0, s>>>(logits, scale, T, E, K, ids, w);
+  else if (E <= 64) route_kernel<2><<<grid, 256, 0, s>>>(logits, scale, T, E, K, ids, w);
+  else if (E <= 128) route_kernel<4><<<grid, 256, 0, s>>>(logits, scale, T, E, K, ids, w);
+  else route_kernel<8><<<grid, 256, 0, s>>>(logits, scale, T, E, K, ids, w);
+  return 0;
+}
+
+// ------------------------------------------------------------------------------------------------------
+// K2a count: per-segment expert histogram (segment = kSegTokens consecutive tokens). Shared-memory integer
+// atomics: exact counts, independent of order. Out-of-range ids are flagged and skipped.
+// ------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) count_kernel(const int* __restrict__ ids, int m, int k, int E,
+                                                    int* __restrict__ seg_counts, int* status) {
+  __shared__ int hist[kMaxExperts];
+  for (int i = threadIdx.x; i < E; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int64_t t0 = (int64_t)blockIdx.x * kSegTokens;
+  const int n = (int)(kSegTokens < m - t0 ? (int64_t)kSegTokens : m - t0) * k;
+  const int* p = ids + t0 * k;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = p[i];
+    if ((unsigned)e < (unsigned)E) atomicAdd(&hist[e], 1);
+    else set_status(status, REAXMOE_ERR_BAD_EXPERT_ID);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < E; i += blockDim.x) seg_counts[(int64_t)blockIdx.x * E + i] = hist[i];
+}
+
+// ------------------------------------------------------------------------------------------------------
+// K2b plan: one CTA. Column scan of seg_counts [nseg, E] into seg_base (slots of expert e that precede
+// segment s), per-expert counts, expert_offsets[E+1], blockscale_offsets[E+1] (counts rounded up to 128),
+// tile_prefix[E+1] (128-row GEMM m-tiles) and, optionally, vLLM's problem_sizes1/2 [E, 3]
+// (get_cutlass_moe_mm_data; blink_moe.py:271-299).
+// ------------------------------------------------------------------------------------------------------
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanMaxParts = 32;
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restrict__ seg_counts, int nseg, int E,
+                                                            int* __restrict__ seg_base, int* __restrict__ counts,
+                                                            int* __restrict__ eoff, int* __restrict__ boff,
+                                                            int* __restrict__ tile_prefix, int* ps1, int* ps2,
+                                                            int n1, int k1, int n2, int k2) {
+  __shared__ int partial[kPlanMaxParts][kMaxExperts];
+  __shared__ int total[kMaxExperts];
+  const int P = min(kPlanMaxParts, kPlanThreads / E);
+  const int e = threadIdx.x % E;
+  const int part = threadIdx.x / E;
+  const int chunk = (nseg + P - 1) / P;
+  const int s0 = part * chunk;
+  const int s1 = min(nseg, s0 + chunk);
+  if (part < P) {
+    int sum = 0;
+    for (int s = s0; s < s1; ++s) sum += seg_counts[(int64_t)s * E + e];
+    partial[part][e] = sum;
+  }
+  __syncthreads();
+  if (part == 0) {
+    int run = 0;
+    for (int q = 0; q < P; ++q) {
+      const int c = partial[q][e];
+      partial[q][e] = run;
+      run += c;
+    }
+    total[e] = run;
+  }
+  __syncthreads();
+  if (part < P) {
+    int base = partial[part][e];
+    for (int s = s0; s < s1; ++s) {
+      const int64_t i = (int64_t)s * E + e;
+      const int c = seg_counts[i];
+      seg_base[i] = base;
+      base += c;
+    }
+  }
+  if (threadIdx.x == 0) {
+    int eo = 0, bo = 0, tp = 0;
+    for (int x = 0; x < E; ++x) {
+      const int c = total[x];
+      counts[x] = c;
+      eoff[x] = eo;
+      boff[x] = bo;
+      tile_prefix[x] = tp;
+      eo += c;
+      bo += (c + 127) / 128 * 128;
+      tp += (c + 127) / 128;
+    }
+    eoff[E] = eo;
+    boff[E] = bo;
+    tile_prefix[E] = tp;
+  }
+  if (ps1 != nullptr && threadIdx.x < E) {
+    ps1[threadIdx.x * 3 + 0] = total[threadIdx.x];
+    ps1[threadIdx.x * 3 + 1] = n1;
+    ps1[threadIdx.x * 3 + 2] = k1;
+  }
+  if (ps2 != nullptr && threadIdx.x < E) {
+    ps2[threadIdx.x * 3 + 0] = total[threadIdx.x];
+    ps2[threadIdx.x * 3 + 1] = n2;
+    ps2[threadIdx.x * 3 + 2] = k2;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------
+// K3 permute_quant: one CTA per segment.
+//  Phase A (warp 0): canonical slot of every (token, j) pair of the segment. For a chunk of 32 tokens
+//  (one per lane) each lane sets its bit in a per-expert shared mask for each of its k experts; the slot of
+//  (t, j) is run[e] + popc(mask[e] & lanes_below) where run[e] = expert_offsets[e] + seg_base[seg][e] + the
+//  slots of e in the earlier chunks. Token-major order inside an expert, no data-dependent atomics.
+//  Phase B (all warps): each token row is NVFP4-quantised once per distinct expert input scale and written
+//  to its k slots (FP4 bytes + one 32-bit word of 4 scale bytes per 64-element group), the same bytes as
+//  vLLM's per-slot quant of the shuffled rows (blink_moe.py:301-323, cutlass_moe.py:585-593).
+// ------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) permute_quant_kernel(
+    const __nv_bfloat16* __restrict__ a, const float* __restrict__ a1_gscale, const int* __restrict__ ids,
+    const int* __restrict__ seg_base, const int* __restrict__ eoff, const int* __restrict__ boff, int m, int H,
+    int E, int k, uint8_t* __restrict__ rep_fp4, uint8_t* __restrict__ rep_sf, int* __restrict__ c_map) {
+  __shared__ int run[kMaxExperts];
+  __shared__ uint32_t mask[kMaxExperts];
+  __shared__ float gq[kMaxExperts];
+  __shared__ int pos_s[kSegTokens * kMaxTopk];
+  __shared__ short exp_s[kSegTokens * kMaxTopk];
+  const int seg = blockIdx.x;
+  const int64_t t0 = (int64_t)seg * kSegTokens;
+  const int nt = (int)(kSegTokens < m - t0 ? (int64_t)kSegTokens : m - t0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    run[e] = eoff[e] + seg_base[(int64_t)seg * E + e];
+    mask[e] = 0u;
+    gq[e] = __fdiv_rn(1.0f, a1_gscale[e]);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t below = (1u << lane) - 1u;
+    for (int c0 = 0; c0 < nt; c0 += 32) {
+      const int tl = c0 + lane;
+      const bool active = tl < nt;
+      int ej[kMaxTopk];
+#pragma unroll
+      for (int j = 0; j < kMaxTopk; ++j) {
+        ej[j] = -1;
+        if (j < k && active) {
+          const int e = ids[(t0 + tl) * k + j];
+          if ((unsigned)e < (unsigned)E) {
+            ej[j] = e;
+            atomicOr(&mask[e], 1u << lane);
+          }
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kMaxTopk; ++j) {
+        if (j < k && active) {
+          int pos = -1;
+          if (ej[j] >= 0) pos = run[ej[j]] + __popc(mask[ej[j]] & below);
+          pos_s[tl * k + j] = pos;
+          exp_s[tl * k + j] = (short)ej[j];
+          c_map[(t0 + tl) * k + j] = pos;
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kMaxTopk; ++j) {
+        if (j < k && ej[j] >= 0) {
+          const uint32_t mk = mask[ej[j]];
+          if ((mk & below) == 0u) run[ej[j]] += __popc(mk);
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kMaxTopk; ++j)
+        if (j < k && ej[j] >= 0) mask[ej[j]] = 0u;
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  const int groups = H / 64;
+  const int k64 = H / 64;
+  const int nwarps = blockDim.x >> 5;
+  for (int tl = warp; tl < nt; tl += nwarps) {
+    const int64_t t = t0 + tl;
+    const uint4* src = reinterpret_cast<const uint4*>(a + t * H);
+    for (int grp = lane; grp < groups; grp += 32) {
+      float v[64];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) bf16x8_to_f32(__ldg(src + grp * 8 + i), v + 8 * i);
+      uint32_t w[8];
+      uint32_t sbytes = 0u;
+      uint32_t gbits = 0xFFFFFFFFu;  // a NaN pattern: never equal to a real scale
+      for (int j = 0; j < k; ++j) {
+        const int e = exp_s[tl * k + j];
+        if (e < 0) continue;
+        const float g = gq[e];
+        if (__float_as_uint(g) != gbits) {
+          gbits = __float_as_uint(g);
+          sbytes = 0u;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            float blk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) blk[i] = v[b * 16 + i];
+            const uint32_t s8 = quant_block16(blk, g, w[2 * b], w[2 * b + 1]);
+            sbytes |= s8 << (8 * b);
+          }
+        }
+        const int pos = pos_s[tl * k + j];
+        uint4* dst = reinterpret_cast<uint4*>(rep_fp4 + (int64_t)pos * (H / 2) + grp * 32);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        const int64_t sfrow = (int64_t)boff[e] + (pos - eoff[e]);
+        *reinterpret_cast<uint32_t*>(rep_sf + sf_offset(sfrow, grp * 4, k64)) = sbytes;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------
+// K7 combine: one warp per token, 8 columns (one 16-byte load per slot row) per lane step.
+// out = bf16( sum_j bf16( c3[c_map[t,j]] * bf16(w[t,j]) ) ), partial sums j % 4 in increasing j, then
+// ((s0 + s1) + s2) + s3 (blink_moe.py:168-198 ORDER 1 for top-8; cutlass_moe.py:650-662).
+// ------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ c3,
+                                                      const int* __restrict__ c_map,
+                                                      const float* __restrict__ topk_w, int m, int H, int k,
+                                                      __nv_bfloat16* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < m; t += warps) {
+    int mypos = 0;
+    float myw = 0.0f;
+    if (lane < k) {
+      mypos = c_map[t * k + lane];
+      myw = bf16r(topk_w[t * k + lane]);
+    }
+    int pos[kMaxTopk];
+    float wb[kMaxTopk];
+#pragma unroll
+    for (int j = 0; j < kMaxTopk; ++j) {
+      pos[j] = __shfl_sync(0xffffffffu, mypos, j);
+      wb[j] = __shfl_sync(0xffffffffu, myw, j);
+    }
+    for (int ch = lane; ch < H / 8; ch += 32) {
+      float part[4][8];
+#pragma unroll
+      for (int j = 0; j < kMaxTopk; ++j) {
+        if (j < k) {
+          float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (pos[j] >= 0)  // -1 marks a pair whose expert id was out of range (flagged by the plan)
+            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(c3 + (int64_t)pos[j] * H) + ch), f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float p = bf16r(__fmul_rn(f[i], wb[j]));
+            part[j & 3][i] = (j < 4) ? p : __fadd_rn(part[j & 3][i], p);
+          }
+        }
+      }
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[i] = part[0][i];
+        if (k > 1) acc[i] = __fadd_rn(acc[i], part[1][i]);
+        if (k > 2) acc[i] = __fadd_rn(acc[i], part[2][i]);
+        if (k > 3) acc[i] = __fadd_rn(acc[i], part[3][i]);
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      reinterpret_cast<uint4*>(out + t * H)[ch] = o;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------
+// NVFP4 quantisation of rows (engine/fp4.py::quantize_nvfp4 numerics; fp4_triton.py nvfp4_quant_static).
+// One warp per row, one 64-element group (4 scale blocks) per lane step.
+// ------------------------------------------------------------------------------------------------------
+template <bool F32>
+__global__ void __launch_bounds__(256) quantize_kernel(const void* __restrict__ x, int64_t rows, int cols,
+                                                       int group_rows, const float* __restrict__ gscale,
+                                                       uint8_t* __restrict__ packed, uint8_t* __restrict__ scales) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int64_t grp_id = r / group_rows;
+  const int64_t sfrow = grp_id * ((group_rows + 127) / 128 * 128) + (r - grp_id * group_rows);
+  const float g = __fdiv_rn(1.0f, gscale[grp_id]);
+  const int k64 = cols / 64;
+  for (int grp = lane; grp < cols / 64; grp += 32) {
+    float v[64];
+    if constexpr (F32) {
+      const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) + r * cols) + grp * 16;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 q = __ldg(src + i);
+        v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+      }
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + r * cols) + grp * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) bf16x8_to_f32(__ldg(src + i), v + 8 * i);
+    }
+    uint32_t w[8];
+    uint32_t sbytes = 0u;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      float blk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) blk[i] = v[b * 16 + i];
+      sbytes |= quant_block16(blk, g, w[2 * b], w[2 * b + 1]) << (8 * b);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(packed + r * (cols / 2) + grp * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    *reinterpret_cast<uint32_t*>(scales + sf_offset(sfrow, grp * 4, k64)) = sbytes;
+  }
+}
+
+int launch_quantize(const void* x, bool f32, int64_t rows, int cols, int group_rows, const float* gscale,
+                    uint8_t* packed, uint8_t* scales, cudaStream_t s) {
+  if (rows == 0) return 0;
+  const dim3 grid((unsigned)ceil_div64(rows, 8));
+  if (f32) quantize_kernel<true><<<grid, 256, 0, s>>>(x, rows, cols, group_rows, gscale, packed, scales);
+  else quantize_kernel<false><<<grid, 256, 0, s>>>(x, rows, cols, group_rows, gscale, packed, scales);
+  return 0;
+}
+
+// ------------------------------------------------------------------------------------------------------
+// w13 prepack: output row r (block b = r / 128, w = r % 128) <- gate row 64b + w (w < 64) or up row
+// inter + 64b + (w - 64); its 16-element block scales move with it.
+// ------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) prepack_w13_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ sf,
+                                                          int inter, int H, uint8_t* __restrict__ wp,
+                                                          uint8_t* __restrict__ sfp) {
+  const int N = 2 * inter;
+  const int e = blockIdx.y;
+  const int r = blockIdx.x;
+  const int b = r >> 7, wi = r & 127;
+  const int src = wi < 64 ? b * 64 + wi : inter + b * 64 + (wi - 64);
+  const int64_t row_bytes = H / 2;
+  const uint4* s4 = reinterpret_cast<const uint4*>(w + ((int64_t)e * N + src) * row_bytes);
+  uint4* d4 = reinterpret_cast<uint4*>(wp + ((int64_t)e * N + r) * row_bytes);
+  for (int i = threadIdx.x; i < row_bytes / 16; i += blockDim.x) d4[i] = s4[i];
+  const int k64 = H / 64;
+  const int64_t esz = (int64_t)(N / 128) * k64 * 512;
+  for (int kb = threadIdx.x; kb < H / 16; kb += blockDim.x)
+    sfp[e * esz + sf_offset(r, kb, k64)] = sf[e * esz + sf_offset(src, kb, k64)];
+}
+
+int launch_prepack_w13(const uint8_t* w, const uint8_t* sf, int E, int inter, int H, uint8_t* wp, uint8_t* sfp,
+                       cudaStream_t s) {
+  prepack_w13_kernel<<<dim3(2 * inter, E), 128, 0, s>>>(w, sf, inter, H, wp, sfp);
+  return 0;
+}
+
+int launch_count(const int* ids, int m, int k, int E, int* seg_counts, int* status, cudaStream_t s) {
+  const int nseg = (int)ceil_div64(m, kSegTokens);
+  if (nseg > 0) count_kernel<<<nseg, 256, 0, s>>>(ids, m, k, E, seg_counts, status);
+  return 0;
+}
+
+int launch_plan(const int* seg_counts, int nseg, int E, int* seg_base, int* counts, int* eoff, int* boff,
+                int* tile_prefix, int* ps1, int* ps2, int n1, int k1, int n2, int k2, cudaStream_t s) {
+  plan_kernel<<<1, kPlanThreads, 0, s>>>(seg_counts, nseg, E, seg_base, counts, eoff, boff, tile_prefix, ps1, ps2,
+                                         n1, k1, n2, k2);
+  return 0;
+}
+
+int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const int* seg_base,
+                         const int* eoff, const int* boff, int m, int H, int E, int k, uint8_t* rep_fp4,
+                         uint8_t* rep_sf, int* c_map, cudaStream_t s) {
+  const int nseg = (int)ceil_div64(m, kSegTokens);
+  if (nseg > 0)
+    permute_quant_kernel<<<nseg, 256, 0, s>>>(a, a1_gscale, ids, seg_base, eoff, boff, m, H, E, k, rep_fp4, rep_sf,
+                                              c_map);
+  return 0;
+}
+
+int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
+                   __nv_bfloat16* out, int num_sms, cudaStream_t s) {
+  if (m == 0) return 0;
+  const int64_t want = ceil_div64(m, 8), cap = (int64_t)num_sms * 8;
+  const int64_t blocks = want < cap ? want : cap;
+  combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, k, out);
+  return 0;
+}
+
+}  // namespace reaxmoe

@@ -1,0 +1,46 @@
+// kernels.cuh -- host launchers of the routing / permute / combine / quantise / prepack kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace reaxmoe {
+
+int launch_route(const float* logits, const float* scale, int T, int E, int K, int* ids, float* w, cudaStream_t s);
+int launch_count(const int* ids, int m, int k, int E, int* seg_counts, int* status, cudaStream_t s);
+int launch_plan(const int* seg_counts, int nseg, int E, int* seg_base, int* counts, int* eoff, int* boff,
+                int* tile_prefix, int* ps1, int* ps2, int n1, int k1, int n2, int k2, cudaStream_t s);
+int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const int* seg_base,
+                         const int* eoff, const int* boff, int m, int H, int E, int k, uint8_t* rep_fp4,
+                         uint8_t* rep_sf, int* c_map, cudaStream_t s);
+int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
+                   __nv_bfloat16* out, int num_sms, cudaStream_t s);
+int launch_quantize(const void* x, bool f32, int64_t rows, int cols, int group_rows, const float* gscale,
+                    uint8_t* packed, uint8_t* scales, cudaStream_t s);
+int launch_prepack_w13(const uint8_t* w, const uint8_t* sf, int E, int inter, int H, uint8_t* wp, uint8_t* sfp,
+                       cudaStream_t s);
+
+// Grouped NVFP4 GEMM (gemm_sm100.cu). mode 0: out bf16 [slots, N]; mode 1: fused act(gate)*up + NVFP4 quant
+// into q_out [slots, N/4] (N = 2*inter interleaved) and q_sf atoms.
+struct GemmLaunch {
+  int mode;          // 0 = plain (w2), 1 = w13 fused
+  int act;           // REAXMOE_ACT_*
+  const void* a;     // [slots, K/2]
+  int64_t slots;
+  const void* a_sf;  // atoms over blockscale rows
+  const void* b;     // [E, N, K/2]
+  const void* b_sf;  // [E][N/128][K/64][512]
+  const float* alphas;
+  int E, N, K;
+  const int* counts; const int* eoff; const int* boff; const int* tile_prefix;
+  void* out;         // mode 0: bf16 [slots, N]
+  void* q_out;       // mode 1: [slots, N/4]
+  void* q_sf;        // mode 1: atoms over blockscale rows, K/64 = (N/2)/64 atom columns
+  const float* q_gscale;
+  int* status;
+  unsigned long long timeout_ns;
+};
+int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s);
+
+}  // namespace reaxmoe

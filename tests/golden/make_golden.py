@@ -127,7 +127,7 @@ def route_cases(route_fn):
 
 def layer_case(fp4, route_fn, activation: str, seed: int):
     gen = torch.Generator().manual_seed(seed)
-    T, H, E, k, inter = 40, 256, 8, 2, 128
+    T, H, E, k, inter = 40, 256, 8, 2, 256
     x = torch.randn(T, H, generator=gen).bfloat16()
     gate_w = torch.randn(E, H, generator=gen) * 0.02
     w1 = torch.randn(E, 2 * inter, H, generator=gen) * 0.02

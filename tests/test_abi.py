@@ -1,0 +1,96 @@
+"""CPU checks of the C-ABI boundary: the library loads, exports every symbol include/reaxmoe.h declares, and its
+host-side argument checks return the documented status codes (no kernel is launched by these calls)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import reax_engine_b200 as R
+from reax_engine_b200 import _lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = ""
+    for f in os.listdir(os.path.join(ROOT, "include")):
+        if f.endswith(".h"):
+            src += open(os.path.join(ROOT, "include", f)).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(reaxmoe_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.lib()
+    names = declared_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in L.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_version():
+    assert L.lib().reaxmoe_version() >= 100
+
+
+def test_workspace_size_matches_layout():
+    m, H, I, E, k = 36864, 2816, 704, 128, 8
+    n = R.workspace_size(m, H, I, E, k)
+    slots = m * k
+    sfblk = slots // 128 + E + 1
+    expect_min = slots * (H // 2 + I // 2 + 2 * H + 4) + sfblk * (H // 64 + I // 64) * 512
+    assert expect_min <= n <= expect_min + 64 * 1024 + 2 * ((m + 127) // 128) * E * 4 + 4096
+
+
+@pytest.mark.parametrize("bad", [dict(hidden=200), dict(hidden=128), dict(inter=100), dict(experts=300),
+                                 dict(topk=17), dict(topk=9, experts=8), dict(tokens=-1), dict(activation=7)])
+def test_bad_shapes_rejected(bad):
+    p = dict(tokens=16, hidden=2816, inter=704, experts=128, topk=8, activation=1)
+    p.update(bad)
+    prob = L.problem(**p)
+    assert L.lib().reaxmoe_workspace_size(ctypes.byref(prob)) == 0
+    assert L.last_error()
+
+
+def test_forward_rejects_null_and_small_workspace():
+    lib = L.lib()
+    assert lib.reaxmoe_forward(None, None, 0, None) == L.ERR_NULL
+    args = L.ForwardArgs(L.problem(16, 2816, 704, 128, 8, 1))
+    assert lib.reaxmoe_forward(ctypes.byref(args), None, 0, None) == L.ERR_WORKSPACE
+    buf = ctypes.create_string_buffer(4096 + 16)
+    addr = (ctypes.addressof(buf) + 15) & ~15
+    assert lib.reaxmoe_forward(ctypes.byref(args), addr, 4096, None) == L.ERR_WORKSPACE
+    assert "workspace" in L.last_error()
+
+
+def test_forward_rejects_missing_pointers():
+    lib = L.lib()
+    prob = L.problem(16, 256, 256, 8, 2, 0)
+    n = lib.reaxmoe_workspace_size(ctypes.byref(prob))
+    buf = ctypes.create_string_buffer(n + 256)
+    addr = (ctypes.addressof(buf) + 255) & ~255
+    args = L.ForwardArgs(prob)
+    assert lib.reaxmoe_forward(ctypes.byref(args), addr, n, None) == L.ERR_NULL
+
+
+def test_route_rejects_unsupported():
+    lib = L.lib()
+    assert lib.reaxmoe_route(None, None, 4, 300, 8, None, None, None) == L.ERR_TOO_MANY_EXPERTS
+    assert lib.reaxmoe_route(None, None, 4, 128, 0, None, None, None) == L.ERR_TOO_MANY_EXPERTS
+    assert lib.reaxmoe_route(None, None, 4, 128, 8, None, None, None) == L.ERR_NULL
+    assert lib.reaxmoe_route(None, None, 0, 128, 8, None, None, None) == L.OK
+
+
+def test_quantize_and_prepack_reject_bad_args():
+    lib = L.lib()
+    assert lib.reaxmoe_quantize(None, 0, 4, 100, 4, None, None, None, None) == L.ERR_BAD_SHAPE
+    assert lib.reaxmoe_quantize(None, 0, 4, 128, 4, None, None, None, None) == L.ERR_NULL
+    assert lib.reaxmoe_prepack_w13(None, None, 4, 100, 256, None, None, None) == L.ERR_BAD_SHAPE
+    assert lib.reaxmoe_prepack_w13(None, None, 4, 128, 256, None, None, None) == L.ERR_NULL
+
+
+def test_python_api_refuses_cpu_tensors():
+    import torch
+    with pytest.raises(ValueError):
+        R.route(None, torch.zeros(4, 128), 8)

@@ -1,0 +1,368 @@
+"""Parity of every CUDA stage, called through the C ABI, against the CPU oracle on the same seeded inputs.
+
+Bit-exact: routing ids, per-expert counts / offsets, the canonical slot map, quantised bytes and scales, the w13
+prepack and the combine (given identical inputs). Tolerance (north star): layer output max-abs <= 2e-2 and
+rel-L2 <= 1e-2 of the bf16 reference; GEMM outputs compared element-wise within one bf16 ulp.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from moe_cases import ACT_ID, make_case, packed_lengths, tol_check, zipf_bias
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def R():
+    import reax_engine_b200 as R
+    return R
+
+
+def _sync():
+    torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------------------------------------------ routing
+
+@pytest.mark.parametrize("T,E,k", [(1, 128, 8), (33, 128, 8), (4096, 128, 8), (512, 64, 4), (77, 8, 2),
+                                   (300, 256, 16), (5, 32, 1)])
+def test_route_matches_oracle(R, T, E, k):
+    g = torch.Generator().manual_seed(T * 1000 + E)
+    logits = torch.randn(T, E, generator=g)
+    scale = torch.rand(E, generator=g) + 0.5
+    w, ids = R.route(None, logits.cuda(), k, True, scale.cuda())
+    wr, idr = O.route(logits.numpy(), k, scale.numpy())
+    assert np.array_equal(ids.cpu().numpy(), idr)
+    np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-7)
+
+
+def test_route_ties_go_to_lower_expert(R):
+    g = torch.Generator().manual_seed(5)
+    logits = torch.randint(-3, 3, (1000, 128), generator=g).float()   # many exact ties
+    logits[0] = 0.0
+    logits[1, 7] = -0.0
+    w, ids = R.route(None, logits.cuda(), 8)
+    wr, idr = O.route(logits.numpy(), 8)
+    assert np.array_equal(ids.cpu().numpy(), idr)
+    assert ids[0].tolist() == list(range(8))
+    np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-7)
+
+
+def test_route_golden_vllm(R):
+    d = np.load(os.path.join(G, "route_golden.npz"))
+    for name in ("e128k8", "e64k4"):
+        k = d[f"{name}_ids"].shape[1]
+        w, ids = R.route(None, torch.from_numpy(d[f"{name}_logits"]).cuda(), k, True,
+                         torch.from_numpy(d[f"{name}_scale"]).cuda())
+        assert np.array_equal(ids.cpu().numpy(), d[f"{name}_ids"])
+        np.testing.assert_allclose(w.cpu().numpy(), d[f"{name}_w"], rtol=1e-5, atol=1e-7)
+
+
+# ------------------------------------------------------------------------------------------------ NVFP4 quant
+
+@pytest.mark.parametrize("case", ["a", "b", "c", "d"])
+def test_quantize_golden_engine_fp4(R, case):
+    """The device quantiser reproduces engine/fp4.py::quantize_nvfp4 bytes (fp32 input)."""
+    d = np.load(os.path.join(G, "quant_golden.npz"))
+    x = d[f"{case}_x"]
+    if x.shape[1] % 64:
+        pytest.skip("device quantiser works on 64-column groups")
+    g = d[f"{case}_g"]
+    gs = np.float32(1.0) / np.float32(g)
+    if np.float32(1.0) / gs != np.float32(g):
+        pytest.skip("scale not representable as a quant-side reciprocal")
+    packed, sf = R.quantize_nvfp4(torch.from_numpy(x).cuda(), torch.tensor([gs]).cuda())
+    assert np.array_equal(packed.cpu().numpy(), d[f"{case}_packed"])
+    n = d[f"{case}_sf"].size
+    assert np.array_equal(sf.cpu().numpy()[:n], d[f"{case}_sf"])
+
+
+@pytest.mark.parametrize("rows,cols,group", [(1, 64, 1), (300, 2816, 300), (256, 704, 128), (130, 2048, 65)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_quantize_matches_oracle(R, rows, cols, group, dtype):
+    g = torch.Generator().manual_seed(rows + cols)
+    x = (torch.randn(rows, cols, generator=g) * torch.rand(1, cols, generator=g) * 4).to(dtype)
+    x[0, :16] = 0.0
+    groups = -(-rows // group)
+    gs = (2688.0 / (torch.rand(groups, generator=g) * 5 + 0.5)).float()
+    packed, sf = R.quantize_nvfp4(x.cuda(), gs.cuda(), group_rows=group)
+    xf = x.float().numpy()
+    gq = O.inv_scale(gs.numpy())
+    row_g = gq[np.arange(rows) // group]
+    p_ref, s_ref = O.quantize_rows(xf, row_g)
+    assert np.array_equal(packed.cpu().numpy(), p_ref)
+    sfn = sf.cpu().numpy()
+    rows_idx = (np.arange(rows) // group) * (-(-group // 128) * 128) + np.arange(rows) % group
+    r, c = np.meshgrid(rows_idx, np.arange(cols // 16), indexing="ij")
+    assert np.array_equal(sfn[O.swizzle_offset(r, c, cols // 16)], s_ref)
+
+
+def test_prepack_w13_matches_oracle(R):
+    E, inter, H = 3, 320, 256
+    g = torch.Generator(device="cuda").manual_seed(3)
+    w = torch.randn(E, 2 * inter, H, generator=g, device="cuda") * 0.02
+    q, s, _ = R.quantize_weights(w)
+    qp, sp = R.prepack_w13(q, s, inter)
+    rq, rs = O.interleave_w13(q.cpu().numpy(), s.cpu().numpy(), inter)
+    assert np.array_equal(qp.cpu().numpy(), rq)
+    assert np.array_equal(sp.cpu().numpy(), rs)
+
+
+# ------------------------------------------------------------------------------------------------ plan / permute
+
+def _plan_permute(R, c):
+    st = R.Stages(c["T"], c["H"], c["inter"], c["E"], c["k"], c["act"], "cuda")
+    w, ids = R.route(None, c["logits"], c["k"])
+    st.plan(ids)
+    st.permute_quant(c["x"], c["a1_gscale"])
+    _sync()
+    assert st.status() == 0
+    return st, w, ids
+
+
+@pytest.mark.parametrize("T,skew", [(1, None), (130, None), (389, None), (1024, 1.0), (16, 1.0)])
+def test_plan_and_permute_bit_exact(R, T, skew):
+    c = make_case(T, 256, 64, 4, 256, "silu", seed=T, skew=skew)
+    st, w, ids = _plan_permute(R, c)
+    n = c["np"]
+    wr, idr = O.route(n["logits"], c["k"])
+    assert np.array_equal(ids.cpu().numpy(), idr)
+    pl = O.plan(idr, c["E"])
+    assert np.array_equal(st.expert_offsets.cpu().numpy(), pl["expert_offsets"])
+    assert np.array_equal(st.blockscale_offsets.cpu().numpy(), pl["blockscale_offsets"])
+    ps1 = st.problem_sizes1.cpu().numpy()
+    assert np.array_equal(ps1[:, 0], pl["counts"])
+    assert np.array_equal(st.c_map.cpu().numpy(), pl["c_map"])
+    rep, rsf = O.permute_quant(n["x"], idr, n["a1_gscale"], pl)
+    assert np.array_equal(st.rep_fp4.cpu().numpy(), rep)
+    used = O.sf_rows(pl)
+    r, cc = np.meshgrid(used, np.arange(c["H"] // 16), indexing="ij")
+    off = O.swizzle_offset(r, cc, c["H"] // 16)
+    assert np.array_equal(st.rep_sf.cpu().numpy()[off], rsf[off])
+
+
+def test_permute_nonuniform_input_scales(R):
+    c = make_case(200, 256, 8, 2, 256, "silu", seed=11)
+    c["a1_gscale"] = torch.linspace(50, 400, c["E"]).float().cuda()
+    c["np"]["a1_gscale"] = c["a1_gscale"].cpu().numpy()
+    st, w, ids = _plan_permute(R, c)
+    idr = ids.cpu().numpy()
+    pl = O.plan(idr, c["E"])
+    rep, rsf = O.permute_quant(c["np"]["x"], idr, c["np"]["a1_gscale"], pl)
+    assert np.array_equal(st.rep_fp4.cpu().numpy(), rep)
+
+
+# ------------------------------------------------------------------------------------------------ GEMMs
+
+def _ulp_close(got, ref, frac_exact=0.99):
+    """bf16 results within one bf16 ulp of the oracle, and nearly all identical."""
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    tol = np.maximum(np.abs(ref) * 2.0 ** -7, 1e-6)
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), f"{bad.sum()} elements beyond one bf16 ulp; max diff {np.abs(got - ref).max()}"
+    assert (got == ref).mean() >= frac_exact
+
+
+@pytest.mark.parametrize("shape", [(256, 256, 8, 2, 256), (512, 2048, 64, 4, 1024), (300, 2816, 128, 8, 704)])
+def test_gemm_w2_matches_oracle(R, shape):
+    T, H, E, k, inter = shape
+    c = make_case(T, H, E, k, inter, "gelu_tanh", seed=21)
+    n = c["np"]
+    wr, idr = O.route(n["logits"], k)
+    pl = O.plan(idr, E)
+    # oracle intermediate as the GEMM input
+    g = torch.Generator().manual_seed(4)
+    h = (torch.randn(T * k, inter, generator=g) * 2).bfloat16().float().numpy()
+    gq = O.inv_scale(n["a2_gscale"])
+    packed, s8 = O.quantize_rows(h, gq[pl["slot_expert"]])
+    sf = np.zeros((T * k // 128 + E + 1) * (inter // 64) * 512, np.uint8)
+    r, cc = np.meshgrid(O.sf_rows(pl), np.arange(inter // 16), indexing="ij")
+    sf[O.swizzle_offset(r, cc, inter // 16)] = s8
+    c3_ref = O.grouped_gemm(packed, sf, n["w2q"], n["w2s"], n["w2_alphas"], pl)
+    st = R.Stages(T, H, inter, E, k, "gelu_tanh", "cuda")
+    st.plan(torch.from_numpy(idr).cuda())
+    st.gemm_w2(c["w2q"], c["w2s"], c["w2_alphas"], int_fp4=torch.from_numpy(packed).cuda(),
+               int_sf=torch.from_numpy(sf).cuda())
+    _sync()
+    assert st.status() == 0
+    _ulp_close(st.c3.float().cpu().numpy(), c3_ref)
+
+
+@pytest.mark.parametrize("act", ["gelu_tanh", "silu"])
+@pytest.mark.parametrize("shape", [(256, 256, 8, 2, 256), (300, 2816, 128, 8, 704)])
+def test_gemm_w13_fused_matches_oracle(R, act, shape):
+    T, H, E, k, inter = shape
+    c = make_case(T, H, E, k, inter, act, seed=31)
+    n = c["np"]
+    wr, idr = O.route(n["logits"], k)
+    pl = O.plan(idr, E)
+    rep, rsf = O.permute_quant(n["x"], idr, n["a1_gscale"], pl)
+    c1 = O.grouped_gemm(rep, rsf, n["w1q"], n["w1s"], n["w1_alphas"], pl)
+    int_fp4, int_sf, hh = O.act_quant(c1, n["a2_gscale"], act, pl, inter)
+    st = R.Stages(T, H, inter, E, k, act, "cuda")
+    st.plan(torch.from_numpy(idr).cuda())
+    w1p, w1p_sf = R.prepack_w13(c["w1q"], c["w1s"], inter)
+    st.gemm_w13(w1p, w1p_sf, c["w1_alphas"], c["a2_gscale"], rep_fp4=torch.from_numpy(rep).cuda(),
+                rep_sf=torch.from_numpy(rsf).cuda())
+    _sync()
+    assert st.status() == 0
+    got = st.int_fp4.cpu().numpy()
+    assert (got == int_fp4).mean() >= 0.98
+    # dequantised intermediate (values x block scales) within tolerance of the oracle's
+    used = O.sf_rows(pl)
+    r, cc = np.meshgrid(used, np.arange(inter // 16), indexing="ij")
+    off = O.swizzle_offset(r, cc, inter // 16)
+    hg = O.dequant(got, st.int_sf.cpu().numpy()[off])
+    hr = O.dequant(int_fp4, int_sf[off])
+    assert np.abs(hg - hr).max() <= 0.25 * max(1.0, np.abs(hr).max())
+    assert np.linalg.norm(hg - hr) <= 2e-2 * np.linalg.norm(hr)
+
+
+# ------------------------------------------------------------------------------------------------ combine
+
+@pytest.mark.parametrize("k", [1, 2, 4, 6, 8])
+def test_combine_bit_exact(R, k):
+    T, H, E = 257, 512, 16
+    g = torch.Generator().manual_seed(k)
+    logits = torch.randn(T, E, generator=g)
+    wr, idr = O.route(logits.numpy(), k)
+    pl = O.plan(idr, E)
+    c3 = (torch.randn(T * k, H, generator=g) * 3).bfloat16()
+    ref = O.combine(c3.float().numpy(), pl["c_map"], wr)
+    st = R.Stages(T, H, 256, E, k, "silu", "cuda")
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    st.combine(torch.from_numpy(wr).cuda(), out, c3=c3.cuda(), c_map=torch.from_numpy(pl["c_map"]).cuda())
+    _sync()
+    assert np.array_equal(out.float().cpu().numpy(), ref)
+
+
+# ------------------------------------------------------------------------------------------------ whole layer
+
+def _run_layer(R, c, w, ids):
+    out = torch.empty(c["T"], c["H"], dtype=torch.bfloat16, device="cuda")
+    R.run_moe_nvfp4(out, c["x"], c["a1_gscale"], c["w1q"], c["w1s"], c["w1_alphas"], c["a2_gscale"], c["w2q"],
+                    c["w2s"], c["w2_alphas"], w, ids, c["act"], None, None, c["T"], c["inter"], c["H"], c["E"],
+                    "cuda")
+    _sync()
+    return out
+
+
+def _oracle_layer(c, w, ids, wcache=None):
+    n = c["np"]
+    return O.moe_forward(n["x"], w, ids, n["w1q"], n["w1s"], n["w1_alphas"], n["w2q"], n["w2s"], n["w2_alphas"],
+                         n["a1_gscale"], n["a2_gscale"], c["act"], wcache)
+
+
+@pytest.mark.parametrize("name,shape,act,skew", [
+    ("cfg1_packed_4seq", (sum([64, 96, 160, 192]), 2048, 64, 4, 1024), "silu", None),
+    ("cfg2_shape_T256", (256, 2816, 128, 8, 704), "gelu_tanh", None),
+    ("cfg5_skew_T16", (16, 2816, 128, 8, 704), "gelu_tanh", 2.0),
+    ("small_T1", (1, 256, 8, 2, 256), "gelu_tanh", None),
+])
+def test_layer_matches_oracle(R, name, shape, act, skew):
+    T, H, E, k, inter = shape
+    c = make_case(T, H, E, k, inter, act, seed=0, skew=skew)
+    w, ids = R.route(None, c["logits"], k)
+    out = _run_layer(R, c, w, ids)
+    ref = _oracle_layer(c, w.cpu().numpy(), ids.cpu().numpy())
+    tol_check(out.float().cpu().numpy(), ref["out"])
+
+
+@pytest.mark.parametrize("act", ["gelu_tanh", "silu"])
+def test_layer_golden_reference_composition(R, act):
+    """The GPU layer against the fixture composed from the reference's own engine/fp4.py and vLLM routing."""
+    d = np.load(os.path.join(G, "layer_golden.npz"))
+    p = act + "_"
+    T, H = d[p + "x"].shape
+    E, N2, _ = d[p + "w1_fp4"].shape
+    inter = N2 // 2
+    cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    x = cuda(d[p + "x"]).bfloat16()
+    w, ids = R.route(None, cuda(d[p + "logits"]), d[p + "topk_ids"].shape[1])
+    assert np.array_equal(ids.cpu().numpy(), d[p + "topk_ids"])
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    R.run_moe_nvfp4(out, x, cuda(d[p + "a1_gscale"]), cuda(d[p + "w1_fp4"]), cuda(d[p + "w1_sf"]),
+                    cuda(d[p + "w1_alphas"]), cuda(d[p + "a2_gscale"]), cuda(d[p + "w2_fp4"]), cuda(d[p + "w2_sf"]),
+                    cuda(d[p + "w2_alphas"]), w, ids, act)
+    _sync()
+    tol_check(out.float().cpu().numpy(), d[p + "out"])
+
+
+def test_layer_full_cfg2_sampled_tokens(R):
+    """BASELINE config 2 at full size (32 packed sequences, lengths U[256, 2048]): routing, counts and the slot map
+    bit-exact for every token; the output of 96 sampled tokens against the oracle run on those tokens alone
+    (a token's output depends only on its own row and routing)."""
+    lens = packed_lengths(32, 256, 2048, seed=0)
+    T = sum(lens)
+    c = make_case(T, 2816, 128, 8, 704, "gelu_tanh", seed=0)
+    w, ids = R.route(None, c["logits"], 8)
+    wr, idr = O.route(c["np"]["logits"], 8)
+    assert np.array_equal(ids.cpu().numpy(), idr)
+    st = R.Stages(T, 2816, 704, 128, 8, "gelu_tanh", "cuda")
+    st.plan(ids)
+    st.permute_quant(c["x"], c["a1_gscale"])
+    _sync()
+    pl = O.plan(idr, 128)
+    assert np.array_equal(st.expert_offsets.cpu().numpy(), pl["expert_offsets"])
+    assert np.array_equal(st.c_map.cpu().numpy(), pl["c_map"])
+    out = _run_layer(R, c, w, ids)
+    sel = np.sort(np.random.default_rng(0).choice(T, 96, replace=False))
+    sub = dict(c)
+    sub["np"] = dict(c["np"])
+    sub["np"]["x"] = c["np"]["x"][sel]
+    ref = _oracle_layer(sub, w.cpu().numpy()[sel], idr[sel])
+    tol_check(out.float().cpu().numpy()[sel], ref["out"])
+
+
+def test_layer_skewed_large_T_sampled(R):
+    """Skewed routing (Zipf bias), T = 131072: hottest expert far above the mean, some experts empty."""
+    T = 131072
+    c = make_case(T, 2816, 128, 8, 704, "gelu_tanh", seed=5, skew=2.0)
+    w, ids = R.route(None, c["logits"], 8)
+    counts = torch.bincount(ids.flatten().long(), minlength=128)
+    assert counts.max().item() > 4 * counts.float().mean().item()
+    out = _run_layer(R, c, w, ids)
+    sel = np.sort(np.random.default_rng(1).choice(T, 64, replace=False))
+    sub = dict(c)
+    sub["np"] = dict(c["np"])
+    sub["np"]["x"] = c["np"]["x"][sel]
+    ref = _oracle_layer(sub, w.cpu().numpy()[sel], ids.cpu().numpy()[sel])
+    tol_check(out.float().cpu().numpy()[sel], ref["out"])
+
+
+def test_layer_zero_tokens_is_noop(R):
+    c = make_case(4, 256, 8, 2, 256, "silu", seed=1)
+    out = torch.full((0, 256), 7.0, dtype=torch.bfloat16, device="cuda")
+    R.run_moe_nvfp4(out, c["x"][:0], c["a1_gscale"], c["w1q"], c["w1s"], c["w1_alphas"], c["a2_gscale"], c["w2q"],
+                    c["w2s"], c["w2_alphas"], torch.zeros(0, 2, device="cuda"),
+                    torch.zeros(0, 2, dtype=torch.int32, device="cuda"), "silu")
+    _sync()
+
+
+def test_layer_all_tokens_one_expert(R):
+    """Every token routed to experts {3, 5}: one huge group, all other experts empty."""
+    c = make_case(700, 256, 8, 2, 256, "gelu_tanh", seed=2)
+    ids = torch.tensor([[3, 5]] * 700, dtype=torch.int32, device="cuda")
+    w = torch.full((700, 2), 0.5, device="cuda")
+    out = _run_layer(R, c, w, ids)
+    ref = _oracle_layer(c, w.cpu().numpy(), ids.cpu().numpy())
+    tol_check(out.float().cpu().numpy(), ref["out"])
+
+
+def test_bad_expert_id_flagged_not_faulting(R):
+    """An out-of-range routed id is reported through the device status word; no out-of-bounds access."""
+    c = make_case(64, 256, 8, 2, 256, "silu", seed=3)
+    ids = torch.randint(0, 8, (64, 2), dtype=torch.int32, device="cuda")
+    ids[:, 1] = (ids[:, 0] + 1) % 8
+    ids[10, 1] = 9
+    st = R.Stages(64, 256, 256, 8, 2, "silu", "cuda")
+    st.plan(ids)
+    _sync()
+    assert st.status() == 8   # REAXMOE_ERR_BAD_EXPERT_ID
