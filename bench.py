@@ -284,35 +284,37 @@ def run_ours(args, wl: dict) -> None:
     value = world * T * args.steps / (ms / 1000.0)
 
     # ---- end to end through the public API, pinned host buffers in, output back
-    x_h = inp["x"].cpu().pin_memory()
-    lg_h = inp["logits"].cpu().pin_memory()
-    out_h = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    x_d = torch.empty_like(inp["x"])
-    lg_d = torch.empty_like(inp["logits"])
+    e2e_value = None
+    if not args.no_e2e:
+        x_h = inp["x"].cpu().pin_memory()
+        lg_h = inp["logits"].cpu().pin_memory()
+        out_h = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+        x_d = torch.empty_like(inp["x"])
+        lg_d = torch.empty_like(inp["logits"])
 
-    def e2e_step():
-        x_d.copy_(x_h, non_blocking=True)
-        lg_d.copy_(lg_h, non_blocking=True)
-        w, ids = R.route(None, lg_d, k)
-        R.run_moe_nvfp4(out, x_d, inp["a1_gscale"], inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"],
-                        inp["w2q"], inp["w2s"], inp["w2_alphas"], w, ids, wl["act"], w1_prepacked=True)
-        out_h.copy_(out, non_blocking=True)
+        def e2e_step():
+            x_d.copy_(x_h, non_blocking=True)
+            lg_d.copy_(lg_h, non_blocking=True)
+            w, ids = R.route(None, lg_d, k)
+            R.run_moe_nvfp4(out, x_d, inp["a1_gscale"], inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"],
+                            inp["w2q"], inp["w2s"], inp["w2_alphas"], w, ids, wl["act"], w1_prepacked=True)
+            out_h.copy_(out, non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    e0.record(s)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(s)
-    torch.cuda.synchronize(dev)
-    ems = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    if world > 1:
-        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-    e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        e0.record(s)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+        ems = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
 
     # ---- roofline of the dominant kernel and per-kernel figures
     peaks = load_peaks()
@@ -356,8 +358,9 @@ def run_ours(args, wl: dict) -> None:
                             l2="inputs larger than L2 (x %.0f MB, weights %.0f MB); no flush" % (
                                 T * H * 2 / 1e6, (inp["w1q"].numel() + inp["w1s"].numel() + inp["w2q"].numel() +
                                                   inp["w2s"].numel()) / 1e6)),
-                e2e=dict(value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * H * 2 + T * E * 4,
-                         d2h_bytes_per_step=T * H * 2),
+                e2e=None if e2e_value is None else dict(
+                    value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * H * 2 + T * E * 4,
+                    d2h_bytes_per_step=T * H * 2),
                 gpu_launches=launches_per_step * args.steps, roofline=roof, layer=layer, kernels=kernels,
                 cpu_baseline=cpu, clocks=clk.summary())
     if rank == 0:
@@ -376,9 +379,13 @@ def main():
     ap.add_argument("--workload", default=None)
     ap.add_argument("--cpu-tokens", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count (profiling)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     wl = workload(args.workload or ("cfg4" if world > 1 else "cfg2"))
+    if args.tokens is not None:
+        wl = dict(wl, T=args.tokens, name=wl["name"] + f" [tokens overridden to {args.tokens}]")
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

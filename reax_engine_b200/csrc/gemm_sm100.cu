@@ -312,11 +312,12 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
         for (int ks = 0; ks < k_stages; ++ks) {
           const int nk = min(KPS, k_chunks - ks * KPS);
+          // TMA data and tcgen05.mma operands both live in the async proxy: the completed full barrier is all
+          // the ordering the MMAs need (no tcgen05.fence here; it would stall the issue stream every stage).
           if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag, p.status, p.timeout_ns)) {
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint32_t a_s = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t b_s = a_s + A_BYTES;
           const uint32_t sfa_s = b_s + B_BYTES;

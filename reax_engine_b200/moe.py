@@ -16,6 +16,7 @@ from __future__ import annotations
 import ctypes
 import enum
 import threading
+import weakref
 
 import torch
 
@@ -125,13 +126,21 @@ def prepack_w13(w1_fp4: torch.Tensor, w1_blockscale: torch.Tensor, inter: int) -
 
 
 def _prepacked(w1_fp4, w1_blockscale, inter):
-    key = (w1_fp4.data_ptr(), w1_blockscale.data_ptr(), tuple(w1_fp4.shape), w1_fp4._version, w1_blockscale._version)
+    """Prepacked w13, cached per source tensor. An entry is valid only while the very same tensor objects are
+    alive and unmodified (weak references + version counters): a freed tensor whose address is reused by new
+    weights must never hit a stale entry."""
+    key = (w1_fp4.data_ptr(), w1_blockscale.data_ptr(), tuple(w1_fp4.shape))
     with _prepack_lock:
-        hit = _prepack_cache.get(key)
-        if hit is None:
-            hit = prepack_w13(w1_fp4, w1_blockscale, inter)
-            _prepack_cache[key] = hit
-    return hit
+        for k in [k for k, v in _prepack_cache.items() if v[0]() is None or v[1]() is None]:
+            del _prepack_cache[k]
+        ent = _prepack_cache.get(key)
+        if (ent is not None and ent[0]() is w1_fp4 and ent[1]() is w1_blockscale
+                and ent[2] == (w1_fp4._version, w1_blockscale._version)):
+            return ent[3]
+        res = prepack_w13(w1_fp4, w1_blockscale, inter)
+        _prepack_cache[key] = (weakref.ref(w1_fp4), weakref.ref(w1_blockscale),
+                               (w1_fp4._version, w1_blockscale._version), res)
+        return res
 
 
 # ---------------------------------------------------------------------------------------------------- workspace

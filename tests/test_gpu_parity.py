@@ -366,3 +366,17 @@ def test_bad_expert_id_flagged_not_faulting(R):
     st.plan(ids)
     _sync()
     assert st.status() == 8   # REAXMOE_ERR_BAD_EXPERT_ID
+
+
+def test_prepack_cache_not_fooled_by_address_reuse(R):
+    """New weights allocated at a freed tensor's address must not reuse its cached prepack."""
+    outs = []
+    for seed in (40, 41):
+        c = make_case(64, 256, 8, 2, 256, "silu", seed=seed)
+        w, ids = R.route(None, c["logits"], 2)
+        out = _run_layer(R, c, w, ids)
+        ref = _oracle_layer(c, w.cpu().numpy(), ids.cpu().numpy())
+        tol_check(out.float().cpu().numpy(), ref["out"])
+        outs.append(out)
+        del c
+        torch.cuda.empty_cache()
