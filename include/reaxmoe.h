@@ -145,6 +145,16 @@ int reaxmoe_quantize(const void* x, int32_t x_is_fp32, int64_t rows, int32_t col
 int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, int32_t inter, int32_t hidden,
                         void* w1p_fp4, void* w1p_sf, void* stream);
 
+/* The routing-data plan of reaxmoe_plan for callers that cannot allocate device memory (no counterpart in the
+ * reference). Same outputs as reaxmoe_plan (expert_offsets, blockscale_offsets and the optional problem sizes),
+ * but no caller workspace: its scratch is a file-scope static device array of about 1 MiB that every GPU loading
+ * this library holds until exit. Limit: tokens <= 65536 (REAXMOE_ERR_BAD_SHAPE beyond). The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) and should come before any stream capture. All calls
+ * share the array, so calls that overlap on the GPU (e.g. on two streams) race; routed ids outside [0, experts)
+ * are skipped as in reaxmoe_plan. Allocates nothing (no cudaMalloc / cudaFree). */
+int reaxmoe_plan_static(const reaxmoe_problem* p, const int32_t* topk_ids, int32_t* expert_offsets,
+                        int32_t* blockscale_offsets, int32_t* problem_sizes1, int32_t* problem_sizes2, void* stream);
+
 /* Synchronises `stream`, returns the device status word of the workspace (0 = ok, else REAXMOE_ERR_*) and
  * clears it when `clear` != 0. Not for the hot path. */
 int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream);

@@ -24,6 +24,8 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 static int cuda_check(const char* what) {
   const cudaError_t e = cudaPeekAtLastError();
   if (e != cudaSuccess) return fail(REAXMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
