@@ -145,6 +145,7 @@ def build_inputs(wl: dict, device, seed: int = 0):
                a2_gscale=torch.full((E,), 1.0 / a2_g, device=device),
                w1_alphas=(w1g * a1_g).float(), w2_alphas=(w2g * a2_g).float())
     inp["w1p"], inp["w1p_sf"] = R.prepack_w13(w1q, w1s, I)
+    inp["w2sx"] = R.expand_scales(w2s, H, I)
     torch.cuda.synchronize(device)
     return inp
 
@@ -244,7 +245,7 @@ def run_ours(args, wl: dict) -> None:
         if ev is not None: ev[2].record(s)
         st.gemm_w13(inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"])
         if ev is not None: ev[3].record(s)
-        st.gemm_w2(inp["w2q"], inp["w2s"], inp["w2_alphas"])
+        st.gemm_w2(inp["w2q"], inp["w2sx"], inp["w2_alphas"])
         if ev is not None: ev[4].record(s)
         st.combine(w, out)
         if ev is not None: ev[5].record(s)
@@ -297,7 +298,8 @@ def run_ours(args, wl: dict) -> None:
             lg_d.copy_(lg_h, non_blocking=True)
             w, ids = R.route(None, lg_d, k)
             R.run_moe_nvfp4(out, x_d, inp["a1_gscale"], inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"],
-                            inp["w2q"], inp["w2s"], inp["w2_alphas"], w, ids, wl["act"], w1_prepacked=True)
+                            inp["w2q"], inp["w2sx"], inp["w2_alphas"], w, ids, wl["act"], w1_prepacked=True,
+                            w2_prepacked=True)
             out_h.copy_(out, non_blocking=True)
 
         for _ in range(args.warmup):

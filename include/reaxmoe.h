@@ -62,8 +62,9 @@ enum {
 
 enum { REAXMOE_ACT_SILU = 0, REAXMOE_ACT_GELU_TANH = 1 };
 
-/* Layer shape. vLLM names in brackets. Preconditions: hidden [k] % 128 == 0 and >= 256; inter [n] % 64 == 0
- * and >= 256; 1 <= experts [e] <= 256; 1 <= topk <= min(16, experts); tokens [m] >= 0. */
+/* Layer shape. vLLM names in brackets. Preconditions: hidden [k] % 128 == 0 in [256, 3072]; inter [n] % 64 == 0
+ * in [256, 3072] (a GEMM m-tile's activation scales stay resident in tensor memory); 1 <= experts [e] <= 256;
+ * 1 <= topk <= min(16, experts); tokens [m] >= 0. */
 typedef struct reaxmoe_problem {
   int32_t tokens;
   int32_t hidden;
@@ -78,11 +79,11 @@ typedef struct reaxmoe_forward_args {
   const void* a;              /* [tokens, hidden] bf16 */
   const float* a1_gscale;     /* [experts] quant-side input scale of w13 */
   const void* w1_fp4;         /* [experts, 2*inter, hidden/2] u8, gate/up INTERLEAVED (reaxmoe_prepack_w13) */
-  const void* w1_sf;          /* [experts][2*inter/128][hidden/64][512] e4m3, interleaved like w1_fp4 */
+  const void* w1_sf;          /* scales of the interleaved w1_fp4, expanded by reaxmoe_expand_scales(n = 2*inter, k = hidden) */
   const float* w1_alphas;     /* [experts] */
   const float* a2_gscale;     /* [experts] quant-side scale of the intermediate */
   const void* w2_fp4;         /* [experts, hidden, inter/2] u8 */
-  const void* w2_sf;          /* [experts][hidden/128][inter/64][512] e4m3 */
+  const void* w2_sf;          /* scales of w2_fp4, expanded by reaxmoe_expand_scales(n = hidden, k = inter) */
   const float* w2_alphas;     /* [experts] */
   const float* topk_weights;  /* [tokens, topk] fp32 */
   const int32_t* topk_ids;    /* [tokens, topk] int32 */
@@ -117,12 +118,14 @@ int reaxmoe_permute_quant(const reaxmoe_problem* p, const void* a, const float* 
                           void* stream);
 
 /* Grouped NVFP4 GEMM w13 with the fused activation(gate) * up and NVFP4 re-quantisation epilogue
- * (blink_moegemm.cu:472-934 MODE 1). Needs the plan of the same workspace. */
+ * (blink_moegemm.cu:472-934 MODE 1). Needs the plan of the same workspace. w1_fp4 is interleaved
+ * (reaxmoe_prepack_w13) and w1_sf expanded (reaxmoe_expand_scales). hidden <= 3072. */
 int reaxmoe_gemm_w13(const reaxmoe_problem* p, const void* rep_fp4, const void* rep_sf, const void* w1_fp4,
                      const void* w1_sf, const float* w1_alphas, const float* a2_gscale, void* workspace,
                      size_t workspace_bytes, void* int_fp4, void* int_sf, void* stream);
 
-/* Grouped NVFP4 GEMM w2: c3[slot] = bf16(alpha_e * int[slot] . w2_e^T) (blink_moegemm.cu:1173-1197). */
+/* Grouped NVFP4 GEMM w2: c3[slot] = bf16(alpha_e * int[slot] . w2_e^T) (blink_moegemm.cu:1173-1197). w2_sf expanded
+ * (reaxmoe_expand_scales). inter <= 3072. */
 int reaxmoe_gemm_w2(const reaxmoe_problem* p, const void* int_fp4, const void* int_sf, const void* w2_fp4,
                     const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes, void* c3,
                     void* stream);
@@ -140,8 +143,9 @@ int reaxmoe_combine(const reaxmoe_problem* p, const void* c3, const int32_t* c_m
 int reaxmoe_quantize(const void* x, int32_t x_is_fp32, int64_t rows, int32_t cols, int32_t group_rows,
                      const float* gscale, void* packed, void* scales, void* stream);
 
-/* One-time re-layout of w13 for the fused gate/up epilogue: output row block b (128 rows) = gate rows
- * [64b, 64b+64) then up rows inter + [64b, 64b+64); scales move with their rows. In-place is NOT allowed. */
+/* One-time re-layout of w13 for the fused gate/up epilogue: output row block b (256 rows) = gate rows
+ * [128b, 128b+h) then up rows inter + [128b, 128b+h), h = min(128, inter - 128b) (the last block is narrower when
+ * inter % 128 != 0); scales move with their rows. In-place is NOT allowed. */
 int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, int32_t inter, int32_t hidden,
                         void* w1p_fp4, void* w1p_sf, void* stream);
 
@@ -154,6 +158,14 @@ int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, 
  * are skipped as in reaxmoe_plan. Allocates nothing (no cudaMalloc / cudaFree). */
 int reaxmoe_plan_static(const reaxmoe_problem* p, const int32_t* topk_ids, int32_t* expert_offsets,
                         int32_t* blockscale_offsets, int32_t* problem_sizes1, int32_t* problem_sizes2, void* stream);
+
+/* One-time expansion of weight block scales ([experts][n/128][k/64][512] atoms, engine/fp4.py layout per expert) into
+ * the grouped GEMMs' B-scale records: [experts][ceil(n/256)][k/64][4096 B]. Each record holds the scales of one 256-row
+ * n-tile and one 64-element k-chunk laid out for a single tcgen05.cp.128x256b (16 groups of 8 rows: block 0's 8 rows
+ * of 16 B then block 1's; row i of group g = row (8g+i) % 32 of the 512-byte atom); a 128-row last tile has zeros
+ * for block 1. Size: reaxmoe_expanded_scales_size(). */
+size_t reaxmoe_expanded_scales_size(int32_t experts, int32_t n, int32_t k);
+int reaxmoe_expand_scales(const void* sf, int32_t experts, int32_t n, int32_t k, void* out, void* stream);
 
 /* Synchronises `stream`, returns the device status word of the workspace (0 = ok, else REAXMOE_ERR_*) and
  * clears it when `clear` != 0. Not for the hot path. */

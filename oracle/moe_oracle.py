@@ -401,15 +401,17 @@ def quantize_weights(w: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]
     return fp4, np.stack(sfs), gs
 
 
-def interleave_w13(w1_fp4: np.ndarray, w1_sf: np.ndarray, inter: int, half_tile: int = 64):
-    """The w13 re-layout the fused gate/up epilogue reads: output row block b (2*half_tile rows) holds gate
-    rows [b*half_tile, (b+1)*half_tile) then the matching up rows inter + [b*half_tile, ...)."""
+def interleave_w13(w1_fp4: np.ndarray, w1_sf: np.ndarray, inter: int, half_tile: int = 128):
+    """The w13 re-layout the fused gate/up epilogue reads: output row block b holds the gate rows of intermediate
+    columns [b*half_tile, b*half_tile + h_b) then the matching up rows inter + [b*half_tile, ...), where
+    h_b = min(half_tile, inter - b*half_tile) (the last block is narrower when inter % half_tile != 0)."""
     E, N, K2 = w1_fp4.shape
-    assert N == 2 * inter and inter % half_tile == 0
+    assert N == 2 * inter and inter % 64 == 0
     src = np.empty(N, dtype=np.int64)
     for r in range(N):
         b, w = divmod(r, 2 * half_tile)
-        src[r] = b * half_tile + w if w < half_tile else inter + b * half_tile + (w - half_tile)
+        hb = min(half_tile, inter - b * half_tile)
+        src[r] = b * half_tile + w if w < hb else inter + b * half_tile + (w - hb)
     k16 = 2 * K2 // 16
     fp4 = w1_fp4[:, src]
     sf = np.empty_like(w1_sf)
@@ -417,3 +419,22 @@ def interleave_w13(w1_fp4: np.ndarray, w1_sf: np.ndarray, inter: int, half_tile:
         s8 = from_blocked(w1_sf[e], N, k16)
         sf[e] = to_blocked(s8[src])
     return fp4, sf
+
+
+def expand_b_scales(w_sf: np.ndarray, N: int, K: int) -> np.ndarray:
+    """The grouped GEMMs' B-scale records (test restatement of reaxmoe_expand_scales): w_sf [E, N/128 atoms-rows *
+    K/64 atoms * 512] -> [E, ceil(N/256), K/64, 4096]: per record 16 groups of 8 rows, block 0's rows then block 1's,
+    row i of group g = row (8g + i) % 32 of the 512-byte atom; zeros for a missing block 1."""
+    E = w_sf.shape[0]
+    kc = K // 64
+    nblk = N // 128
+    nt = -(-N // 256)
+    atoms = np.asarray(w_sf, dtype=np.uint8).reshape(E, nblk, kc, 32, 16)
+    out = np.zeros((E, nt, kc, 16, 2, 8, 16), dtype=np.uint8)
+    rows = (8 * np.arange(16)[:, None] + np.arange(8)[None, :]) % 32
+    for t in range(nt):
+        for h in range(2):
+            b = 2 * t + h
+            if b < nblk:
+                out[:, t, :, :, h] = atoms[:, b][:, :, rows]
+    return out.reshape(E, nt, kc, 4096)

@@ -5,8 +5,8 @@ Public API (mirrors the reference's operator interfaces; see ``moe.py``):
     ep (expert-parallel layer over torch.distributed / NCCL)
 """
 from ._lib import ReaxMoEError, lib  # noqa: F401
-from .moe import (MoEActivation, Stages, Workspace, prepack_w13, quantize_nvfp4, quantize_weights,  # noqa: F401
-                  read_status, route, run_moe_nvfp4, workspace_size)
+from .moe import (MoEActivation, Stages, Workspace, expand_scales, prepack_w13, quantize_nvfp4,  # noqa: F401
+                  quantize_weights, read_status, route, run_moe_nvfp4, workspace_size)
 
-__all__ = ["ReaxMoEError", "MoEActivation", "Stages", "Workspace", "prepack_w13", "quantize_nvfp4",
+__all__ = ["ReaxMoEError", "MoEActivation", "Stages", "Workspace", "expand_scales", "prepack_w13", "quantize_nvfp4",
            "quantize_weights", "read_status", "route", "run_moe_nvfp4", "workspace_size", "lib"]

@@ -47,10 +47,10 @@ static int check_problem(const reaxmoe_problem* p) {
     return fail(REAXMOE_ERR_TOO_MANY_EXPERTS, "experts=%d outside [1, %d]", p->experts, kMaxExperts);
   if (p->topk < 1 || p->topk > kMaxTopk || p->topk > p->experts)
     return fail(REAXMOE_ERR_TOO_MANY_EXPERTS, "topk=%d outside [1, min(%d, experts)]", p->topk, kMaxTopk);
-  if (p->hidden < 256 || p->hidden % 128 != 0)
-    return fail(REAXMOE_ERR_BAD_SHAPE, "hidden=%d must be a multiple of 128 and >= 256", p->hidden);
-  if (p->inter < 256 || p->inter % 64 != 0)
-    return fail(REAXMOE_ERR_BAD_SHAPE, "inter=%d must be a multiple of 64 and >= 256", p->inter);
+  if (p->hidden < 256 || p->hidden > 3072 || p->hidden % 128 != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "hidden=%d must be a multiple of 128 in [256, 3072]", p->hidden);
+  if (p->inter < 256 || p->inter > 3072 || p->inter % 64 != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "inter=%d must be a multiple of 64 in [256, 3072]", p->inter);
   if (p->tokens < 0) return fail(REAXMOE_ERR_BAD_SHAPE, "tokens=%d < 0", p->tokens);
   if ((int64_t)p->tokens * p->topk > (int64_t)1 << 30)
     return fail(REAXMOE_ERR_BAD_SHAPE, "tokens*topk=%lld too large", (long long)p->tokens * p->topk);
@@ -383,6 +383,21 @@ int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, 
   launch_prepack_w13(static_cast<const uint8_t*>(w1_fp4), static_cast<const uint8_t*>(w1_sf), experts, inter, hidden,
                      static_cast<uint8_t*>(w1p_fp4), static_cast<uint8_t*>(w1p_sf), static_cast<cudaStream_t>(stream));
   return cuda_check("prepack_w13");
+}
+
+size_t reaxmoe_expanded_scales_size(int32_t experts, int32_t n, int32_t k) {
+  if (experts < 1 || n < 128 || n % 128 != 0 || k < 64 || k % 64 != 0) return 0;
+  return (size_t)experts * ((n + 255) / 256) * (k / 64) * 4096;
+}
+
+int reaxmoe_expand_scales(const void* sf, int32_t experts, int32_t n, int32_t k, void* out, void* stream) {
+  if (reaxmoe_expanded_scales_size(experts, n, k) == 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "expand_scales: experts=%d n=%d k=%d (n %% 128, k %% 64)", experts, n, k);
+  if (!sf || !out) return fail(REAXMOE_ERR_NULL, "expand_scales: NULL pointer");
+  if (!aligned16(sf) || !aligned16(out)) return fail(REAXMOE_ERR_MISALIGNED, "expand_scales: misaligned");
+  launch_expand_scales(static_cast<const uint8_t*>(sf), experts, n, k, static_cast<uint8_t*>(out),
+                       static_cast<cudaStream_t>(stream));
+  return cuda_check("expand_scales");
 }
 
 int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream) {

@@ -50,8 +50,35 @@ __device__ __forceinline__ uint32_t e2m1_code(float q) {
   return idx | ((q < 0.0f) ? 8u : 0u);
 }
 
+// Division-free e2m1 decision thresholds for one block with scale sf. The reference rounds q = fl(x / sf) to fp32
+// and then compares q with the grid midpoints m (q > m for the midpoints that tie down, q >= m for those that tie
+// up). Because every midpoint has an even fp32 significand, fl(x / sf) > m  <=>  x / sf > m + ulp(m)/2 and
+// fl(x / sf) >= m  <=>  x / sf >= m - ulp-(m)/2 exactly. Each shifted midpoint c has at most 25 significant bits,
+// so c * sf (<= 49 bits) is exact in fp64. T[i] is then the float threshold such that, for any float a = |x|,
+// (a > T[i]) is exactly the i-th comparison: T = RD(c * sf) for the strict ones, the largest float below c * sf
+// for the non-strict ones.
+__device__ __forceinline__ void e2m1_thresholds(float sf, float (&T)[7]) {
+  const double c[7] = {0.25 + 0x1p-26, 0.75 - 0x1p-25, 1.25 + 0x1p-24, 1.75 - 0x1p-24,
+                       2.5 + 0x1p-23,  3.5 - 0x1p-23,  5.0 + 0x1p-22};
+  const double s = (double)sf;
+#pragma unroll
+  for (int i = 0; i < 7; ++i) {
+    const double P = c[i] * s;
+    float f = __double2float_rd(P);
+    if ((i & 1) && (double)f == P) f = __int_as_float(__float_as_int(f) - 1);  // P > 0 always
+    T[i] = f;
+  }
+}
+
+// e2m1 code of x / sf (sign = x < 0), identical to e2m1_code(__fdiv_rn(x, sf)) for the thresholds of sf.
+__device__ __forceinline__ uint32_t e2m1_code_t(float x, const float (&T)[7]) {
+  const float a = fabsf(x);
+  const uint32_t idx = (a > T[0]) + (a > T[1]) + (a > T[2]) + (a > T[3]) + (a > T[4]) + (a > T[5]) + (a > T[6]);
+  return idx | ((x < 0.0f) ? 8u : 0u);
+}
+
 // Quantise one 16-element block with dequant-side global scale g. Returns the e4m3 scale byte; writes the
-// 8 packed bytes (element 2i in the low nibble of byte i) into lo/hi words.
+// 8 packed bytes (element 2i in the low nibble of byte i) into lo/hi words. Numerics of engine/fp4.py:45-51.
 __device__ __forceinline__ uint32_t quant_block16(const float (&v)[16], float g, uint32_t& lo, uint32_t& hi) {
   float bamax = 0.0f;
 #pragma unroll
@@ -59,12 +86,11 @@ __device__ __forceinline__ uint32_t quant_block16(const float (&v)[16], float g,
   const float s = fminf(__fdiv_rn(bamax, __fmul_rn(6.0f, g)), 448.0f);
   const uint32_t s8 = e4m3_rn(s);
   const float sf = fmaxf(__fmul_rn(e4m3_to_f32(s8), g), 1e-30f);
+  float T[7];
+  e2m1_thresholds(sf, T);
   uint32_t w[2] = {0u, 0u};
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t c = e2m1_code(__fdiv_rn(v[i], sf));
-    w[i >> 3] |= c << ((i & 7) * 4);
-  }
+  for (int i = 0; i < 16; ++i) w[i >> 3] |= e2m1_code_t(v[i], T) << ((i & 7) * 4);
   lo = w[0];
   hi = w[1];
   return s8;

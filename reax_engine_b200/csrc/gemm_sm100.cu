@@ -8,14 +8,23 @@
 //   mode 1 (w13): gate/up = bf16(alpha_e * acc); h = bf16(bf16(act(gate)) * up); NVFP4 quant of h with the
 //                 expert's intermediate scale (engine/fp4.py numerics) -> FP4 rows + 128x4 scale atoms.
 //
-// Design (one CTA per SM, persistent over a static list of (expert, 128-row m-tile, 128-col n-tile) units):
-//   warp 0      TMA producer: A (routed FP4 rows) and B (expert weights) tiles by 2D TMA with 128-byte
-//               swizzle, the matching 512-byte scale atoms by 1D bulk copies, into a STAGES-deep smem ring.
-//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.cp (scale atoms smem -> TMEM,
-//               32x128b.warpx4) and tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (M=128, N=128, K=64 per
-//               instruction) into a double-buffered fp32 accumulator, and tcgen05.commit to free the stage.
-//   warps 2..9  epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane TMEM quarter and half of the
-//               columns), release it to the MMA warp at once, then convert / activate / quantise and store.
+// Design (one CTA per SM, persistent). Work is handed out per m-tile (expert, 128 routed rows); a CTA computes all
+// n-tiles of its m-tile in a row (256 output columns each; a narrower last n-tile of 128 when N % 256 == 128).
+//   warp 0      TMA producer: A (routed FP4 rows, 128 x 256 K) and B (expert weights, 256 x 256 K) tiles by 2D TMA
+//               with 128-byte swizzle plus the stage's B-scale records by one 1D bulk copy, into a 3-deep ring;
+//               once per m-tile, all its A scale atoms by a bulk copy.
+//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.mma.kind::mxf4nvf4.block_scale.block16
+//               (M=128, N=256, K=64: 512 clk of tensor work per stage, enough to hide the per-stage barrier
+//               round trip) into the fp32 accumulator, and tcgen05.commit.
+//   warp 2      one thread issues every tcgen05.cp: once per m-tile the A scales into a resident TMEM region
+//               (32x128b.warpx4 per 64-element chunk), and per k-step the B scales of the whole 256-row tile with a
+//               single 128x256b copy of the pre-expanded record (reaxmoe_expand_scales), into one of two buffers.
+//               Copies cost tensor-pipe time in proportion to the (4x replicated) TMEM bytes they write; issued from
+//               this thread they overlap the MMAs, and the MMA thread's barrier waits do not queue behind them.
+//   warps 3..10 epilogue: tcgen05.ld the whole accumulator into registers (each warp owns its 32-lane TMEM quarter
+//               and half of the columns) and release it to the MMA warp at once, then convert / activate /
+//               quantise and store while the next unit's MMAs run.
+// TMEM: accumulator [0, 256), two B-scale buffers of 32 columns, resident A scales (4 columns per k-chunk).
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records REAXMOE_ERR_DEVICE_TIMEOUT in the
 // status word, raises a CTA-wide abort flag, drains its own in-flight copies and MMAs, frees TMEM and returns.
 // No TMA multicast and no clusters: the same kernel runs on every rank of the expert-parallel path.
@@ -28,29 +37,39 @@ namespace reaxmoe {
 namespace gemm {
 
 constexpr int BM = 128;                 // rows per tile (MMA M)
-constexpr int BN = 128;                 // cols per tile (MMA N); mode 1: 64 gate + 64 up columns
+constexpr int BN = 256;                 // cols per tile (MMA N); mode 1: 128 gate + 128 up columns
 constexpr int KSTEP = 64;               // K per tcgen05.mma (FP4)
 constexpr int KSTAGE = 256;             // K per pipeline stage = one 128-byte swizzle row of FP4
-constexpr int KPS = KSTAGE / KSTEP;     // MMAs (and scale atoms) per stage
+constexpr int KPS = KSTAGE / KSTEP;     // MMAs per stage
 constexpr int A_BYTES = BM * KSTAGE / 2;
 constexpr int B_BYTES = BN * KSTAGE / 2;
-constexpr int SF_BYTES = KPS * 512;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 2 * SF_BYTES;
-constexpr int STAGES = 5;
+constexpr int SFB_REC = 4096;           // expanded B-scale record per k-chunk
+constexpr int SFB_BYTES = KPS * SFB_REC;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFB_BYTES;
+constexpr int STAGES = 3;
+constexpr int MAX_K_CHUNKS = 48;        // K <= 3072: the resident A scales fit in TMEM
+constexpr int SFA_SMEM_BYTES = MAX_K_CHUNKS * 512;
 constexpr int NUM_EPI_WARPS = 8;
-constexpr int THREADS = (2 + NUM_EPI_WARPS) * 32;
+constexpr int EPI_WARP0 = 3;
+constexpr int THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
 constexpr int TMEM_COLS = 512;
-constexpr int SFA_COL = 2 * BN;         // after the two accumulators
-constexpr int SFB_COL = SFA_COL + 4 * KPS;
+constexpr int SFB_COL = BN;             // two B-scale buffers of 8 * KPS columns
+constexpr int SFB_BUF_COLS = 8 * KPS;
+constexpr int SFA_COL = SFB_COL + 2 * SFB_BUF_COLS;
+constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 2 + 2;
 constexpr int SMEM_TABLE_INTS = 4 * (kMaxExperts + 1);
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + SMEM_TABLE_INTS * 4;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + SFA_SMEM_BYTES + 256 + SMEM_TABLE_INTS * 4;
 static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned for the 128B swizzle");
-static_assert(SFB_COL + 4 * KPS <= TMEM_COLS, "TMEM budget");
+static_assert(SFA_COL + 4 * MAX_K_CHUNKS <= TMEM_COLS, "TMEM budget");
+static_assert(NUM_BARS * 8 + 8 <= 256, "barrier area");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 // Instruction descriptor of tcgen05.mma.kind::mxf4nvf4 (block-scaled): A/B = e2m1 (MXF4 format 1) at bits
 // [7,10) / [10,13), K-major both, N >> 3 at [17,23), scale type ue4m3 (0) at bit 23, M >> 4 at [24,29),
 // scale-factor ids 0, dense K = 64.
-constexpr uint32_t IDESC = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_for(int n) {
+  return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
 
 struct Params {
   CUtensorMap tmA;  // [slots, K/2] u8, box 128 x 128 rows, 128B swizzle
@@ -69,6 +88,7 @@ struct Params {
   int* status;
   unsigned long long timeout_ns;
   int E, N, K, n_tiles, k_chunks;
+  int tail_n;           // width of the last n-tile (256, or 128 when N % 256 == 128)
 };
 
 // ---------------------------------------------------------------- PTX wrappers
@@ -151,6 +171,15 @@ __device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | (8ull << 32) | (1ull << 46);
 }
 
+// Expanded B-scale record for tcgen05.cp 128x256b: no swizzle, 8-row groups 256 bytes apart (SBO), the two 16-byte
+// halves of each row 128 bytes apart (LBO).
+__device__ __forceinline__ uint64_t desc_sfb_x(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) | (1ull << 46);
+}
+__device__ __forceinline__ void tc_cp_sfb_x(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 // Bounded wait. Returns false if the CTA aborted or the deadline passed (then records the timeout).
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
                                              unsigned long long timeout_ns) {
@@ -176,20 +205,20 @@ __device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity) {
   }
 }
 
-struct Unit {
-  int e, mt, nt, row0, rows, sfblk;
+struct MTile {
+  int e, mt, row0, rows, sfblk;
 };
 
-__device__ __forceinline__ Unit decode(int u, int n_tiles, int E, const int* s_tp, const int* s_cnt,
-                                       const int* s_eoff, const int* s_boff) {
-  const int gm = u / n_tiles;
-  Unit r;
-  r.nt = u - gm * n_tiles;
+// m-tile gm (global index over all experts' 128-row tiles) -> expert, tile inside the expert, first routed row,
+// valid rows and its scale-atom row block.
+__device__ __forceinline__ MTile decode_mtile(int gm, int E, const int* s_tp, const int* s_cnt, const int* s_eoff,
+                                              const int* s_boff) {
   int lo = 0, hi = E;  // largest e < E with s_tp[e] <= gm
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (s_tp[mid] <= gm) lo = mid; else hi = mid;
   }
+  MTile r;
   r.e = lo;
   r.mt = gm - s_tp[lo];
   r.row0 = s_eoff[lo] + r.mt * BM;
@@ -198,27 +227,71 @@ __device__ __forceinline__ Unit decode(int u, int n_tiles, int E, const int* s_t
   return r;
 }
 
+// tanh from its definition, tanh(y) = 1 - 2 / (1 + e^(2y)), with the hardware exp2 and reciprocal approximations
+// (relative error ~1e-7 away from 0, absolute ~1e-7 near 0); saturates correctly at +-1.
+__device__ __forceinline__ float tanh_fast(float y) {
+  const float e = exp2f(2.8853900817779268f * y);  // e^(2y)
+  return 1.0f - __fdividef(2.0f, 1.0f + e);
+}
+// GELU with the tanh approximation: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) (blink_moegemm.cu:349-355).
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float kBeta = 0.7978845608028654f, kKappa = 0.044715f;
-  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
-  const float inner = __fmul_rn(kBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+  const float inner = kBeta * fmaf(kKappa * x, x * x, x);
+  return 0.5f * x * (1.0f + tanh_fast(inner));
 }
-__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+template <int ACT>
+__device__ __forceinline__ float act_fn(float x) {
+  if constexpr (ACT == REAXMOE_ACT_GELU_TANH) return gelu_tanh(x);
+  else return silu(x);
+}
+
+// Fused w13 epilogue for one thread: 32 gate and 32 up accumulators of one row -> 16 packed FP4 bytes + 2 scale
+// bytes. gate/up = bf16(alpha * acc); h = bf16(bf16(act(gate)) * up) (a bf16 product of two bf16 values rounds
+// exactly like the fp32 product rounded to bf16); NVFP4 quantisation of h with engine/fp4.py numerics.
+template <int ACT>
+__device__ __forceinline__ uint32_t act_quant32(const uint32_t (&x0)[32], const uint32_t (&x1)[32], float alpha,
+                                                float g, uint32_t (&w)[4]) {
+  uint32_t sbytes = 0u;
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    float h[16];
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const __nv_bfloat162 gb = __floats2bfloat162_rn(alpha * __uint_as_float(x0[16 * b + i]),
+                                                      alpha * __uint_as_float(x0[16 * b + i + 1]));
+      const __nv_bfloat162 ub = __floats2bfloat162_rn(alpha * __uint_as_float(x1[16 * b + i]),
+                                                      alpha * __uint_as_float(x1[16 * b + i + 1]));
+      const float2 gf = __bfloat1622float2(gb);
+      const __nv_bfloat162 ab = __floats2bfloat162_rn(act_fn<ACT>(gf.x), act_fn<ACT>(gf.y));
+      const float2 hf = __bfloat1622float2(__hmul2(ab, ub));
+      h[i] = hf.x;
+      h[i + 1] = hf.y;
+    }
+    sbytes |= quant_block16(h, g, w[2 * b], w[2 * b + 1]) << (8 * b);
+  }
+  return sbytes;
+}
 
 template <int MODE, int ACT>
 __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* accf = bars + 2 * STAGES;
-  uint64_t* acce = accf + 2;
-  uint64_t* drain = acce + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint8_t* sfa_smem = smem + STAGES * STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sfa_smem + SFA_SMEM_BYTES);
+  uint64_t* full = bars;                 // [STAGES] A, B and the B-scale records landed (TMA tx)
+  uint64_t* empty = bars + STAGES;       // [STAGES] MMAs of the stage done: smem stage free
+  uint64_t* sff = empty + STAGES;        // [2] B-scale TMEM buffer b filled (commit of the copy thread)
+  uint64_t* accf = sff + 2;              // accumulator ready for the epilogue
+  uint64_t* acce = accf + 1;             // accumulator drained by the epilogue
+  uint64_t* sfa_full = acce + 1;         // A scales of the next m-tile landed in smem
+  uint64_t* sfa_ready = sfa_full + 1;    // A scales copied to TMEM (and the smem copy free again)
+  uint64_t* drain_mma = sfa_ready + 1;
+  uint64_t* drain_cp = drain_mma + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_cp + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  int* s_tp = reinterpret_cast<int*>(smem + STAGES * STAGE_BYTES + 256);
+  int* s_tp = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + 256);
   int* s_cnt = s_tp + (kMaxExperts + 1);
   int* s_eoff = s_cnt + (kMaxExperts + 1);
   int* s_boff = s_eoff + (kMaxExperts + 1);
@@ -239,11 +312,14 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&accf[b]), 1);
-      mbar_init(smem_u32(&acce[b]), NUM_EPI_WARPS);
-    }
-    mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(&sff[0]), 1);
+    mbar_init(smem_u32(&sff[1]), 1);
+    mbar_init(smem_u32(accf), 1);
+    mbar_init(smem_u32(acce), NUM_EPI_WARPS);
+    mbar_init(smem_u32(sfa_full), 1);
+    mbar_init(smem_u32(sfa_ready), 1);
+    mbar_init(smem_u32(drain_mma), 1);
+    mbar_init(smem_u32(drain_cp), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmA)) : "memory");
@@ -260,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   const int n_tiles = p.n_tiles;
-  const int total_units = s_tp[E] * n_tiles;
+  const int total_mtiles = s_tp[E];
   const int k_chunks = p.k_chunks;
   const int k_stages = (k_chunks + KPS - 1) / KPS;
 
@@ -270,145 +346,213 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
       int stage = 0;
       uint32_t phase = 0;
       long fills = 0;
+      int groups = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        const Unit U = decode(u, n_tiles, E, s_tp, s_cnt, s_eoff, s_boff);
-        const int brow = U.e * p.N + U.nt * BN;
-        const uint8_t* sfa = p.sfA + (size_t)U.sfblk * k_chunks * 512;
-        const uint8_t* sfb = p.sfB + ((size_t)U.e * (p.N / 128) + U.nt) * k_chunks * 512;
-        for (int ks = 0; ks < k_stages; ++ks) {
-          const int kc0 = ks * KPS;
-          const int nk = min(KPS, k_chunks - kc0);
-          if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
-            ok = false;
-            break;
+      for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x, ++groups) {
+        const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
+        // the A scales of the whole K of this m-tile, once; the smem copy is free once the copy thread's
+        // tcgen05.cp of the previous m-tile's scales completed
+        if (groups > 0 &&
+            !wait_bounded(smem_u32(sfa_ready), (uint32_t)((groups - 1) & 1), abort_flag, p.status, p.timeout_ns))
+          break;
+        mbar_expect_tx(smem_u32(sfa_full), (uint32_t)(k_chunks * 512));
+        bulk_load(smem_u32(sfa_smem), p.sfA + (size_t)M.sfblk * k_chunks * 512, (uint32_t)(k_chunks * 512),
+                  smem_u32(sfa_full));
+        for (int nt = 0; nt < n_tiles && ok; ++nt) {
+          const int brow = M.e * p.N + nt * BN;
+          const uint8_t* sfb = p.sfB + ((size_t)M.e * n_tiles + nt) * k_chunks * SFB_REC;
+          for (int ks = 0; ks < k_stages; ++ks) {
+            const int kc0 = ks * KPS;
+            const int nk = min(KPS, k_chunks - kc0);
+            if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            uint8_t* st = smem + stage * STAGE_BYTES;
+            const uint32_t bar = smem_u32(&full[stage]);
+            mbar_expect_tx(bar, (uint32_t)(A_BYTES + B_BYTES + nk * SFB_REC));
+            tma_load_2d(smem_u32(st), &p.tmA, bar, kc0 * (KSTEP / 2), M.row0);
+            tma_load_2d(smem_u32(st + A_BYTES), &p.tmB, bar, kc0 * (KSTEP / 2), brow);
+            bulk_load(smem_u32(st + A_BYTES + B_BYTES), sfb + (size_t)kc0 * SFB_REC, (uint32_t)(nk * SFB_REC), bar);
+            ++fills;
+            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
           }
-          uint8_t* st = smem + stage * STAGE_BYTES;
-          const uint32_t bar = smem_u32(&full[stage]);
-          mbar_expect_tx(bar, (uint32_t)(A_BYTES + B_BYTES + 2 * nk * 512));
-          tma_load_2d(smem_u32(st), &p.tmA, bar, kc0 * (KSTEP / 2), U.row0);
-          tma_load_2d(smem_u32(st + A_BYTES), &p.tmB, bar, kc0 * (KSTEP / 2), brow);
-          bulk_load(smem_u32(st + A_BYTES + B_BYTES), sfa + (size_t)kc0 * 512, (uint32_t)(nk * 512), bar);
-          bulk_load(smem_u32(st + A_BYTES + B_BYTES + SF_BYTES), sfb + (size_t)kc0 * 512, (uint32_t)(nk * 512), bar);
-          ++fills;
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
-      // let the last fills of every stage land before the CTA may exit (only matters after an abort)
+      // let the last fills land before the CTA may exit (only matters after an abort)
       for (long f = fills - 1; f >= 0 && f >= fills - STAGES; --f)
         wait_drain(smem_u32(&full[f % STAGES]), (uint32_t)((f / STAGES) & 1));
+      if (groups > 0) wait_drain(smem_u32(sfa_full), (uint32_t)((groups - 1) & 1));
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (one thread)
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
+      long n = 0;  // global stage counter of this CTA
       uint32_t acc_phase = 0;
+      int groups = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        if (!wait_bounded(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, p.status, p.timeout_ns)) break;
+      for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x, ++groups) {
+        if (!wait_bounded(smem_u32(sfa_ready), (uint32_t)(groups & 1), abort_flag, p.status, p.timeout_ns)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
-        for (int ks = 0; ks < k_stages; ++ks) {
-          const int nk = min(KPS, k_chunks - ks * KPS);
-          // TMA data and tcgen05.mma operands both live in the async proxy: the completed full barrier is all
-          // the ordering the MMAs need (no tcgen05.fence here; it would stall the issue stream every stage).
-          if (!wait_bounded(smem_u32(&full[stage]), phase, abort_flag, p.status, p.timeout_ns)) {
+        for (int nt = 0; nt < n_tiles && ok; ++nt) {
+          const uint32_t idesc = idesc_for(nt == n_tiles - 1 ? p.tail_n : BN);
+          if (!wait_bounded(smem_u32(acce), acc_phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
             ok = false;
             break;
           }
-          const uint32_t a_s = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t b_s = a_s + A_BYTES;
-          const uint32_t sfa_s = b_s + B_BYTES;
-          const uint32_t sfb_s = sfa_s + SF_BYTES;
-          for (int kk = 0; kk < nk; ++kk) {
-            tc_cp_sf(tmem + SFA_COL + 4 * kk, desc_sf(sfa_s + kk * 512));
-            tc_cp_sf(tmem + SFB_COL + 4 * kk, desc_sf(sfb_s + kk * 512));
-            tc_mma_fp4(d_tmem, desc_sw128(a_s + kk * (KSTEP / 2)), desc_sw128(b_s + kk * (KSTEP / 2)), IDESC,
-                       tmem + SFA_COL + 4 * kk, tmem + SFB_COL + 4 * kk, (ks | kk) != 0 ? 1u : 0u);
+          tc_fence_after();
+          for (int ks = 0; ks < k_stages; ++ks, ++n) {
+            const int stage = (int)(n % STAGES);
+            const int b = (int)(n & 1);
+            const int nk = min(KPS, k_chunks - ks * KPS);
+            // the B scales of this stage are in TMEM buffer b (the copy thread waited for the stage's TMA data
+            // before copying them, so the A/B tiles of the stage have landed as well)
+            if (!wait_bounded(smem_u32(&sff[b]), (uint32_t)((n >> 1) & 1), abort_flag, p.status, p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_s = smem_u32(smem + stage * STAGE_BYTES);
+            const uint32_t b_s = a_s + A_BYTES;
+            for (int kk = 0; kk < nk; ++kk) {
+              const int kc = ks * KPS + kk;
+              tc_mma_fp4(tmem, desc_sw128(a_s + kk * (KSTEP / 2)), desc_sw128(b_s + kk * (KSTEP / 2)), idesc,
+                         tmem + SFA_COL + 4 * kc, tmem + SFB_COL + SFB_BUF_COLS * b + 8 * kk,
+                         (ks | kk) != 0 ? 1u : 0u);
+            }
+            tc_commit(smem_u32(&empty[stage]));
           }
-          tc_commit(smem_u32(&empty[stage]));
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          if (!ok) break;
+          tc_commit(smem_u32(accf));
+          acc_phase ^= 1u;
         }
-        if (!ok) break;
-        tc_commit(smem_u32(&accf[acc]));
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
       }
       // all tcgen05 work of this thread has completed once this commit arrives
-      tc_commit(smem_u32(drain));
-      wait_drain(smem_u32(drain), 0);
+      tc_commit(smem_u32(drain_mma));
+      wait_drain(smem_u32(drain_mma), 0);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ scale-factor copies (one thread)
+    if (lane == 0) {
+      long n = 0;
+      int groups = 0;
+      bool ok = true;
+      for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x, ++groups) {
+        if (!wait_bounded(smem_u32(sfa_full), (uint32_t)(groups & 1), abort_flag, p.status, p.timeout_ns)) break;
+        // the previous m-tile's MMAs must be done reading the resident A scales before they are replaced
+        if (n > 0 && !wait_bounded(smem_u32(&empty[(n - 1) % STAGES]), (uint32_t)(((n - 1) / STAGES) & 1), abort_flag,
+                                   p.status, p.timeout_ns))
+          break;
+        tc_fence_after();
+        const uint32_t sfa_s = smem_u32(sfa_smem);
+        for (int kc = 0; kc < k_chunks; ++kc) tc_cp_sf(tmem + SFA_COL + 4 * kc, desc_sf(sfa_s + kc * 512));
+        tc_commit(smem_u32(sfa_ready));
+        for (int nt = 0; nt < n_tiles && ok; ++nt) {
+          for (int ks = 0; ks < k_stages; ++ks, ++n) {
+            const int stage = (int)(n % STAGES);
+            const int b = (int)(n & 1);
+            const int nk = min(KPS, k_chunks - ks * KPS);
+            if (!wait_bounded(smem_u32(&full[stage]), (uint32_t)((n / STAGES) & 1), abort_flag, p.status,
+                              p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            // B-scale buffer b was last read by the MMAs of stage n - 2
+            if (n >= 2 && !wait_bounded(smem_u32(&empty[(n - 2) % STAGES]), (uint32_t)(((n - 2) / STAGES) & 1),
+                                        abort_flag, p.status, p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sfb_s = smem_u32(smem + stage * STAGE_BYTES + A_BYTES + B_BYTES);
+            for (int kk = 0; kk < nk; ++kk)
+              tc_cp_sfb_x(tmem + SFB_COL + SFB_BUF_COLS * b + 8 * kk, desc_sfb_x(sfb_s + kk * SFB_REC));
+            tc_commit(smem_u32(&sff[b]));
+          }
+        }
+      }
+      tc_commit(smem_u32(drain_cp));
+      wait_drain(smem_u32(drain_cp), 0);
     }
   } else {
     // ------------------------------------------------------------------ epilogue warps
-    const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int sub = (warp - 2) >> 2;        // which half of the tile's columns
-    const int r = q * 32 + lane;            // row inside the tile
-    int acc = 0;
+    const int q = warp & 3;                       // TMEM lane quarter this warp may access
+    const int sub = (warp - EPI_WARP0) >> 2;      // which half of the tile's columns
+    const int r = q * 32 + lane;                  // row inside the tile
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-      const Unit U = decode(u, n_tiles, E, s_tp, s_cnt, s_eoff, s_boff);
-      if (!wait_bounded(smem_u32(&accf[acc]), acc_phase, abort_flag, p.status, p.timeout_ns)) break;
-      tc_fence_after();
-      const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      uint32_t x0[32], x1[32];
-      if constexpr (MODE == 0) {
-        tc_ld_32x32b_x32(t_base + sub * 64, x0);
-        tc_ld_32x32b_x32(t_base + sub * 64 + 32, x1);
-      } else {
-        tc_ld_32x32b_x32(t_base + sub * 32, x0);        // gate columns
-        tc_ld_32x32b_x32(t_base + 64 + sub * 32, x1);   // up columns
-      }
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
-      if (r >= U.rows) continue;
-      const float alpha = p.alphas[U.e];
-      const int64_t row = (int64_t)U.row0 + r;
-      if constexpr (MODE == 0) {
-        uint4* dst = reinterpret_cast<uint4*>(p.out + row * p.N + U.nt * BN + sub * 64);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint4 o;
-          o.x = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x0[8 * i + 0])), __fmul_rn(alpha, __uint_as_float(x0[8 * i + 1])));
-          o.y = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x0[8 * i + 2])), __fmul_rn(alpha, __uint_as_float(x0[8 * i + 3])));
-          o.z = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x0[8 * i + 4])), __fmul_rn(alpha, __uint_as_float(x0[8 * i + 5])));
-          o.w = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x0[8 * i + 6])), __fmul_rn(alpha, __uint_as_float(x0[8 * i + 7])));
-          dst[i] = o;
+    bool ok = true;
+    for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
+      const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
+      const int64_t row = (int64_t)M.row0 + r;
+      for (int nt = 0; nt < n_tiles; ++nt) {
+        const int un = (nt == n_tiles - 1) ? p.tail_n : BN;
+        if (!wait_bounded(smem_u32(accf), acc_phase, abort_flag, p.status, p.timeout_ns)) {
+          ok = false;
+          break;
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint4 o;
-          o.x = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x1[8 * i + 0])), __fmul_rn(alpha, __uint_as_float(x1[8 * i + 1])));
-          o.y = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x1[8 * i + 2])), __fmul_rn(alpha, __uint_as_float(x1[8 * i + 3])));
-          o.z = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x1[8 * i + 4])), __fmul_rn(alpha, __uint_as_float(x1[8 * i + 5])));
-          o.w = pack_bf16x2(__fmul_rn(alpha, __uint_as_float(x1[8 * i + 6])), __fmul_rn(alpha, __uint_as_float(x1[8 * i + 7])));
-          dst[4 + i] = o;
-        }
-      } else {
-        const float g = __fdiv_rn(1.0f, p.q_gscale[U.e]);
-        const int inter = p.N / 2;
-        uint32_t w[4];
-        uint32_t sbytes = 0u;
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          float h[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float gate = bf16r(__fmul_rn(alpha, __uint_as_float(x0[16 * b + i])));
-            const float up = bf16r(__fmul_rn(alpha, __uint_as_float(x1[16 * b + i])));
-            const float a = bf16r(ACT == REAXMOE_ACT_GELU_TANH ? gelu_tanh(gate) : silu(gate));
-            h[i] = bf16r(__fmul_rn(a, up));
+        acc_phase ^= 1u;
+        tc_fence_after();
+        const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16);
+        // full tiles: this warp's half = 128 output columns (mode 0) or 64 gate + 64 up columns (mode 1);
+        // the narrow last tile: 64 columns (mode 0) or 32 gate + 32 up (mode 1)
+        const int half = un / 2;
+        uint32_t x[4][32];
+        if constexpr (MODE == 0) {
+          tc_ld_32x32b_x32(t_base + sub * half, x[0]);
+          tc_ld_32x32b_x32(t_base + sub * half + 32, x[1]);
+          if (un == BN) {
+            tc_ld_32x32b_x32(t_base + sub * half + 64, x[2]);
+            tc_ld_32x32b_x32(t_base + sub * half + 96, x[3]);
           }
-          sbytes |= quant_block16(h, g, w[2 * b], w[2 * b + 1]) << (8 * b);
+        } else {
+          const int hw = un / 4;                  // h columns per warp half
+          tc_ld_32x32b_x32(t_base + sub * hw, x[0]);             // gate
+          tc_ld_32x32b_x32(t_base + half + sub * hw, x[1]);      // up
+          if (un == BN) {
+            tc_ld_32x32b_x32(t_base + sub * hw + 32, x[2]);
+            tc_ld_32x32b_x32(t_base + half + sub * hw + 32, x[3]);
+          }
         }
-        *reinterpret_cast<uint4*>(p.q_out + row * (inter / 2) + U.nt * 32 + sub * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        const int64_t sfrow = (int64_t)U.sfblk * 128 + r;
-        *reinterpret_cast<uint16_t*>(p.q_sf + sf_offset(sfrow, U.nt * 4 + sub * 2, inter / 64)) = (uint16_t)sbytes;
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(acce));
+        if (r >= M.rows) continue;
+        const float alpha = p.alphas[M.e];
+        if constexpr (MODE == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(p.out + row * p.N + nt * BN + sub * half);
+          const int nq = un == BN ? 4 : 2;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (j < nq) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                uint4 o;
+                o.x = pack_bf16x2(alpha * __uint_as_float(x[j][8 * i + 0]), alpha * __uint_as_float(x[j][8 * i + 1]));
+                o.y = pack_bf16x2(alpha * __uint_as_float(x[j][8 * i + 2]), alpha * __uint_as_float(x[j][8 * i + 3]));
+                o.z = pack_bf16x2(alpha * __uint_as_float(x[j][8 * i + 4]), alpha * __uint_as_float(x[j][8 * i + 5]));
+                o.w = pack_bf16x2(alpha * __uint_as_float(x[j][8 * i + 6]), alpha * __uint_as_float(x[j][8 * i + 7]));
+                dst[4 * j + i] = o;
+              }
+            }
+          }
+        } else {
+          const int inter = p.N / 2;
+          const float g = __fdiv_rn(1.0f, p.q_gscale[M.e]);
+          const int hw = un / 4;
+          const int c0 = nt * (BN / 2) + sub * hw;   // first intermediate column of this thread's slice
+          uint8_t* qrow = p.q_out + row * (inter / 2);
+          const int64_t sfrow = (int64_t)M.sfblk * 128 + r;
+          uint32_t w[4];
+          uint32_t sb = act_quant32<ACT>(x[0], x[1], alpha, g, w);
+          *reinterpret_cast<uint4*>(qrow + c0 / 2) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint16_t*>(p.q_sf + sf_offset(sfrow, c0 / 16, inter / 64)) = (uint16_t)sb;
+          if (un == BN) {
+            sb = act_quant32<ACT>(x[2], x[3], alpha, g, w);
+            *reinterpret_cast<uint4*>(qrow + c0 / 2 + 16) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint16_t*>(p.q_sf + sf_offset(sfrow, c0 / 16 + 2, inter / 64)) = (uint16_t)sb;
+          }
+        }
       }
     }
   }
@@ -439,12 +583,12 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-static int make_map(CUtensorMap* tm, const void* base, int64_t rows, int row_bytes) {
+static int make_map(CUtensorMap* tm, const void* base, int64_t rows, int row_bytes, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return REAXMOE_ERR_CUDA;
   const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-  const cuuint32_t box[2] = {128u, 128u};
+  const cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1u, 1u};
   const CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -468,9 +612,9 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   if (g.slots == 0) return 0;
   Params prm;
   memset(&prm, 0, sizeof(prm));
-  int rc = make_map(&prm.tmA, g.a, g.slots, g.K / 2);
+  int rc = make_map(&prm.tmA, g.a, g.slots, g.K / 2, BM);
   if (rc) return rc;
-  rc = make_map(&prm.tmB, g.b, (int64_t)g.E * g.N, g.K / 2);
+  rc = make_map(&prm.tmB, g.b, (int64_t)g.E * g.N, g.K / 2, BN);
   if (rc) return rc;
   prm.sfA = static_cast<const uint8_t*>(g.a_sf);
   prm.sfB = static_cast<const uint8_t*>(g.b_sf);
@@ -488,10 +632,13 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   prm.E = g.E;
   prm.N = g.N;
   prm.K = g.K;
-  prm.n_tiles = g.N / BN;
+  if (g.N % 128 != 0) return REAXMOE_ERR_BAD_SHAPE;
+  prm.n_tiles = (g.N + BN - 1) / BN;
+  prm.tail_n = g.N - (prm.n_tiles - 1) * BN;   // 256 or 128
   prm.k_chunks = g.K / KSTEP;
-  const int64_t max_units = (g.slots / BM + g.E + 1) * (int64_t)prm.n_tiles;
-  const int grid = (int)(max_units < num_sms ? max_units : num_sms);
+  if (prm.k_chunks > MAX_K_CHUNKS) return REAXMOE_ERR_BAD_SHAPE;  // resident A scales would not fit in TMEM
+  const int64_t max_mtiles = g.slots / BM + g.E + 1;
+  const int grid = (int)(max_mtiles < num_sms ? max_mtiles : num_sms);
   if (g.mode == 0) return launch_t<0, 0>(prm, grid, s);
   if (g.act == REAXMOE_ACT_GELU_TANH) return launch_t<1, REAXMOE_ACT_GELU_TANH>(prm, grid, s);
   return launch_t<1, REAXMOE_ACT_SILU>(prm, grid, s);

@@ -404,8 +404,10 @@ int launch_quantize(const void* x, bool f32, int64_t rows, int cols, int group_r
 }
 
 // ------------------------------------------------------------------------------------------------------
-// w13 prepack: output row r (block b = r / 128, w = r % 128) <- gate row 64b + w (w < 64) or up row
-// inter + 64b + (w - 64); its 16-element block scales move with it.
+// w13 prepack: output row block b (256 rows; the last one narrower when inter % 128 != 0) holds the gate rows of
+// intermediate columns [128b, 128b + h) then the matching up rows inter + [128b, 128b + h), h = min(128,
+// inter - 128b): output row r = 256b + w <- gate row 128b + w (w < h) or up row inter + 128b + (w - h). Its
+// 16-element block scales move with it.
 // ------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) prepack_w13_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ sf,
                                                           int inter, int H, uint8_t* __restrict__ wp,
@@ -413,8 +415,9 @@ __global__ void __launch_bounds__(128) prepack_w13_kernel(const uint8_t* __restr
   const int N = 2 * inter;
   const int e = blockIdx.y;
   const int r = blockIdx.x;
-  const int b = r >> 7, wi = r & 127;
-  const int src = wi < 64 ? b * 64 + wi : inter + b * 64 + (wi - 64);
+  const int b = r >> 8, wi = r & 255;
+  const int h = min(128, inter - 128 * b);
+  const int src = wi < h ? 128 * b + wi : inter + 128 * b + (wi - h);
   const int64_t row_bytes = H / 2;
   const uint4* s4 = reinterpret_cast<const uint4*>(w + ((int64_t)e * N + src) * row_bytes);
   uint4* d4 = reinterpret_cast<uint4*>(wp + ((int64_t)e * N + r) * row_bytes);
@@ -428,6 +431,35 @@ __global__ void __launch_bounds__(128) prepack_w13_kernel(const uint8_t* __restr
 int launch_prepack_w13(const uint8_t* w, const uint8_t* sf, int E, int inter, int H, uint8_t* wp, uint8_t* sfp,
                        cudaStream_t s) {
   prepack_w13_kernel<<<dim3(2 * inter, E), 128, 0, s>>>(w, sf, inter, H, wp, sfp);
+  return 0;
+}
+
+// ------------------------------------------------------------------------------------------------------
+// Weight-scale expansion for the grouped GEMMs (one-time, at weight load). For every expert e, 256-row n-tile nt
+// and 64-element k-chunk kc, a 4 KiB record holds the scales of both 128-row blocks of the tile in the layout one
+// tcgen05.cp.128x256b copies into TMEM as the B scales of one N=256 MMA: 16 groups of 8 rows; per group the
+// 8 x 16 B rows of block 0 then the 8 x 16 B rows of block 1, row i of group g being row (8g + i) % 32 of the
+// block's 512-byte 128x4 atom. A 128-row last tile has zeros for block 1.
+// ------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) expand_scales_kernel(const uint8_t* __restrict__ sf, int N, int k_chunks,
+                                                            int n_tiles, uint8_t* __restrict__ out) {
+  const int e = blockIdx.z, nt = blockIdx.y, kc = blockIdx.x;
+  const int64_t rec = ((int64_t)e * n_tiles + nt) * k_chunks + kc;
+  uint4* dst = reinterpret_cast<uint4*>(out + rec * 4096);
+  const int nblk = N / 128;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {   // 256 rows of 16 bytes
+    const int g = i >> 4, h = (i >> 3) & 1, r = i & 7;
+    const int row = (8 * g + r) & 31;
+    const int blk = 2 * nt + h;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (blk < nblk) v = *reinterpret_cast<const uint4*>(sf + (((int64_t)e * nblk + blk) * k_chunks + kc) * 512 + row * 16);
+    dst[i] = v;
+  }
+}
+
+int launch_expand_scales(const uint8_t* sf, int E, int N, int K, uint8_t* out, cudaStream_t s) {
+  const int k_chunks = K / 64, n_tiles = (N + 255) / 256;
+  expand_scales_kernel<<<dim3(k_chunks, n_tiles, E), 256, 0, s>>>(sf, N, k_chunks, n_tiles, out);
   return 0;
 }
 

@@ -111,9 +111,26 @@ _prepack_cache: dict = {}
 _prepack_lock = threading.Lock()
 
 
+def expand_scales(w_blockscale: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    """Weight block scales ([E, n, k/16] e4m3 in 128x4 atoms per expert) -> the grouped GEMMs' B-scale records
+    [E, ceil(n/256), k/64, 4096] uint8 (reaxmoe_expand_scales). One-time, at weight load."""
+    _require_cuda(w_blockscale)
+    E = w_blockscale.shape[0]
+    src = w_blockscale.view(torch.uint8).reshape(E, -1).contiguous()
+    assert src.shape[1] == n * k // 16, "scale tensor does not match n x k/16 per expert"
+    nbytes = L.lib().reaxmoe_expanded_scales_size(E, n, k)
+    if nbytes == 0:
+        raise L.ReaxMoEError(L.ERR_BAD_SHAPE, f"expand_scales: n={n} k={k}")
+    out = torch.empty(nbytes, dtype=torch.uint8, device=w_blockscale.device)
+    L.check(L.lib().reaxmoe_expand_scales(src.data_ptr(), E, n, k, out.data_ptr(), _stream(w_blockscale.device)))
+    return out.view(E, -1)
+
+
 def prepack_w13(w1_fp4: torch.Tensor, w1_blockscale: torch.Tensor, inter: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Re-lay w13 for the fused gate/up epilogue (row block b of 128 = gate rows [64b, 64b+64) then the matching up
-    rows). One-time, at weight load (the analogue of ``process_weights_after_loading``)."""
+    """Re-lay w13 for the fused gate/up epilogue (row block b of 256 = gate rows [128b, 128b+128) then the matching
+    up rows; a narrower last block when inter % 128 != 0) and expand its scales for the GEMM
+    (:func:`expand_scales`). One-time, at weight load (the analogue of ``process_weights_after_loading``).
+    Returns (interleaved fp4 [E, 2*inter, hidden/2], expanded scales)."""
     _require_cuda(w1_fp4, w1_blockscale)
     E, N, K2 = w1_fp4.shape
     assert N == 2 * inter
@@ -122,24 +139,23 @@ def prepack_w13(w1_fp4: torch.Tensor, w1_blockscale: torch.Tensor, inter: int) -
     sfp = torch.empty_like(src_sf)
     L.check(L.lib().reaxmoe_prepack_w13(w1_fp4.view(torch.uint8).contiguous().data_ptr(), src_sf.data_ptr(), E, inter,
                                         K2 * 2, w1p.data_ptr(), sfp.data_ptr(), _stream(w1_fp4.device)))
-    return w1p, sfp
+    return w1p, expand_scales(sfp, N, K2 * 2)
 
 
-def _prepacked(w1_fp4, w1_blockscale, inter):
-    """Prepacked w13, cached per source tensor. An entry is valid only while the very same tensor objects are
-    alive and unmodified (weak references + version counters): a freed tensor whose address is reused by new
-    weights must never hit a stale entry."""
-    key = (w1_fp4.data_ptr(), w1_blockscale.data_ptr(), tuple(w1_fp4.shape))
+def _cached(kind, tensors, fn):
+    """Per-source-tensor cache of one-time weight re-layouts. An entry is valid only while the very same tensor
+    objects are alive and unmodified (weak references + version counters): a freed tensor whose address is reused
+    by new weights must never hit a stale entry."""
+    key = (kind,) + tuple((t.data_ptr(), tuple(t.shape)) for t in tensors)
+    vers = tuple(t._version for t in tensors)
     with _prepack_lock:
-        for k in [k for k, v in _prepack_cache.items() if v[0]() is None or v[1]() is None]:
+        for k in [k for k, v in _prepack_cache.items() if any(r() is None for r in v[0])]:
             del _prepack_cache[k]
         ent = _prepack_cache.get(key)
-        if (ent is not None and ent[0]() is w1_fp4 and ent[1]() is w1_blockscale
-                and ent[2] == (w1_fp4._version, w1_blockscale._version)):
-            return ent[3]
-        res = prepack_w13(w1_fp4, w1_blockscale, inter)
-        _prepack_cache[key] = (weakref.ref(w1_fp4), weakref.ref(w1_blockscale),
-                               (w1_fp4._version, w1_blockscale._version), res)
+        if ent is not None and all(r() is t for r, t in zip(ent[0], tensors)) and ent[1] == vers:
+            return ent[2]
+        res = fn()
+        _prepack_cache[key] = (tuple(weakref.ref(t) for t in tensors), vers, res)
         return res
 
 
@@ -178,14 +194,16 @@ def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor
                   topk_weights: torch.Tensor, topk_ids: torch.Tensor, activation, workspace13=None, workspace2=None,
                   m: int | None = None, n: int | None = None, k: int | None = None, e: int | None = None,
                   device=None, apply_router_weight_on_input: bool = False, *, w1_prepacked: bool = False,
-                  workspace: torch.Tensor | None = None) -> None:
+                  w2_prepacked: bool = False, workspace: torch.Tensor | None = None) -> None:
     """NVFP4 MoE experts, result written into ``output`` [m, k] (vLLM ``run_cutlass_moe_fp4`` contract).
 
     a [m, k] bf16; a1_gscale / a2_gscale [e] fp32 quant-side scales; w1_fp4 [e, 2n, k/2] uint8 (gate rows then up
     rows, or the interleaved layout when ``w1_prepacked``); w1_blockscale [e, 2n, k/16] e4m3 in 128x4 atoms per
     expert; w2_fp4 [e, k, n/2]; w2_blockscale [e, k, n/16]; w*_alphas [e]; topk_weights / topk_ids [m, topk].
     ``workspace13`` / ``workspace2`` are accepted for signature compatibility; the library's workspace comes from
-    ``workspace`` (uint8, >= :func:`workspace_size` bytes) or a cached per-device buffer.
+    ``workspace`` (uint8, >= :func:`workspace_size` bytes) or a cached per-device buffer. Weights are re-laid for the
+    GEMMs once per weight tensor and cached (:func:`prepack_w13`, :func:`expand_scales`); pass already prepacked
+    tensors with ``w1_prepacked`` / ``w2_prepacked``.
     """
     act = MoEActivation.parse(activation)
     _require_cuda(output, a, a1_gscale, w1_fp4, w1_blockscale, w1_alphas, a2_gscale, w2_fp4, w2_blockscale,
@@ -217,8 +235,11 @@ def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor
     if w1_prepacked:
         w1p, w1p_sf = w1_fp4.contiguous(), w1_blockscale.view(torch.uint8).reshape(e, -1).contiguous()
     else:
-        w1p, w1p_sf = _prepacked(w1_fp4, w1_blockscale, n)
-    w2_sf = w2_blockscale.view(torch.uint8).reshape(e, -1).contiguous()
+        w1p, w1p_sf = _cached("w13", (w1_fp4, w1_blockscale), lambda: prepack_w13(w1_fp4, w1_blockscale, n))
+    if w2_prepacked:
+        w2_sf = w2_blockscale.view(torch.uint8).reshape(e, -1).contiguous()
+    else:
+        w2_sf = _cached("w2", (w2_blockscale,), lambda: expand_scales(w2_blockscale, k, n))
     ids = topk_ids.to(torch.int32).contiguous()
     tw = topk_weights.float().contiguous()
     a1 = a1_gscale.float().reshape(-1).contiguous()

@@ -43,7 +43,8 @@ def test_workspace_size_matches_layout():
     assert expect_min <= n <= expect_min + 64 * 1024 + 2 * ((m + 127) // 128) * E * 4 + 4096
 
 
-@pytest.mark.parametrize("bad", [dict(hidden=200), dict(hidden=128), dict(inter=100), dict(experts=300),
+@pytest.mark.parametrize("bad", [dict(hidden=200), dict(hidden=128), dict(hidden=3200), dict(inter=100),
+                                 dict(inter=3136), dict(experts=300),
                                  dict(topk=17), dict(topk=9, experts=8), dict(tokens=-1), dict(activation=7)])
 def test_bad_shapes_rejected(bad):
     p = dict(tokens=16, hidden=2816, inter=704, experts=128, topk=8, activation=1)
