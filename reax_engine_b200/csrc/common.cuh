@@ -111,6 +111,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return l | (h << 16);
 }
 
+// 256-bit global store of 8 words (one full 32-byte sector per lane; sm_100 vector width).
+__device__ __forceinline__ void st_global_v8(void* ptr, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(ptr), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 // Device status word: first error wins.
 __device__ __forceinline__ void set_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);

@@ -520,19 +520,20 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         if (r >= M.rows) continue;
         const float alpha = p.alphas[M.e];
         if constexpr (MODE == 0) {
-          uint4* dst = reinterpret_cast<uint4*>(p.out + row * p.N + nt * BN + sub * half);
+          // 32 columns per x[j] -> 64 bytes of bf16 -> two full 32-byte sectors per 256-bit store
+          uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + row * p.N + nt * BN + sub * half);
           const int nq = un == BN ? 4 : 2;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             if (j < nq) {
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                uint4 o;
-                o.x = pack_bf16x2(alpha * __uint_as_float(x[j][8 * i + 0]), alpha * __uint_as_float(x[j][8 * i + 1]));
-                o.y = pack_bf16x2(alpha * __uint_as_float(x[j][8 * i + 2]), alpha * __uint_as_float(x[j][8 * i + 3]));
-                o.z = pack_bf16x2(alpha * __uint_as_float(x[j][8 * i + 4]), alpha * __uint_as_float(x[j][8 * i + 5]));
-                o.w = pack_bf16x2(alpha * __uint_as_float(x[j][8 * i + 6]), alpha * __uint_as_float(x[j][8 * i + 7]));
-                dst[4 * j + i] = o;
+              for (int h = 0; h < 2; ++h) {
+                uint32_t o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  o[i] = pack_bf16x2(alpha * __uint_as_float(x[j][16 * h + 2 * i]),
+                                     alpha * __uint_as_float(x[j][16 * h + 2 * i + 1]));
+                st_global_v8(dst + 64 * j + 32 * h, o);
               }
             }
           }

@@ -251,17 +251,32 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
     }
   }
   __syncthreads();
-  const int groups = H / 64;
+  // phase B: each lane owns 32-element units (two scale blocks: 16 FP4 bytes + 2 scale bytes per slot); all of a
+  // lane's loads for a token are issued before any arithmetic
+  const int units = H / 32;
   const int k64 = H / 64;
   const int nwarps = blockDim.x >> 5;
+  constexpr int kMaxUnits = 4;  // per lane per token: H <= 32 * 32 * kMaxUnits
   for (int tl = warp; tl < nt; tl += nwarps) {
     const int64_t t = t0 + tl;
     const uint4* src = reinterpret_cast<const uint4*>(a + t * H);
-    for (int grp = lane; grp < groups; grp += 32) {
-      float v[64];
+    uint4 raw[kMaxUnits][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) bf16x8_to_f32(__ldg(src + grp * 8 + i), v + 8 * i);
-      uint32_t w[8];
+    for (int it = 0; it < kMaxUnits; ++it) {
+      const int un = lane + 32 * it;
+      if (un < units) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) raw[it][i] = __ldg(src + un * 4 + i);
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < kMaxUnits; ++it) {
+      const int un = lane + 32 * it;
+      if (un >= units) continue;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) bf16x8_to_f32(raw[it][i], v + 8 * i);
+      uint32_t w[4];
       uint32_t sbytes = 0u;
       uint32_t gbits = 0xFFFFFFFFu;  // a NaN pattern: never equal to a real scale
       for (int j = 0; j < k; ++j) {
@@ -272,20 +287,17 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
           gbits = __float_as_uint(g);
           sbytes = 0u;
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
+          for (int b = 0; b < 2; ++b) {
             float blk[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) blk[i] = v[b * 16 + i];
-            const uint32_t s8 = quant_block16(blk, g, w[2 * b], w[2 * b + 1]);
-            sbytes |= s8 << (8 * b);
+            sbytes |= quant_block16(blk, g, w[2 * b], w[2 * b + 1]) << (8 * b);
           }
         }
         const int pos = pos_s[tl * k + j];
-        uint4* dst = reinterpret_cast<uint4*>(rep_fp4 + (int64_t)pos * (H / 2) + grp * 32);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        *reinterpret_cast<uint4*>(rep_fp4 + (int64_t)pos * (H / 2) + un * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         const int64_t sfrow = (int64_t)boff[e] + (pos - eoff[e]);
-        *reinterpret_cast<uint32_t*>(rep_sf + sf_offset(sfrow, grp * 4, k64)) = sbytes;
+        *reinterpret_cast<uint16_t*>(rep_sf + sf_offset(sfrow, un * 2, k64)) = (uint16_t)sbytes;
       }
     }
   }
@@ -295,7 +307,73 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
 // K7 combine: one warp per token, 8 columns (one 16-byte load per slot row) per lane step.
 // out = bf16( sum_j bf16( c3[c_map[t,j]] * bf16(w[t,j]) ) ), partial sums j % 4 in increasing j, then
 // ((s0 + s1) + s2) + s3 (blink_moe.py:168-198 ORDER 1 for top-8; cutlass_moe.py:650-662).
+// The compile-time-k variant issues all k row loads of two lane steps before any arithmetic, so 2k 16-byte
+// loads per lane are in flight; other k use the runtime-k loop.
 // ------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void combine_accumulate(const uint4& v, float wb, int j, float (&part)[4][8]) {
+  float f[8];
+  bf16x8_to_f32(v, f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float p = bf16r(__fmul_rn(f[i], wb));
+    part[j & 3][i] = (j < 4) ? p : __fadd_rn(part[j & 3][i], p);
+  }
+}
+__device__ __forceinline__ uint4 combine_finish(float (&part)[4][8], int k) {
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    acc[i] = part[0][i];
+    if (k > 1) acc[i] = __fadd_rn(acc[i], part[1][i]);
+    if (k > 2) acc[i] = __fadd_rn(acc[i], part[2][i]);
+    if (k > 3) acc[i] = __fadd_rn(acc[i], part[3][i]);
+  }
+  uint4 o;
+  o.x = pack_bf16x2(acc[0], acc[1]);
+  o.y = pack_bf16x2(acc[2], acc[3]);
+  o.z = pack_bf16x2(acc[4], acc[5]);
+  o.w = pack_bf16x2(acc[6], acc[7]);
+  return o;
+}
+
+template <int K>
+__global__ void __launch_bounds__(256, 3) combine_kernel_k(const __nv_bfloat16* __restrict__ c3,
+                                                           const int* __restrict__ c_map,
+                                                           const float* __restrict__ topk_w, int m, int H,
+                                                           __nv_bfloat16* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nch = H / 8;
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < m; t += warps) {
+    int mypos = 0;
+    float myw = 0.0f;
+    if (lane < K) {
+      mypos = c_map[t * K + lane];
+      myw = bf16r(topk_w[t * K + lane]);
+    }
+    const uint4* rowp[K];
+    float wb[K];
+    bool valid[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const int pj = __shfl_sync(0xffffffffu, mypos, j);
+      wb[j] = __shfl_sync(0xffffffffu, myw, j);
+      valid[j] = pj >= 0;  // -1 marks a pair whose expert id was out of range (flagged by the plan)
+      rowp[j] = reinterpret_cast<const uint4*>(c3 + (int64_t)(valid[j] ? pj : 0) * H);
+    }
+    uint4* orow = reinterpret_cast<uint4*>(out + t * H);
+    for (int ch = lane; ch < nch; ch += 32) {
+      uint4 v[K];
+#pragma unroll
+      for (int j = 0; j < K; ++j) v[j] = valid[j] ? __ldg(rowp[j] + ch) : make_uint4(0u, 0u, 0u, 0u);
+      float part[4][8];
+#pragma unroll
+      for (int j = 0; j < K; ++j) combine_accumulate(v[j], wb[j], j, part);
+      orow[ch] = combine_finish(part, K);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ c3,
                                                       const int* __restrict__ c_map,
                                                       const float* __restrict__ topk_w, int m, int H, int k,
@@ -321,30 +399,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 #pragma unroll
       for (int j = 0; j < kMaxTopk; ++j) {
         if (j < k) {
-          float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          if (pos[j] >= 0)  // -1 marks a pair whose expert id was out of range (flagged by the plan)
-            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(c3 + (int64_t)pos[j] * H) + ch), f);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float p = bf16r(__fmul_rn(f[i], wb[j]));
-            part[j & 3][i] = (j < 4) ? p : __fadd_rn(part[j & 3][i], p);
-          }
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (pos[j] >= 0) v = __ldg(reinterpret_cast<const uint4*>(c3 + (int64_t)pos[j] * H) + ch);
+          combine_accumulate(v, wb[j], j, part);
         }
       }
-      float acc[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        acc[i] = part[0][i];
-        if (k > 1) acc[i] = __fadd_rn(acc[i], part[1][i]);
-        if (k > 2) acc[i] = __fadd_rn(acc[i], part[2][i]);
-        if (k > 3) acc[i] = __fadd_rn(acc[i], part[3][i]);
-      }
-      uint4 o;
-      o.x = pack_bf16x2(acc[0], acc[1]);
-      o.y = pack_bf16x2(acc[2], acc[3]);
-      o.z = pack_bf16x2(acc[4], acc[5]);
-      o.w = pack_bf16x2(acc[6], acc[7]);
-      reinterpret_cast<uint4*>(out + t * H)[ch] = o;
+      reinterpret_cast<uint4*>(out + t * H)[ch] = combine_finish(part, k);
     }
   }
 }
@@ -489,9 +549,13 @@ int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const i
 int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
                    __nv_bfloat16* out, int num_sms, cudaStream_t s) {
   if (m == 0) return 0;
-  const int64_t want = ceil_div64(m, 8), cap = (int64_t)num_sms * 8;
+  const int64_t want = ceil_div64(m, 8), cap = (int64_t)num_sms * 12;
   const int64_t blocks = want < cap ? want : cap;
-  combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, k, out);
+  if (k == 8) combine_kernel_k<8><<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
+  else if (k == 4) combine_kernel_k<4><<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
+  else if (k == 2) combine_kernel_k<2><<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
+  else if (k == 1) combine_kernel_k<1><<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
+  else combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, k, out);
   return 0;
 }
 
