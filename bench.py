@@ -127,6 +127,7 @@ def build_inputs(wl: dict, device, seed: int = 0):
     T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
     g = torch.Generator(device=device).manual_seed(seed)
     x = torch.randn(T, H, generator=g, device=device).bfloat16()
+    gate = None
     if wl["skew"] is None:
         gate = torch.randn(E, H, generator=g, device=device) * 0.02
         logits = x.float() @ gate.t()
@@ -140,10 +141,10 @@ def build_inputs(wl: dict, device, seed: int = 0):
     del w2
     a1_g = float(x.float().abs().max()) / 2688.0
     a2_g = 8.0 / 2688.0
-    inp = dict(x=x, logits=logits, w1q=w1q, w1s=w1s, w2q=w2q, w2s=w2s,
+    inp = dict(x=x, logits=logits, gate=gate, w1q=w1q, w1s=w1s, w2q=w2q, w2s=w2s,
                a1_gscale=torch.full((E,), 1.0 / a1_g, device=device),
                a2_gscale=torch.full((E,), 1.0 / a2_g, device=device),
-               w1_alphas=(w1g * a1_g).float(), w2_alphas=(w2g * a2_g).float())
+               w1_alphas=(w1g * a1_g).float(), w2_alphas=(w2g * a2_g).float(), w1g=w1g, a2_g=a2_g)
     inp["w1p"], inp["w1p_sf"] = R.prepack_w13(w1q, w1s, I)
     inp["w2sx"] = R.expand_scales(w2s, H, I)
     torch.cuda.synchronize(device)
@@ -160,8 +161,8 @@ def cpu_sample(wl: dict, inp_cpu: dict, n_tokens: int, reps: int = 1):
     # untimed: dequantise the touched experts' weights once (model-load work for a CPU engine)
     w, ids = O.route(logits, wl["k"])
     for e in np.unique(ids):
-        wcache[(id(inp_cpu["w1q"]), int(e))] = O.expert_weights(inp_cpu["w1q"], inp_cpu["w1s"], int(e))
-        wcache[(id(inp_cpu["w2q"]), int(e))] = O.expert_weights(inp_cpu["w2q"], inp_cpu["w2s"], int(e))
+        wcache[O.weight_cache_key(inp_cpu["w1q"], e)] = O.expert_weights(inp_cpu["w1q"], inp_cpu["w1s"], int(e))
+        wcache[O.weight_cache_key(inp_cpu["w2q"], e)] = O.expert_weights(inp_cpu["w2q"], inp_cpu["w2s"], int(e))
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
@@ -356,7 +357,7 @@ def run_ours(args, wl: dict) -> None:
                 ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
                 data="synthetic",
                 config=dict(workload=wl["name"], tokens=T, hidden=H, experts=E, topk=k, inter=I,
-                            activation=wl["act"], parallelism="replicas" if world > 1 else "single",
+                            activation=wl["act"], parallelism="single",
                             l2="inputs larger than L2 (x %.0f MB, weights %.0f MB); no flush" % (
                                 T * H * 2 / 1e6, (inp["w1q"].numel() + inp["w1s"].numel() + inp["w2q"].numel() +
                                                   inp["w2s"].numel()) / 1e6)),
@@ -370,6 +371,160 @@ def run_ours(args, wl: dict) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_ours_ep(args, wl: dict) -> None:
+    """N > 1: the expert-parallel layer (reax_engine_b200.ep) on every rank, NCCL all-to-alls between them. Rank r
+    owns experts [r E/R, (r+1) E/R); every rank routes its own batch of wl["T"] tokens (seed = rank) through one
+    shared router gate."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import reax_engine_b200 as R
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
+    El = E // world
+    inp = build_inputs(dict(wl, T=256), dev, seed=0)          # shared weights, gate and static input scale
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(T, H, generator=g, device=dev).bfloat16()
+    logits = x.float() @ inp["gate"].t()
+    amax = x.float().abs().max().reshape(1)
+    dist.all_reduce(amax, op=dist.ReduceOp.MAX)          # one static input scale for all ranks
+    a1_g = float(amax.item()) / 2688.0
+    inp["a1_gscale"] = torch.full((E,), 1.0 / a1_g, device=dev)
+    inp["w1_alphas"] = (inp["w1g"] * a1_g).float()
+    sl = slice(rank * El, (rank + 1) * El)
+    w1p, w1p_sf = R.prepack_w13(inp["w1q"][sl].contiguous(), inp["w1s"][sl].contiguous(), I)
+    local_w = R.ep.LocalExperts(w1p, w1p_sf, inp["w1_alphas"][sl].contiguous(), inp["a2_gscale"][sl].contiguous(),
+                                inp["w2q"][sl].contiguous(), R.expand_scales(inp["w2s"][sl].contiguous(), H, I),
+                                inp["w2_alphas"][sl].contiguous())
+    weight_bytes = sum(t.numel() for t in (inp["w1q"], inp["w1s"], inp["w2q"], inp["w2s"])) // world
+    for key in ("w1q", "w1s", "w2q", "w2s", "w1p", "w1p_sf", "w2sx"):
+        inp.pop(key)
+    torch.cuda.empty_cache()
+    layer = R.ep.ExpertParallelMoE(H, I, E, k, wl["act"], inp["a1_gscale"], local_w)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    s = torch.cuda.current_stream(dev)
+
+    def step():
+        w, ids = R.route(None, logits, k)
+        layer(x, w, ids, out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if layer.ops.status() != 0:
+        raise SystemExit(f"rank {rank}: device status {layer.ops.status()} after warm-up")
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    phases: dict[str, list[float]] = {}
+    counts = []
+    with ClockSampler(dev.index) as clk:
+        start.record(s)
+        for _ in range(args.steps):
+            layer.marks = []
+            step()
+            marks = layer.marks
+            layer.marks = None
+            counts.append(layer.last_counts)
+            for (_, a), (n, b) in zip(marks[:-1], marks[1:]):
+                phases.setdefault(n, []).append((a, b))
+        stop.record(s)
+        torch.cuda.synchronize(dev)
+    dist.barrier()
+    ms_local = start.elapsed_time(stop)
+    t_max = torch.tensor([ms_local], device=dev)
+    dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms = float(t_max.item())
+    ms_step = ms / args.steps
+    value = world * T * args.steps / (ms / 1000.0)
+    phase_ms = {n: statistics.mean(a.elapsed_time(b) for a, b in v) for n, v in phases.items()}
+
+    # bytes that cross NVLink per step on this rank (records to / rows from the other ranks), per direction
+    rec = R.ep.record_bytes(H, k)
+    send, recv = counts[-1]
+    out_bytes = sum(c for r, c in enumerate(send) if r != rank) * rec + \
+        sum(c for r, c in enumerate(recv) if r != rank) * H * 2
+    in_bytes = sum(c for r, c in enumerate(recv) if r != rank) * rec + \
+        sum(c for r, c in enumerate(send) if r != rank) * H * 2
+    nvl = torch.tensor([float(max(out_bytes, in_bytes))], device=dev)
+    dist.all_reduce(nvl, op=dist.ReduceOp.MAX)
+    peaks = load_peaks()
+    fp4_peak = 4.0 * peaks["bf16"]
+    nvlink_gbs = 770.0                     # measured peer copy per direction on this pool's B200s
+    slots_local = T * k                    # pairs this rank's tokens route (processed somewhere)
+    flop_rank = 6.0 * slots_local * H * I
+    t_tensor = flop_rank / (fp4_peak * 1e12)
+    t_nvl = float(nvl.item()) / (nvlink_gbs * 1e9)
+    ex_ms = phase_ms.get("exchange_records", 0.0) + phase_ms.get("exchange_rows", 0.0)
+    roof = dict(kernel="ep_step", bound="nvlink" if t_nvl > t_tensor else "tensor",
+                achieved=(float(nvl.item()) / (ex_ms / 1000.0) / 1e9) if t_nvl > t_tensor and ex_ms > 0
+                else flop_rank / (ms_step / 1000.0) / 1e12,
+                peak=nvlink_gbs if t_nvl > t_tensor else fp4_peak,
+                unit="GB/s" if t_nvl > t_tensor else "TFLOP/s", traffic=None,
+                target_ms=1000.0 * max(t_nvl, t_tensor), step_frac_of_target=1000.0 * max(t_nvl, t_tensor) / ms_step,
+                peak_basis="measured NVLink peer copy 770 GB/s per direction per GPU" if t_nvl > t_tensor else
+                "4 x measured cuBLAS bf16 dense")
+    roof["frac"] = roof["achieved"] / roof["peak"]
+
+    # ---- end to end: pinned host tokens + logits in, output back, every step
+    e2e_value = None
+    if not args.no_e2e:
+        x_h = x.cpu().pin_memory()
+        lg_h = logits.cpu().pin_memory()
+        out_h = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+        x_d = torch.empty_like(x)
+        lg_d = torch.empty_like(logits)
+
+        def e2e_step():
+            x_d.copy_(x_h, non_blocking=True)
+            lg_d.copy_(lg_h, non_blocking=True)
+            w, ids = R.route(None, lg_d, k)
+            layer(x_d, w, ids, out)
+            out_h.copy_(out, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+        ems = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
+
+    launches_per_step = 13   # route; dispatch 4; expert forward 7 (unpack, count, plan, permute, w13, w2, combine); combine
+    line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
+                ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
+                data="synthetic",
+                config=dict(workload=wl["name"], tokens_per_rank=T, hidden=H, experts=E, topk=k, inter=I,
+                            activation=wl["act"], parallelism=f"ep{world}", experts_per_rank=El,
+                            l2="inputs larger than L2 (x %.0f MB per rank, local weights %.0f MB); no flush" % (
+                                T * H * 2 / 1e6, weight_bytes / 1e6)),
+                e2e=None if e2e_value is None else dict(
+                    value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * H * 2 + T * E * 4,
+                    d2h_bytes_per_step=T * H * 2),
+                gpu_launches=launches_per_step * args.steps, roofline=roof,
+                phases_ms={n: v for n, v in phase_ms.items()},
+                exchange=dict(records_sent=send, records_received=recv, record_bytes=rec,
+                              nvlink_bytes_per_direction=float(nvl.item())),
+                cpu_baseline=None, clocks=clk.summary())
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def main():
@@ -392,6 +547,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args, wl)
+    elif world > 1:
+        run_ours_ep(args, wl)
     else:
         run_ours(args, wl)
 

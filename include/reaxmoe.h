@@ -56,7 +56,7 @@ enum {
   REAXMOE_ERR_WORKSPACE = 5,       /* workspace NULL or smaller than reaxmoe_workspace_size() */
   REAXMOE_ERR_CUDA = 6,            /* a CUDA runtime / driver call failed */
   REAXMOE_ERR_NULL = 7,            /* a required pointer is NULL */
-  REAXMOE_ERR_BAD_EXPERT_ID = 8,   /* a routed expert id outside [0, experts) (device-detected) */
+  REAXMOE_ERR_BAD_EXPERT_ID = 8,   /* a routed expert id >= experts (device-detected; negative ids mark unused slots) */
   REAXMOE_ERR_UNSUPPORTED = 9      /* e.g. no sm_100 device */
 };
 
@@ -86,7 +86,7 @@ typedef struct reaxmoe_forward_args {
   const void* w2_sf;          /* scales of w2_fp4, expanded by reaxmoe_expand_scales(n = hidden, k = inter) */
   const float* w2_alphas;     /* [experts] */
   const float* topk_weights;  /* [tokens, topk] fp32 */
-  const int32_t* topk_ids;    /* [tokens, topk] int32 */
+  const int32_t* topk_ids;    /* [tokens, topk] int32; a negative id marks an unused slot (contributes nothing) */
   void* output;               /* [tokens, hidden] bf16, written (not accumulated) */
 } reaxmoe_forward_args;
 
@@ -166,6 +166,44 @@ int reaxmoe_plan_static(const reaxmoe_problem* p, const int32_t* topk_ids, int32
  * for block 1. Size: reaxmoe_expanded_scales_size(). */
 size_t reaxmoe_expanded_scales_size(int32_t experts, int32_t n, int32_t k);
 int reaxmoe_expand_scales(const void* sf, int32_t experts, int32_t n, int32_t k, void* out, void* stream);
+
+/* ---- Expert parallelism (no counterpart in the reference, which requires ep_size == 1 at
+ * champions/uid240/opt/blink/blink_par.py:99). The three calls below are the device halves of vLLM's
+ * FusedMoEPrepareAndFinalize.prepare / finalize (vllm/model_executor/layers/fused_moe/modular_kernel.py:263-378;
+ * naive form prepare_finalize/naive_dp_ep.py:112-209) around the grouped GEMMs; the caller moves the records with
+ * two all-to-alls (NCCL). Rank r of `ranks` owns experts [r * El, (r + 1) * El), El = experts / ranks.
+ *
+ * Record (reaxmoe_ep_record_bytes(hidden, topk) bytes, a multiple of 16), one per (token, rank owning >= 1 of its
+ * experts): [0, H/2) NVFP4 codes; [H/2, H/2 + H/16) e4m3 block scales, linear; then int32 local expert ids [topk]
+ * (-1 for experts on other ranks) and fp32 router weights [topk]; zero or more padding bytes. */
+size_t reaxmoe_ep_record_bytes(int32_t hidden, int32_t topk);
+
+/* Dispatch: p describes this rank's tokens with the GLOBAL expert count. Writes send_counts [ranks] (records per
+ * destination rank), the records grouped by destination rank in rank order and token order inside a rank
+ * (send_records: capacity tokens * min(ranks, topk) records), and send_map [tokens, topk]: the record index of the
+ * first pair j of a token on each destination rank, -1 elsewhere. The row is quantised with the destination's input
+ * scale; a1_gscale [experts] must be constant over each rank's experts (device status REAXMOE_ERR_UNSUPPORTED
+ * otherwise). 1 <= ranks <= 64, experts % ranks == 0. */
+size_t reaxmoe_ep_dispatch_workspace_size(const reaxmoe_problem* p, int32_t ranks);
+int reaxmoe_ep_dispatch(const reaxmoe_problem* p, int32_t ranks, const void* a, const float* a1_gscale,
+                        const int32_t* topk_ids, const float* topk_weights, void* workspace, size_t workspace_bytes,
+                        int32_t* send_counts, int32_t* send_map, void* send_records, void* stream);
+
+/* Receiver: `local` has tokens = received records, experts = El (topk may exceed El). Runs plan, permute, the two
+ * grouped GEMMs on this rank's expert weights (the same formats as reaxmoe_forward_args; alphas and a2_gscale are
+ * the local [El] slices) and writes partial [tokens, hidden] bf16: per record, the combine of its local pairs
+ * (the single-GPU combine order with the other ranks' pairs left out). */
+size_t reaxmoe_ep_expert_workspace_size(const reaxmoe_problem* local);
+int reaxmoe_ep_expert_forward(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
+                              const void* w1_sf, const float* w1_alphas, const float* a2_gscale, const void* w2_fp4,
+                              const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes,
+                              void* partial, void* stream);
+
+/* Source-side combine: output[t] = bf16( sum over j = 0..topk-1 with send_map[t, j] >= 0 of
+ * float(returned[send_map[t, j]]) ), summed in fp32 from +0 in increasing j. returned [sum(send_counts), hidden]
+ * bf16 holds the partial rows in send-record order (the reverse all-to-all of reaxmoe_ep_expert_forward's output). */
+int reaxmoe_ep_combine(int32_t tokens, int32_t hidden, int32_t topk, const int32_t* send_map, const void* returned,
+                       void* output, void* stream);
 
 /* Synchronises `stream`, returns the device status word of the workspace (0 = ok, else REAXMOE_ERR_*) and
  * clears it when `clear` != 0. Not for the hot path. */

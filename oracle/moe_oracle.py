@@ -214,15 +214,17 @@ def plan(ids: np.ndarray, num_experts: int) -> dict:
     ids = np.asarray(ids, dtype=np.int64)
     T, k = ids.shape
     flat = ids.reshape(-1)
-    counts = np.bincount(flat, minlength=num_experts).astype(np.int32)
+    valid = (flat >= 0) & (flat < num_experts)              # negative ids mark unused pairs: no slot
+    counts = np.bincount(flat[valid], minlength=num_experts).astype(np.int32)
     eoff = np.zeros(num_experts + 1, dtype=np.int32)
     eoff[1:] = np.cumsum(counts)
     rounded = (counts + 127) // 128 * 128
     boff = np.zeros(num_experts + 1, dtype=np.int32)
     boff[1:] = np.cumsum(rounded)
-    order = np.argsort(flat, kind="stable")                 # by expert, then by t*k + j
-    c_map = np.empty(T * k, dtype=np.int32)
-    c_map[order] = np.arange(T * k, dtype=np.int32)
+    key = np.where(valid, flat, num_experts)
+    order = np.argsort(key, kind="stable")[:int(valid.sum())]  # by expert, then by t*k + j
+    c_map = np.full(T * k, -1, dtype=np.int32)
+    c_map[order] = np.arange(order.shape[0], dtype=np.int32)
     a_map = (order // k).astype(np.int32)
     slot_expert = np.repeat(np.arange(num_experts), counts).astype(np.int32)
     return dict(counts=counts, expert_offsets=eoff, blockscale_offsets=boff, c_map=c_map, a_map=a_map,
@@ -294,6 +296,12 @@ def expert_weights(w_fp4: np.ndarray, w_sf: np.ndarray, e: int) -> np.ndarray:
     return dequant(w_fp4[e], s8)
 
 
+def weight_cache_key(w_fp4: np.ndarray, e: int):
+    """Key of expert e's dequantised weights in a grouped_gemm weight cache: the array's data address and shape, so
+    that slices of one array (e.g. per-rank expert ranges) get distinct keys."""
+    return (w_fp4.__array_interface__["data"][0], w_fp4.shape, int(e))
+
+
 def grouped_gemm(a_fp4: np.ndarray, a_sf: np.ndarray, w_fp4: np.ndarray, w_sf: np.ndarray, alphas: np.ndarray,
                  pl: dict, wcache: dict | None = None) -> np.ndarray:
     """out[slots of e] = bf16(alpha_e * (dequant(A_e) @ dequant(W_e)^T)) with fp32 accumulation
@@ -311,7 +319,7 @@ def grouped_gemm(a_fp4: np.ndarray, a_sf: np.ndarray, w_fp4: np.ndarray, w_sf: n
         s8 = from_blocked(a_sf, m, K // 16, int(boff[e]))
         a = dequant(a_fp4[r0:r0 + m], s8)
         if wcache is not None:
-            key = (id(w_fp4), e)
+            key = weight_cache_key(w_fp4, e)
             if key not in wcache:
                 wcache[key] = expert_weights(w_fp4, w_sf, e)
             w = wcache[key]
@@ -345,11 +353,13 @@ def combine_order(k: int) -> list[list[int]]:
 
 def combine(c3: np.ndarray, c_map: np.ndarray, topk_weights: np.ndarray) -> np.ndarray:
     """out[t] = bf16( sum_j fp32( bf16( c3[c_map[t, j]] * bf16(w[t, j]) ) ) ) in combine_order
-    (``blink_moe.py:161-198``; stock ``cutlass_moe.py:650-662``)."""
+    (``blink_moe.py:161-198``; stock ``cutlass_moe.py:650-662``). A pair without a slot (c_map -1) adds +0."""
     T, k = topk_weights.shape
     wb = bf16_round(np.asarray(topk_weights, dtype=np.float32))
     cm = np.asarray(c_map).reshape(T, k)
-    prods = [bf16_round(c3[cm[:, j]] * wb[:, j:j + 1]) for j in range(k)]
+    prods = [np.where(cm[:, j:j + 1] >= 0, bf16_round(c3[np.maximum(cm[:, j], 0)] * wb[:, j:j + 1]),
+                      np.float32(0.0)).astype(np.float32) if c3.shape[0] else
+             np.zeros((T, c3.shape[1]), np.float32) for j in range(k)]
     parts = []
     for lanes in combine_order(k):
         s = prods[lanes[0]].copy()
@@ -438,3 +448,137 @@ def expand_b_scales(w_sf: np.ndarray, N: int, K: int) -> np.ndarray:
             if b < nblk:
                 out[:, t, :, :, h] = atoms[:, b][:, :, rows]
     return out.reshape(E, nt, kc, 4096)
+
+
+# ----------------------------------------------------------------------------------------------------------
+# Expert parallelism (no counterpart in the reference, which requires ep_size == 1 at
+# ``champions/uid240/opt/blink/blink_par.py:99``). Restates the record exchange of the library's EP path: each
+# token is quantised once per destination rank (vLLM's quantise-then-dispatch, ``fused_moe/prepare_finalize/
+# naive_dp_ep.py:16-52``), the receiver runs the layer on its local pairs and pre-sums them per record, the source
+# adds the returned rows of a token in fp32 and rounds once.
+# ----------------------------------------------------------------------------------------------------------
+
+def ep_record_bytes(hidden: int, topk: int) -> int:
+    """Bytes of one dispatch record: FP4 row, linear e4m3 scales, int32 local ids [k], fp32 weights [k], padded to
+    a multiple of 16."""
+    return (hidden // 2 + hidden // 16 + 8 * topk + 15) // 16 * 16
+
+
+def ep_rank_ids(ids: np.ndarray, experts: int, ranks: int) -> np.ndarray:
+    """Owner rank of each pair for the first pair of a token on that rank, -1 for later pairs on the same rank and
+    for negative ids."""
+    El = experts // ranks
+    ids = np.asarray(ids, dtype=np.int64)
+    owner = np.where(ids >= 0, ids // El, -1)
+    rid = owner.copy()
+    for j in range(ids.shape[1]):
+        for q in range(j):
+            rid[:, j][(owner[:, q] == owner[:, j]) & (owner[:, j] >= 0)] = -1
+    return rid
+
+
+def ep_dispatch(x: np.ndarray, ids: np.ndarray, topk_weights: np.ndarray, a1_gscale: np.ndarray, experts: int,
+                ranks: int) -> dict:
+    """send_counts [R]; send_map [T, k] (record index of the first pair of a token on each rank, else -1); records
+    [S, rec] uint8 grouped by destination rank, token-major inside a rank (padding bytes zero). Each record's row is
+    quantised with the destination rank's input scale (a1_gscale of its first expert)."""
+    x = np.asarray(x, dtype=np.float32)
+    ids = np.asarray(ids, dtype=np.int64)
+    T, k = ids.shape
+    H = x.shape[1]
+    El = experts // ranks
+    rid = ep_rank_ids(ids, experts, ranks)
+    flat = rid.reshape(-1)
+    valid = flat >= 0
+    counts = np.bincount(flat[valid], minlength=ranks).astype(np.int32)
+    order = np.argsort(np.where(valid, flat, ranks), kind="stable")[:int(valid.sum())]
+    send_map = np.full(T * k, -1, dtype=np.int32)
+    send_map[order] = np.arange(order.shape[0], dtype=np.int32)
+    tok = order // k
+    dest = flat[order]
+    rec = ep_record_bytes(H, k)
+    S = order.shape[0]
+    records = np.zeros((S, rec), dtype=np.uint8)
+    if S:
+        g = inv_scale(np.asarray(a1_gscale, dtype=np.float32)[dest * El])
+        packed, s8 = quantize_rows(x[tok], g)
+        owner = np.where(ids[tok] >= 0, ids[tok] // El, -1)
+        lid = np.where(owner == dest[:, None], ids[tok] - dest[:, None] * El, -1).astype(np.int32)
+        lw = np.asarray(topk_weights, dtype=np.float32)[tok]
+        M = H // 2 + H // 16
+        records[:, :H // 2] = packed
+        records[:, H // 2:M] = s8
+        records[:, M:M + 4 * k] = lid.view(np.uint8).reshape(S, 4 * k)
+        records[:, M + 4 * k:M + 8 * k] = lw.view(np.uint8).reshape(S, 4 * k)
+    return dict(send_counts=counts, send_map=send_map.reshape(T, k), records=records)
+
+
+def ep_unpack(records: np.ndarray, hidden: int, topk: int):
+    """(packed [n, H/2], scale bytes [n, H/16], local ids [n, k] int32, weights [n, k] fp32) of received records."""
+    n = records.shape[0]
+    M = hidden // 2 + hidden // 16
+    packed = records[:, :hidden // 2]
+    s8 = records[:, hidden // 2:M]
+    lid = np.ascontiguousarray(records[:, M:M + 4 * topk]).view(np.int32).reshape(n, topk)
+    lw = np.ascontiguousarray(records[:, M + 4 * topk:M + 8 * topk]).view(np.float32).reshape(n, topk)
+    return packed, s8, lid, lw
+
+
+def ep_expert_forward(records: np.ndarray, hidden: int, topk: int, w1_fp4, w1_sf, w1_alphas, w2_fp4, w2_sf,
+                      w2_alphas, a2_gscale, activation: str = "gelu_tanh", wcache: dict | None = None) -> np.ndarray:
+    """Receiver side: the layer over the received records' local pairs (this rank's El experts), then per record the
+    combine of its local pairs (combine with the other ranks' pairs adding +0). Returns partial [n, H]."""
+    packed, s8, lid, lw = ep_unpack(records, hidden, topk)
+    El = w1_fp4.shape[0]
+    inter = w2_fp4.shape[2] * 2
+    pl = plan(lid, El)
+    rep_fp4 = packed[pl["a_map"]]
+    nrows = int(pl["blockscale_offsets"][El])
+    rep_sf = np.zeros(nrows // 128 * (-(-(hidden // 16) // 4)) * 512, dtype=np.uint8)
+    if pl["a_map"].shape[0]:
+        r, c = np.meshgrid(sf_rows(pl), np.arange(hidden // 16), indexing="ij")
+        rep_sf[swizzle_offset(r, c, hidden // 16)] = s8[pl["a_map"]]
+    c1 = grouped_gemm(rep_fp4, rep_sf, w1_fp4, w1_sf, w1_alphas, pl, wcache)
+    int_fp4, int_sf, _ = act_quant(c1, a2_gscale, activation, pl, inter)
+    c3 = grouped_gemm(int_fp4, int_sf, w2_fp4, w2_sf, w2_alphas, pl, wcache)
+    return combine(c3, pl["c_map"], lw)
+
+
+def ep_combine(send_map: np.ndarray, returned: np.ndarray) -> np.ndarray:
+    """out[t] = bf16( sum over j with send_map[t, j] >= 0, in increasing j, of returned[send_map[t, j]] ), the fp32
+    sum started from +0."""
+    T, k = send_map.shape
+    acc = np.zeros((T, returned.shape[1] if returned.ndim == 2 else 0), dtype=np.float32)
+    for j in range(k):
+        m = send_map[:, j]
+        sel = m >= 0
+        acc[sel] = (acc[sel] + returned[m[sel]]).astype(np.float32)
+    return bf16_round(acc)
+
+
+def ep_forward(xs, ids_list, weights_list, w1_fp4, w1_sf, w1_alphas, w2_fp4, w2_sf, w2_alphas, a1_gscale,
+               a2_gscale, ranks: int, activation: str = "gelu_tanh", wcache: dict | None = None) -> list:
+    """The expert-parallel layer over `ranks` ranks, the exchanges done in memory: xs[r], ids_list[r],
+    weights_list[r] are rank r's tokens; weights are global [E, ...] arrays (rank r owns experts [r El, (r+1) El)).
+    Returns the output of every rank."""
+    E = w1_fp4.shape[0]
+    El = E // ranks
+    H = np.asarray(xs[0]).shape[1]
+    k = np.asarray(ids_list[0]).shape[1]
+    disp = [ep_dispatch(xs[r], ids_list[r], weights_list[r], a1_gscale, E, ranks) for r in range(ranks)]
+    offs = [np.concatenate([[0], np.cumsum(d["send_counts"])]) for d in disp]
+    partial = []
+    for r in range(ranks):
+        recv = np.concatenate([disp[s]["records"][offs[s][r]:offs[s][r + 1]] for s in range(ranks)], axis=0)
+        sl = slice(r * El, (r + 1) * El)
+        partial.append(ep_expert_forward(recv, H, k, w1_fp4[sl], w1_sf[sl], w1_alphas[sl], w2_fp4[sl], w2_sf[sl],
+                                         w2_alphas[sl], np.asarray(a2_gscale)[sl], activation, wcache))
+    outs = []
+    for s in range(ranks):
+        pieces = []
+        for r in range(ranks):
+            recv_before = sum(int(disp[q]["send_counts"][r]) for q in range(s))
+            pieces.append(partial[r][recv_before:recv_before + int(disp[s]["send_counts"][r])])
+        returned = np.concatenate(pieces, axis=0) if pieces else np.zeros((0, H), np.float32)
+        outs.append(ep_combine(disp[s]["send_map"], returned))
+    return outs

@@ -69,6 +69,13 @@ SIGNATURES = {
     "reaxmoe_plan_static": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P]),
     "reaxmoe_expanded_scales_size": (ctypes.c_size_t, [_I32, _I32, _I32]),
     "reaxmoe_expand_scales": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P]),
+    "reaxmoe_ep_record_bytes": (ctypes.c_size_t, [_I32, _I32]),
+    "reaxmoe_ep_dispatch_workspace_size": (ctypes.c_size_t, [_PP, _I32]),
+    "reaxmoe_ep_dispatch": (ctypes.c_int, [_PP, _I32, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P, _P]),
+    "reaxmoe_ep_expert_workspace_size": (ctypes.c_size_t, [_PP]),
+    "reaxmoe_ep_expert_forward": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P,
+                                                 _P]),
+    "reaxmoe_ep_combine": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _P, _P]),
 }
 
 _lock = threading.Lock()

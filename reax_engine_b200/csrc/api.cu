@@ -41,11 +41,13 @@ static int num_sms() {
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-static int check_problem(const reaxmoe_problem* p) {
+// local_topk: an expert-parallel receiver's problem, whose records may carry more pairs (topk) than it owns
+// experts; only the local pairs are used.
+static int check_problem(const reaxmoe_problem* p, bool local_topk = false) {
   if (p == nullptr) return fail(REAXMOE_ERR_NULL, "problem is NULL");
   if (p->experts < 1 || p->experts > kMaxExperts)
     return fail(REAXMOE_ERR_TOO_MANY_EXPERTS, "experts=%d outside [1, %d]", p->experts, kMaxExperts);
-  if (p->topk < 1 || p->topk > kMaxTopk || p->topk > p->experts)
+  if (p->topk < 1 || p->topk > kMaxTopk || (!local_topk && p->topk > p->experts))
     return fail(REAXMOE_ERR_TOO_MANY_EXPERTS, "topk=%d outside [1, min(%d, experts)]", p->topk, kMaxTopk);
   if (p->hidden < 256 || p->hidden > 3072 || p->hidden % 128 != 0)
     return fail(REAXMOE_ERR_BAD_SHAPE, "hidden=%d must be a multiple of 128 in [256, 3072]", p->hidden);
@@ -138,6 +140,51 @@ static int check_ws(const reaxmoe_problem* p, void* ws, size_t bytes, Layout* L)
   if (bytes < L->total)
     return fail(REAXMOE_ERR_WORKSPACE, "workspace %zu bytes < required %zu", bytes, L->total);
   return 0;
+}
+
+// Expert-parallel dispatch workspace: rank ids of the pairs and the routing data over ranks.
+struct EpDispatchLayout {
+  size_t status, rid, seg_counts, seg_base, roff, boff, tile_prefix, total;
+};
+
+static EpDispatchLayout ep_dispatch_layout(const reaxmoe_problem* p, int ranks) {
+  EpDispatchLayout L;
+  const int64_t m = p->tokens, k = p->topk;
+  const int64_t nseg = ceil_div64(m, kSegTokens);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = up256(off + bytes);
+    return o;
+  };
+  L.status = take(64);
+  L.rid = take((size_t)m * k * 4);
+  L.seg_counts = take((size_t)nseg * ranks * 4);
+  L.seg_base = take((size_t)nseg * ranks * 4);
+  L.roff = take((size_t)(ranks + 1) * 4);
+  L.boff = take((size_t)(ranks + 1) * 4);
+  L.tile_prefix = take((size_t)(ranks + 1) * 4);
+  L.total = off;
+  return L;
+}
+
+static int check_ep(const reaxmoe_problem* p, int ranks) {
+  int rc = check_problem(p);
+  if (rc) return rc;
+  if (ranks < 1 || ranks > kMaxRanks || p->experts % ranks != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "ranks=%d must be in [1, %d] and divide experts=%d", ranks, kMaxRanks,
+                p->experts);
+  return 0;
+}
+
+// Expert-parallel receiver workspace: the single-GPU layout of the local problem, then the records' local ids and
+// weights as [tokens, topk] arrays.
+static size_t ep_expert_lid(const Layout& L) { return L.total; }
+static size_t ep_expert_lw(const reaxmoe_problem* p, const Layout& L) {
+  return up256(L.total + (size_t)p->tokens * p->topk * 4);
+}
+static size_t ep_expert_total(const reaxmoe_problem* p, const Layout& L) {
+  return up256(ep_expert_lw(p, L) + (size_t)p->tokens * p->topk * 4);
 }
 
 static unsigned long long device_timeout_ns() {
@@ -398,6 +445,113 @@ int reaxmoe_expand_scales(const void* sf, int32_t experts, int32_t n, int32_t k,
   launch_expand_scales(static_cast<const uint8_t*>(sf), experts, n, k, static_cast<uint8_t*>(out),
                        static_cast<cudaStream_t>(stream));
   return cuda_check("expand_scales");
+}
+
+size_t reaxmoe_ep_record_bytes(int32_t hidden, int32_t topk) {
+  if (hidden < 128 || hidden % 128 != 0 || topk < 1 || topk > kMaxTopk) return 0;
+  const size_t b = (size_t)hidden / 2 + (size_t)hidden / 16 + (size_t)topk * 8;
+  return (b + 15) & ~size_t(15);
+}
+
+size_t reaxmoe_ep_dispatch_workspace_size(const reaxmoe_problem* p, int32_t ranks) {
+  if (check_ep(p, ranks)) return 0;
+  return ep_dispatch_layout(p, ranks).total;
+}
+
+int reaxmoe_ep_dispatch(const reaxmoe_problem* p, int32_t ranks, const void* a, const float* a1_gscale,
+                        const int32_t* topk_ids, const float* topk_weights, void* workspace, size_t workspace_bytes,
+                        int32_t* send_counts, int32_t* send_map, void* send_records, void* stream) {
+  int rc = check_ep(p, ranks);
+  if (rc) return rc;
+  const EpDispatchLayout L = ep_dispatch_layout(p, ranks);
+  if (workspace == nullptr) return fail(REAXMOE_ERR_WORKSPACE, "ep_dispatch: workspace is NULL");
+  if (!aligned16(workspace)) return fail(REAXMOE_ERR_MISALIGNED, "ep_dispatch: workspace not 16-byte aligned");
+  if (workspace_bytes < L.total)
+    return fail(REAXMOE_ERR_WORKSPACE, "ep_dispatch: workspace %zu bytes < required %zu", workspace_bytes, L.total);
+  if (send_counts == nullptr) return fail(REAXMOE_ERR_NULL, "ep_dispatch: send_counts is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* b = static_cast<uint8_t*>(workspace);
+  int* status = reinterpret_cast<int*>(b + L.status);
+  cudaMemsetAsync(status, 0, sizeof(int), s);
+  if (p->tokens == 0) {
+    cudaMemsetAsync(send_counts, 0, (size_t)ranks * 4, s);
+    return cuda_check("ep_dispatch");
+  }
+  if (!a || !a1_gscale || !topk_ids || !topk_weights || !send_map || !send_records)
+    return fail(REAXMOE_ERR_NULL, "ep_dispatch: NULL pointer");
+  if (!aligned16(a) || !aligned16(send_records))
+    return fail(REAXMOE_ERR_MISALIGNED, "ep_dispatch: a and send_records must be 16-byte aligned");
+  const int El = p->experts / ranks;
+  const int rec = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
+  int* rid = reinterpret_cast<int*>(b + L.rid);
+  int* seg_counts = reinterpret_cast<int*>(b + L.seg_counts);
+  int* seg_base = reinterpret_cast<int*>(b + L.seg_base);
+  int* roff = reinterpret_cast<int*>(b + L.roff);
+  launch_ep_rank_ids(topk_ids, p->tokens, p->topk, p->experts, El, a1_gscale, rid, status, s);
+  launch_count(rid, p->tokens, p->topk, ranks, seg_counts, status, s);
+  launch_plan(seg_counts, (int)ceil_div64(p->tokens, kSegTokens), ranks, seg_base, send_counts, roff,
+              reinterpret_cast<int*>(b + L.boff), reinterpret_cast<int*>(b + L.tile_prefix), nullptr, nullptr, 0, 0, 0,
+              0, s);
+  launch_ep_pack(static_cast<const __nv_bfloat16*>(a), a1_gscale, topk_ids, topk_weights, rid, seg_base, roff,
+                 p->tokens, p->hidden, p->experts, El, p->topk, rec, static_cast<uint8_t*>(send_records), send_map, s);
+  return cuda_check("ep_dispatch");
+}
+
+size_t reaxmoe_ep_expert_workspace_size(const reaxmoe_problem* local) {
+  if (check_problem(local, true)) return 0;
+  return ep_expert_total(local, layout(local));
+}
+
+int reaxmoe_ep_expert_forward(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
+                              const void* w1_sf, const float* w1_alphas, const float* a2_gscale, const void* w2_fp4,
+                              const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes,
+                              void* partial, void* stream) {
+  const reaxmoe_problem* p = local;
+  int rc = check_problem(p, true);
+  if (rc) return rc;
+  const Layout L = layout(p);
+  const size_t need = ep_expert_total(p, L);
+  if (workspace == nullptr) return fail(REAXMOE_ERR_WORKSPACE, "ep_expert_forward: workspace is NULL");
+  if (!aligned16(workspace)) return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_forward: workspace not 16-byte aligned");
+  if (workspace_bytes < need)
+    return fail(REAXMOE_ERR_WORKSPACE, "ep_expert_forward: workspace %zu bytes < required %zu", workspace_bytes, need);
+  if (p->tokens == 0) return 0;
+  if (!recv_records || !w1_fp4 || !w1_sf || !w1_alphas || !a2_gscale || !w2_fp4 || !w2_sf || !w2_alphas || !partial)
+    return fail(REAXMOE_ERR_NULL, "ep_expert_forward: NULL pointer");
+  if (!aligned16(recv_records) || !aligned16(w1_fp4) || !aligned16(w1_sf) || !aligned16(w2_fp4) ||
+      !aligned16(w2_sf) || !aligned16(partial))
+    return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_forward: records, weights and partial must be 16-byte aligned");
+  const WS w = carve(workspace, L);
+  uint8_t* b = static_cast<uint8_t*>(workspace);
+  int* lid = reinterpret_cast<int*>(b + ep_expert_lid(L));
+  float* lw = reinterpret_cast<float*>(b + ep_expert_lw(p, L));
+  const uint8_t* rec = static_cast<const uint8_t*>(recv_records);
+  const int rec_bytes = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  launch_ep_unpack_meta(rec, p->tokens, p->topk, p->hidden, rec_bytes, lid, lw, s);
+  if ((rc = do_plan(p, lid, w, nullptr, nullptr, s))) return rc;
+  launch_ep_permute(rec, lid, w.seg_base, w.eoff, w.boff, p->tokens, p->hidden, p->experts, p->topk, rec_bytes,
+                    w.rep_fp4, w.rep_sf, w.c_map, s);
+  if ((rc = cuda_check("ep_permute"))) return rc;
+  const int sms = num_sms();
+  GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4, w.int_sf);
+  if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "ep_expert_forward: gemm_w13 launch failed");
+  GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, w2_fp4, w2_sf, w2_alphas, w.c3);
+  if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "ep_expert_forward: gemm_w2 launch failed");
+  launch_combine(w.c3, w.c_map, lw, p->tokens, p->hidden, p->topk, static_cast<__nv_bfloat16*>(partial), sms, s);
+  return cuda_check("ep_expert_forward");
+}
+
+int reaxmoe_ep_combine(int32_t tokens, int32_t hidden, int32_t topk, const int32_t* send_map, const void* returned,
+                       void* output, void* stream) {
+  if (tokens < 0 || hidden < 128 || hidden % 128 != 0 || topk < 1 || topk > kMaxTopk)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "ep_combine: tokens=%d hidden=%d topk=%d", tokens, hidden, topk);
+  if (tokens == 0) return 0;
+  if (!send_map || !returned || !output) return fail(REAXMOE_ERR_NULL, "ep_combine: NULL pointer");
+  if (!aligned16(returned) || !aligned16(output)) return fail(REAXMOE_ERR_MISALIGNED, "ep_combine: misaligned");
+  launch_ep_combine(static_cast<const __nv_bfloat16*>(returned), send_map, tokens, hidden, topk,
+                    static_cast<__nv_bfloat16*>(output), num_sms(), static_cast<cudaStream_t>(stream));
+  return cuda_check("ep_combine");
 }
 
 int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream) {

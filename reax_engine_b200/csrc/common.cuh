@@ -18,6 +18,7 @@ namespace reaxmoe {
 
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopk = 16;
+constexpr int kMaxRanks = 64;     // expert-parallel ranks
 constexpr int kSegTokens = 128;   // tokens per routing segment (count / permute CTA)
 
 __host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }

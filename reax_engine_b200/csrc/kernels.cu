@@ -4,6 +4,7 @@
 // warp shuffles for reductions, no tensor cores.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "slots.cuh"
 
 namespace reaxmoe {
 
@@ -84,7 +85,8 @@ int launch_route(const float* logits, const float* scale, int T, int E, int K, i
 
 // ------------------------------------------------------------------------------------------------------
 // K2a count: per-segment expert histogram (segment = kSegTokens consecutive tokens). Shared-memory integer
-// atomics: exact counts, independent of order. Out-of-range ids are flagged and skipped.
+// atomics: exact counts, independent of order. A negative id marks an unused slot (the expert-parallel path pads
+// a token's experts on another rank with -1) and is skipped; ids >= E are flagged and skipped.
 // ------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) count_kernel(const int* __restrict__ ids, int m, int k, int E,
                                                     int* __restrict__ seg_counts, int* status) {
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(256) count_kernel(const int* __restrict__ ids,
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int e = p[i];
     if ((unsigned)e < (unsigned)E) atomicAdd(&hist[e], 1);
-    else set_status(status, REAXMOE_ERR_BAD_EXPERT_ID);
+    else if (e >= E) set_status(status, REAXMOE_ERR_BAD_EXPERT_ID);  // negative ids mark unused slots
   }
   __syncthreads();
   for (int i = threadIdx.x; i < E; i += blockDim.x) seg_counts[(int64_t)blockIdx.x * E + i] = hist[i];
@@ -180,10 +182,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
 
 // ------------------------------------------------------------------------------------------------------
 // K3 permute_quant: one CTA per segment.
-//  Phase A (warp 0): canonical slot of every (token, j) pair of the segment. For a chunk of 32 tokens
-//  (one per lane) each lane sets its bit in a per-expert shared mask for each of its k experts; the slot of
-//  (t, j) is run[e] + popc(mask[e] & lanes_below) where run[e] = expert_offsets[e] + seg_base[seg][e] + the
-//  slots of e in the earlier chunks. Token-major order inside an expert, no data-dependent atomics.
+//  Phase A (warp 0, segment_slots): canonical slot of every (token, j) pair of the segment, token-major inside
+//  an expert, starting from run[e] = expert_offsets[e] + seg_base[seg][e].
 //  Phase B (all warps): each token row is NVFP4-quantised once per distinct expert input scale and written
 //  to its k slots (FP4 bytes + one 32-bit word of 4 scale bytes per 64-element group), the same bytes as
 //  vLLM's per-slot quant of the shuffled rows (blink_moe.py:301-323, cutlass_moe.py:585-593).
@@ -207,49 +207,7 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
     gq[e] = __fdiv_rn(1.0f, a1_gscale[e]);
   }
   __syncthreads();
-  if (warp == 0) {
-    const uint32_t below = (1u << lane) - 1u;
-    for (int c0 = 0; c0 < nt; c0 += 32) {
-      const int tl = c0 + lane;
-      const bool active = tl < nt;
-      int ej[kMaxTopk];
-#pragma unroll
-      for (int j = 0; j < kMaxTopk; ++j) {
-        ej[j] = -1;
-        if (j < k && active) {
-          const int e = ids[(t0 + tl) * k + j];
-          if ((unsigned)e < (unsigned)E) {
-            ej[j] = e;
-            atomicOr(&mask[e], 1u << lane);
-          }
-        }
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < kMaxTopk; ++j) {
-        if (j < k && active) {
-          int pos = -1;
-          if (ej[j] >= 0) pos = run[ej[j]] + __popc(mask[ej[j]] & below);
-          pos_s[tl * k + j] = pos;
-          exp_s[tl * k + j] = (short)ej[j];
-          c_map[(t0 + tl) * k + j] = pos;
-        }
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < kMaxTopk; ++j) {
-        if (j < k && ej[j] >= 0) {
-          const uint32_t mk = mask[ej[j]];
-          if ((mk & below) == 0u) run[ej[j]] += __popc(mk);
-        }
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < kMaxTopk; ++j)
-        if (j < k && ej[j] >= 0) mask[ej[j]] = 0u;
-      __syncwarp();
-    }
-  }
+  if (warp == 0) segment_slots(ids, t0, nt, k, E, run, mask, pos_s, exp_s, c_map);
   __syncthreads();
   // phase B: each lane owns 32-element units (two scale blocks: 16 FP4 bytes + 2 scale bytes per slot); all of a
   // lane's loads for a token are issued before any arithmetic

@@ -22,6 +22,20 @@ int launch_expand_scales(const uint8_t* sf, int E, int N, int K, uint8_t* out, c
 int launch_prepack_w13(const uint8_t* w, const uint8_t* sf, int E, int inter, int H, uint8_t* wp, uint8_t* sfp,
                        cudaStream_t s);
 
+// Expert-parallel dispatch / receive / combine (ep.cu).
+int launch_ep_rank_ids(const int* ids, int m, int k, int E, int El, const float* a1_gscale, int* rid, int* status,
+                       cudaStream_t s);
+int launch_ep_pack(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const float* w, const int* rid,
+                   const int* seg_base, const int* roff, int m, int H, int E, int El, int k, int rec_bytes,
+                   uint8_t* records, int* send_map, cudaStream_t s);
+int launch_ep_unpack_meta(const uint8_t* records, int n, int k, int H, int rec_bytes, int* lid, float* lw,
+                          cudaStream_t s);
+int launch_ep_permute(const uint8_t* records, const int* lid, const int* seg_base, const int* eoff, const int* boff,
+                      int n, int H, int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* rep_sf, int* c_map,
+                      cudaStream_t s);
+int launch_ep_combine(const __nv_bfloat16* ret, const int* map, int m, int H, int k, __nv_bfloat16* out, int num_sms,
+                      cudaStream_t s);
+
 // Grouped NVFP4 GEMM (gemm_sm100.cu). mode 0: out bf16 [slots, N]; mode 1: fused act(gate)*up + NVFP4 quant
 // into q_out [slots, N/4] (N = 2*inter interleaved) and q_sf atoms.
 struct GemmLaunch {

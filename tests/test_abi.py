@@ -95,3 +95,28 @@ def test_python_api_refuses_cpu_tensors():
     import torch
     with pytest.raises(ValueError):
         R.route(None, torch.zeros(4, 128), 8)
+
+
+def test_ep_entry_points_reject_bad_args():
+    lib = L.lib()
+    assert lib.reaxmoe_ep_record_bytes(2816, 8) == 1648
+    assert lib.reaxmoe_ep_record_bytes(384, 4) == 256       # 248 bytes of fields, padded to 16
+    assert lib.reaxmoe_ep_record_bytes(100, 8) == 0
+    prob = L.problem(64, 2816, 704, 128, 8, 1)
+    assert lib.reaxmoe_ep_dispatch_workspace_size(ctypes.byref(prob), 8) > 0
+    assert lib.reaxmoe_ep_dispatch_workspace_size(ctypes.byref(prob), 3) == 0      # 3 does not divide 128
+    assert lib.reaxmoe_ep_dispatch_workspace_size(ctypes.byref(prob), 65) == 0
+    assert lib.reaxmoe_ep_dispatch(ctypes.byref(prob), 8, None, None, None, None, None, 0, None, None, None,
+                                   None) == L.ERR_WORKSPACE
+    n = lib.reaxmoe_ep_dispatch_workspace_size(ctypes.byref(prob), 8)
+    buf = ctypes.create_string_buffer(n + 256)
+    addr = (ctypes.addressof(buf) + 255) & ~255
+    assert lib.reaxmoe_ep_dispatch(ctypes.byref(prob), 8, None, None, None, None, addr, n, None, None, None,
+                                   None) == L.ERR_NULL
+    # the receiver's local problem may carry more pairs per record than it owns experts
+    local = L.problem(100, 2816, 704, 2, 8, 1)
+    assert lib.reaxmoe_ep_expert_workspace_size(ctypes.byref(local)) > 0
+    assert lib.reaxmoe_workspace_size(ctypes.byref(local)) == 0
+    assert lib.reaxmoe_ep_combine(4, 2816, 8, None, None, None, None) == L.ERR_NULL
+    assert lib.reaxmoe_ep_combine(0, 2816, 8, None, None, None, None) == L.OK
+    assert lib.reaxmoe_ep_combine(4, 2800, 8, None, None, None, None) == L.ERR_BAD_SHAPE
