@@ -65,29 +65,39 @@ def workload(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms around the timed region. The summary keeps the
+    samples taken between __enter__ and __exit__ (the timed region); when the region is shorter than the sampling
+    interval it falls back to the samples nearest to it, and says so."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.t_in = self.t_out = None
 
     def __enter__(self):
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
-                 "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.fh, stderr=subprocess.DEVNULL)
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and os.path.getsize(self.path) == 0:
+                time.sleep(0.01)
         except Exception:  # noqa: BLE001
             self.proc = None
+        self.t_in = time.time()
         return self
 
     def __exit__(self, *a):
+        self.t_out = time.time()
         if self.proc is not None:
+            time.sleep(0.06)     # one more sample after the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -96,26 +106,31 @@ class ClockSampler:
             self.fh.close()
 
     def summary(self) -> dict:
+        import datetime
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm, mx, reasons = [], [], set()
+        rows = []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(f[2]), float(f[3]),
+                             {n for n, v in zip(names, f[6:10]) if v.lower().startswith("active")}))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = [r for r in rows if self.t_in <= r[0] <= self.t_out]
+        basis = "in region"
+        if not inside:
+            inside = sorted(rows, key=lambda r: abs(r[0] - 0.5 * (self.t_in + self.t_out)))[:2]
+            basis = "nearest to a region shorter than the 50 ms sampling interval"
+        reasons = set().union(*(r[3] for r in inside))
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in inside),
+                "reasons": sorted(reasons), "samples": len(inside), "basis": basis}
 
 
 def build_inputs(wl: dict, device, seed: int = 0):

@@ -27,7 +27,7 @@
 // TMEM: accumulator [0, 256), two B-scale buffers of 32 columns, resident A scales (4 columns per k-chunk).
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records REAXMOE_ERR_DEVICE_TIMEOUT in the
 // status word, raises a CTA-wide abort flag, drains its own in-flight copies and MMAs, frees TMEM and returns.
-// No TMA multicast and no clusters: the same kernel runs on every rank of the expert-parallel path.
+// Plain per-CTA TMA loads, no thread-block clusters: the same kernel runs on every rank of the expert-parallel path.
 #include <cuda.h>
 
 #include "common.cuh"
