@@ -63,8 +63,8 @@ static int check_problem(const reaxmoe_problem* p, bool local_topk = false) {
 
 // Workspace regions, each 256-byte aligned.
 struct Layout {
-  size_t status, seg_counts, seg_base, counts, eoff, boff, tile_prefix, c_map, rep_fp4, rep_sf, int_fp4, int_sf, c3,
-      total;
+  size_t status, seg_counts, seg_base, counts, eoff, boff, tile_prefix, c_map, rep_fp4, lin_sf, rep_sf, int_fp4,
+      int_sf, c3, total;
 };
 
 static size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -90,6 +90,7 @@ static Layout layout(const reaxmoe_problem* p) {
   L.tile_prefix = take((size_t)(E + 1) * 4);
   L.c_map = take((size_t)slots * 4);
   L.rep_fp4 = take((size_t)slots * (H / 2));
+  L.lin_sf = take((size_t)slots * (H / 16));
   L.rep_sf = take((size_t)sfblk * (H / 64) * 512);
   L.int_fp4 = take((size_t)slots * (I / 2));
   L.int_sf = take((size_t)sfblk * (I / 64) * 512);
@@ -108,6 +109,7 @@ struct WS {
   int* tile_prefix;
   int* c_map;
   uint8_t* rep_fp4;
+  uint8_t* lin_sf;  // scale bytes of the routed rows in slot order, [slots, H/16] (permute -> swizzle)
   uint8_t* rep_sf;
   uint8_t* int_fp4;
   uint8_t* int_sf;
@@ -126,6 +128,7 @@ static WS carve(void* ws, const Layout& L) {
   w.tile_prefix = reinterpret_cast<int*>(b + L.tile_prefix);
   w.c_map = reinterpret_cast<int*>(b + L.c_map);
   w.rep_fp4 = b + L.rep_fp4;
+  w.lin_sf = b + L.lin_sf;
   w.rep_sf = b + L.rep_sf;
   w.int_fp4 = b + L.int_fp4;
   w.int_sf = b + L.int_sf;
@@ -321,9 +324,11 @@ int reaxmoe_permute_quant(const reaxmoe_problem* p, const void* a, const float* 
   if (!aligned16(a) || !aligned16(rep_fp4) || !aligned16(rep_sf))
     return fail(REAXMOE_ERR_MISALIGNED, "permute_quant: a, rep_fp4 and rep_sf must be 16-byte aligned");
   const WS w = carve(workspace, L);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   launch_permute_quant(static_cast<const __nv_bfloat16*>(a), a1_gscale, topk_ids, w.seg_base, w.eoff, w.boff,
-                       p->tokens, p->hidden, p->experts, p->topk, static_cast<uint8_t*>(rep_fp4),
-                       static_cast<uint8_t*>(rep_sf), c_map, static_cast<cudaStream_t>(stream));
+                       p->tokens, p->hidden, p->experts, p->topk, static_cast<uint8_t*>(rep_fp4), w.lin_sf, c_map, s);
+  launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
+                        (int64_t)p->tokens * p->topk, static_cast<uint8_t*>(rep_sf), s);
   return cuda_check("permute_quant");
 }
 
@@ -394,7 +399,9 @@ int reaxmoe_forward(const reaxmoe_forward_args* args, void* workspace, size_t wo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = do_plan(p, args->topk_ids, w, nullptr, nullptr, s))) return rc;
   launch_permute_quant(static_cast<const __nv_bfloat16*>(args->a), args->a1_gscale, args->topk_ids, w.seg_base,
-                       w.eoff, w.boff, p->tokens, p->hidden, p->experts, p->topk, w.rep_fp4, w.rep_sf, w.c_map, s);
+                       w.eoff, w.boff, p->tokens, p->hidden, p->experts, p->topk, w.rep_fp4, w.lin_sf, w.c_map, s);
+  launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
+                        (int64_t)p->tokens * p->topk, w.rep_sf, s);
   if ((rc = cuda_check("permute_quant"))) return rc;
   const int sms = num_sms();
   GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, args->w1_fp4, args->w1_sf, args->w1_alphas, args->a2_gscale,
@@ -530,8 +537,10 @@ int reaxmoe_ep_expert_forward(const reaxmoe_problem* local, const void* recv_rec
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   launch_ep_unpack_meta(rec, p->tokens, p->topk, p->hidden, rec_bytes, lid, lw, s);
   if ((rc = do_plan(p, lid, w, nullptr, nullptr, s))) return rc;
-  launch_ep_permute(rec, lid, w.seg_base, w.eoff, w.boff, p->tokens, p->hidden, p->experts, p->topk, rec_bytes,
-                    w.rep_fp4, w.rep_sf, w.c_map, s);
+  launch_ep_permute(rec, lid, w.seg_base, w.eoff, p->tokens, p->hidden, p->experts, p->topk, rec_bytes, w.rep_fp4,
+                    w.lin_sf, w.c_map, s);
+  launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
+                        (int64_t)p->tokens * p->topk, w.rep_sf, s);
   if ((rc = cuda_check("ep_permute"))) return rc;
   const int sms = num_sms();
   GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4, w.int_sf);

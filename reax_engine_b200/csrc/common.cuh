@@ -19,6 +19,7 @@ namespace reaxmoe {
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopk = 16;
 constexpr int kMaxRanks = 64;     // expert-parallel ranks
+constexpr int kPermUnits = 3;     // 32-element units per lane and token in the permute kernels: hidden <= 3072
 constexpr int kSegTokens = 128;   // tokens per routing segment (count / permute CTA)
 
 __host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -71,11 +72,16 @@ __device__ __forceinline__ void e2m1_thresholds(float sf, float (&T)[7]) {
   }
 }
 
-// e2m1 code of x / sf (sign = x < 0), identical to e2m1_code(__fdiv_rn(x, sf)) for the thresholds of sf.
-__device__ __forceinline__ uint32_t e2m1_code_t(float x, const float (&T)[7]) {
+// The sign of fl(x / sf) is set iff x < 0 and the quotient does not underflow to -0, i.e. |x| > sf * 2^-150 (a
+// quotient of exactly 2^-150 rounds to 0, ties to even). With z = RD(sf * 2^-150) (exact in fp64, then rounded down
+// to float), |x| > sf * 2^-150  <=>  |x| > z for any float |x|.
+__device__ __forceinline__ float zero_threshold(float sf) { return __double2float_rd((double)sf * 0x1p-150); }
+
+// e2m1 code of x / sf, identical to e2m1_code(__fdiv_rn(x, sf)) for the thresholds T and zero threshold z of sf.
+__device__ __forceinline__ uint32_t e2m1_code_t(float x, const float (&T)[7], float z) {
   const float a = fabsf(x);
   const uint32_t idx = (a > T[0]) + (a > T[1]) + (a > T[2]) + (a > T[3]) + (a > T[4]) + (a > T[5]) + (a > T[6]);
-  return idx | ((x < 0.0f) ? 8u : 0u);
+  return idx | ((x < 0.0f && a > z) ? 8u : 0u);
 }
 
 // Quantise one 16-element block with dequant-side global scale g. Returns the e4m3 scale byte; writes the
@@ -89,9 +95,61 @@ __device__ __forceinline__ uint32_t quant_block16(const float (&v)[16], float g,
   const float sf = fmaxf(__fmul_rn(e4m3_to_f32(s8), g), 1e-30f);
   float T[7];
   e2m1_thresholds(sf, T);
+  const float z = zero_threshold(sf);
   uint32_t w[2] = {0u, 0u};
 #pragma unroll
-  for (int i = 0; i < 16; ++i) w[i >> 3] |= e2m1_code_t(v[i], T) << ((i & 7) * 4);
+  for (int i = 0; i < 16; ++i) w[i >> 3] |= e2m1_code_t(v[i], T, z) << ((i & 7) * 4);
+  lo = w[0];
+  hi = w[1];
+  return s8;
+}
+
+// The same quantisation for 16 values that are exactly bf16 (packed pairs, element 2i in the low half of xw[i]),
+// two elements per instruction. For a bf16 value a and a float threshold T >= 0, a > T  <=>  a > Tb with Tb = T
+// truncated to bf16 (T's upper 16 bits): Tb <= T < the next bf16 above Tb. So the decisions run as bf16x2
+// comparisons against truncated thresholds, as a 3-level binary search over the 7 (non-decreasing) thresholds:
+// bit 2 = a > T3; bit 1 = a > (bit2 ? T5 : T1); bit 0 = a > T[4*bit2 + 2*bit1]. The sign bit is x < 0 and
+// |x| > z (zero_threshold, truncated to bf16 the same way), as in the fp32 path: -0, NaN and quotients that underflow
+// to -0 get no sign.
+__device__ __forceinline__ uint32_t bf2_gt(uint32_t a, uint32_t b) {
+  return __hgt2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+}
+__device__ __forceinline__ uint32_t quant_block16_bf16(const uint32_t (&xw)[8], float g, uint32_t& lo, uint32_t& hi) {
+  uint32_t ab[8];
+  __nv_bfloat162 m2;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    ab[i] = xw[i] & 0x7FFF7FFFu;
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&ab[i]);
+    m2 = i == 0 ? v : __hmax2(m2, v);
+  }
+  const float bamax = fmaxf(__low2float(m2), __high2float(m2));
+  const float s = fminf(__fdiv_rn(bamax, __fmul_rn(6.0f, g)), 448.0f);
+  const uint32_t s8 = e4m3_rn(s);
+  const float sf = fmaxf(__fmul_rn(e4m3_to_f32(s8), g), 1e-30f);
+  float T[7];
+  e2m1_thresholds(sf, T);
+  uint32_t tb[7];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) tb[i] = (__float_as_uint(T[i]) >> 16) * 0x00010001u;
+  const uint32_t zb = (__float_as_uint(zero_threshold(sf)) >> 16) * 0x00010001u;
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t a = ab[i];
+    const uint32_t m2b = bf2_gt(a, tb[3]);
+    const uint32_t t1 = (m2b & tb[5]) | (~m2b & tb[1]);
+    const uint32_t m1b = bf2_gt(a, t1);
+    const uint32_t ta = (m1b & tb[6]) | (~m1b & tb[4]);
+    const uint32_t tc = (m1b & tb[2]) | (~m1b & tb[0]);
+    const uint32_t t0 = (m2b & ta) | (~m2b & tc);
+    const uint32_t m0b = bf2_gt(a, t0);
+    const uint32_t neg = __hlt2_mask(*reinterpret_cast<const __nv_bfloat162*>(&xw[i]), __float2bfloat162_rn(0.0f)) &
+                         bf2_gt(a, zb);
+    const uint32_t idx = (m2b & 0x00040004u) | (m1b & 0x00020002u) | (m0b & 0x00010001u) | (neg & 0x00080008u);
+    const uint32_t byte = (idx & 0xFu) | ((idx >> 12) & 0xF0u);
+    w[i >> 2] |= byte << (8 * (i & 3));
+  }
   lo = w[0];
   hi = w[1];
   return s8;

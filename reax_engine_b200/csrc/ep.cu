@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(256) ep_rank_ids_kernel(const int* __restrict_
 // (token, rank) its record index, token-major inside a rank's contiguous range; send_map [m, k] gets the record
 // index at that pair and -1 elsewhere. Phase B quantises each token row once per distinct rank scale and writes its
 // records.
-__global__ void __launch_bounds__(256) ep_pack_kernel(
+__global__ void __launch_bounds__(256, 3) ep_pack_kernel(
     const __nv_bfloat16* __restrict__ a, const float* __restrict__ a1_gscale, const int* __restrict__ ids,
     const float* __restrict__ topk_w, const int* __restrict__ rid, const int* __restrict__ seg_base,
     const int* __restrict__ roff, int m, int H, int E, int El, int k, int rec_bytes, uint8_t* __restrict__ records,
@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(
   const int units = H / 32;
   const int meta = H / 2 + H / 16;
   const int nwarps = blockDim.x >> 5;
-  constexpr int kMaxUnits = 4;  // per lane per token: H <= 32 * 32 * kMaxUnits
+  constexpr int kMaxUnits = kPermUnits;
   for (int tl = warp; tl < nt; tl += nwarps) {
     const int64_t t = t0 + tl;
     const uint4* src = reinterpret_cast<const uint4*>(a + t * H);
@@ -114,9 +114,6 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(
     for (int it = 0; it < kMaxUnits; ++it) {
       const int un = lane + 32 * it;
       if (un >= units) continue;
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) bf16x8_to_f32(raw[it][i], v + 8 * i);
       uint32_t w[4];
       uint32_t sbytes = 0u;
       uint32_t gbits = 0xFFFFFFFFu;  // a NaN pattern: never equal to a real scale
@@ -129,10 +126,9 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(
           sbytes = 0u;
 #pragma unroll
           for (int b = 0; b < 2; ++b) {
-            float blk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) blk[i] = v[b * 16 + i];
-            sbytes |= quant_block16(blk, g, w[2 * b], w[2 * b + 1]) << (8 * b);
+            const uint4 q0 = raw[it][2 * b], q1 = raw[it][2 * b + 1];
+            const uint32_t xw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            sbytes |= quant_block16_bf16(xw, g, w[2 * b], w[2 * b + 1]) << (8 * b);
           }
         }
         uint8_t* rec = records + (int64_t)pos_s[tl * k + j] * rec_bytes;
@@ -158,12 +154,12 @@ __global__ void __launch_bounds__(256) ep_unpack_meta_kernel(const uint8_t* __re
 
 // Receiver permute: one CTA per segment of kSegTokens records. Phase A assigns the canonical slots of the local
 // pairs (record-major inside a local expert); phase B copies each record's FP4 row and scales to its slots, the scales
-// into the swizzled 128x4 atoms the grouped GEMM reads.
+// into the slot's row of the linear scale buffer (swizzle_scales_kernel then writes the 128x4 atoms the GEMM reads).
 __global__ void __launch_bounds__(256) ep_permute_kernel(const uint8_t* __restrict__ records, const int* __restrict__ lid,
                                                          const int* __restrict__ seg_base, const int* __restrict__ eoff,
-                                                         const int* __restrict__ boff, int n, int H, int El, int k,
-                                                         int rec_bytes, uint8_t* __restrict__ rep_fp4,
-                                                         uint8_t* __restrict__ rep_sf, int* __restrict__ c_map) {
+                                                         int n, int H, int El, int k, int rec_bytes,
+                                                         uint8_t* __restrict__ rep_fp4, uint8_t* __restrict__ lin_sf,
+                                                         int* __restrict__ c_map) {
   __shared__ int run[kMaxExperts];
   __shared__ uint32_t mask[kMaxExperts];
   __shared__ int pos_s[kSegTokens * kMaxTopk];
@@ -180,9 +176,9 @@ __global__ void __launch_bounds__(256) ep_permute_kernel(const uint8_t* __restri
   if (warp == 0) segment_slots(lid, t0, nt, k, El, run, mask, pos_s, exp_s, c_map);
   __syncthreads();
   const int units = H / 32;
-  const int k64 = H / 64;
+  const int k16 = H / 16;
   const int nwarps = blockDim.x >> 5;
-  constexpr int kMaxUnits = 4;
+  constexpr int kMaxUnits = kPermUnits;
   for (int tl = warp; tl < nt; tl += nwarps) {
     const uint8_t* rec = records + (t0 + tl) * rec_bytes;
     uint4 q[kMaxUnits];
@@ -199,13 +195,12 @@ __global__ void __launch_bounds__(256) ep_permute_kernel(const uint8_t* __restri
       const int e = exp_s[tl * k + j];
       if (e < 0) continue;
       const int pos = pos_s[tl * k + j];
-      const int64_t sfrow = (int64_t)boff[e] + (pos - eoff[e]);
 #pragma unroll
       for (int it = 0; it < kMaxUnits; ++it) {
         const int un = lane + 32 * it;
         if (un >= units) continue;
         *reinterpret_cast<uint4*>(rep_fp4 + (int64_t)pos * (H / 2) + un * 16) = q[it];
-        *reinterpret_cast<uint16_t*>(rep_sf + sf_offset(sfrow, un * 2, k64)) = sb[it];
+        *reinterpret_cast<uint16_t*>(lin_sf + (int64_t)pos * k16 + un * 2) = sb[it];
       }
     }
   }
@@ -281,12 +276,11 @@ int launch_ep_unpack_meta(const uint8_t* records, int n, int k, int H, int rec_b
   return 0;
 }
 
-int launch_ep_permute(const uint8_t* records, const int* lid, const int* seg_base, const int* eoff, const int* boff,
-                      int n, int H, int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* rep_sf, int* c_map,
-                      cudaStream_t s) {
+int launch_ep_permute(const uint8_t* records, const int* lid, const int* seg_base, const int* eoff, int n, int H,
+                      int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, cudaStream_t s) {
   const int nseg = (int)ceil_div64(n, kSegTokens);
   if (nseg > 0)
-    ep_permute_kernel<<<nseg, 256, 0, s>>>(records, lid, seg_base, eoff, boff, n, H, El, k, rec_bytes, rep_fp4, rep_sf,
+    ep_permute_kernel<<<nseg, 256, 0, s>>>(records, lid, seg_base, eoff, n, H, El, k, rec_bytes, rep_fp4, lin_sf,
                                            c_map);
   return 0;
 }

@@ -249,14 +249,15 @@ __device__ __forceinline__ float act_fn(float x) {
 
 // Fused w13 epilogue for one thread: 32 gate and 32 up accumulators of one row -> 16 packed FP4 bytes + 2 scale
 // bytes. gate/up = bf16(alpha * acc); h = bf16(bf16(act(gate)) * up) (a bf16 product of two bf16 values rounds
-// exactly like the fp32 product rounded to bf16); NVFP4 quantisation of h with engine/fp4.py numerics.
+// exactly like the fp32 product rounded to bf16); NVFP4 quantisation of h with engine/fp4.py numerics, by the bf16x2
+// quantiser (h is exactly bf16).
 template <int ACT>
 __device__ __forceinline__ uint32_t act_quant32(const uint32_t (&x0)[32], const uint32_t (&x1)[32], float alpha,
                                                 float g, uint32_t (&w)[4]) {
   uint32_t sbytes = 0u;
 #pragma unroll
   for (int b = 0; b < 2; ++b) {
-    float h[16];
+    uint32_t hw[8];
 #pragma unroll
     for (int i = 0; i < 16; i += 2) {
       const __nv_bfloat162 gb = __floats2bfloat162_rn(alpha * __uint_as_float(x0[16 * b + i]),
@@ -265,11 +266,10 @@ __device__ __forceinline__ uint32_t act_quant32(const uint32_t (&x0)[32], const 
                                                       alpha * __uint_as_float(x1[16 * b + i + 1]));
       const float2 gf = __bfloat1622float2(gb);
       const __nv_bfloat162 ab = __floats2bfloat162_rn(act_fn<ACT>(gf.x), act_fn<ACT>(gf.y));
-      const float2 hf = __bfloat1622float2(__hmul2(ab, ub));
-      h[i] = hf.x;
-      h[i + 1] = hf.y;
+      const __nv_bfloat162 h2 = __hmul2(ab, ub);
+      hw[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
     }
-    sbytes |= quant_block16(h, g, w[2 * b], w[2 * b + 1]) << (8 * b);
+    sbytes |= quant_block16_bf16(hw, g, w[2 * b], w[2 * b + 1]) << (8 * b);
   }
   return sbytes;
 }

@@ -185,18 +185,20 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
 //  Phase A (warp 0, segment_slots): canonical slot of every (token, j) pair of the segment, token-major inside
 //  an expert, starting from run[e] = expert_offsets[e] + seg_base[seg][e].
 //  Phase B (all warps): each token row is NVFP4-quantised once per distinct expert input scale and written
-//  to its k slots (FP4 bytes + one 32-bit word of 4 scale bytes per 64-element group), the same bytes as
-//  vLLM's per-slot quant of the shuffled rows (blink_moe.py:301-323, cutlass_moe.py:585-593).
+//  to its k slots (FP4 bytes + the two scale bytes of each 32-element unit), the same bytes as vLLM's per-slot
+//  quant of the shuffled rows (blink_moe.py:301-323, cutlass_moe.py:585-593).
 // ------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) permute_quant_kernel(
+__global__ void __launch_bounds__(256, 3) permute_quant_kernel(
     const __nv_bfloat16* __restrict__ a, const float* __restrict__ a1_gscale, const int* __restrict__ ids,
     const int* __restrict__ seg_base, const int* __restrict__ eoff, const int* __restrict__ boff, int m, int H,
-    int E, int k, uint8_t* __restrict__ rep_fp4, uint8_t* __restrict__ rep_sf, int* __restrict__ c_map) {
+    int E, int k, uint8_t* __restrict__ rep_fp4, uint8_t* __restrict__ lin_sf, int* __restrict__ c_map) {
   __shared__ int run[kMaxExperts];
   __shared__ uint32_t mask[kMaxExperts];
   __shared__ float gq[kMaxExperts];
   __shared__ int pos_s[kSegTokens * kMaxTopk];
   __shared__ short exp_s[kSegTokens * kMaxTopk];
+  __shared__ int sl_pos[8][kMaxTopk];           // per warp: the current token's slots
+  __shared__ float sl_g[8][kMaxTopk];
   const int seg = blockIdx.x;
   const int64_t t0 = (int64_t)seg * kSegTokens;
   const int nt = (int)(kSegTokens < m - t0 ? (int64_t)kSegTokens : m - t0);
@@ -209,56 +211,107 @@ __global__ void __launch_bounds__(256) permute_quant_kernel(
   __syncthreads();
   if (warp == 0) segment_slots(ids, t0, nt, k, E, run, mask, pos_s, exp_s, c_map);
   __syncthreads();
-  // phase B: each lane owns 32-element units (two scale blocks: 16 FP4 bytes + 2 scale bytes per slot); all of a
-  // lane's loads for a token are issued before any arithmetic
+  // phase B: one warp per token. Lanes j < k put slot j and its input scale into the warp's shared slot table; lanes
+  // own 32-element units (16 FP4 bytes + 2 scale bytes per slot). A unit is quantised once per distinct input scale
+  // among the slots (once for a uniform scale) with the bf16x2 quantiser, then stored to every slot: FP4 bytes into
+  // the slot's row, scale bytes into the slot's row of the linear scale buffer (full-sector stores; the atoms are
+  // written from it by swizzle_scales_kernel).
   const int units = H / 32;
-  const int k64 = H / 64;
+  const int k16 = H / 16;
   const int nwarps = blockDim.x >> 5;
-  constexpr int kMaxUnits = 4;  // per lane per token: H <= 32 * 32 * kMaxUnits
   for (int tl = warp; tl < nt; tl += nwarps) {
     const int64_t t = t0 + tl;
     const uint4* src = reinterpret_cast<const uint4*>(a + t * H);
-    uint4 raw[kMaxUnits][4];
+    uint4 raw[kPermUnits][4];
 #pragma unroll
-    for (int it = 0; it < kMaxUnits; ++it) {
+    for (int it = 0; it < kPermUnits; ++it) {
       const int un = lane + 32 * it;
       if (un < units) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) raw[it][i] = __ldg(src + un * 4 + i);
       }
     }
+    if (lane < k) {
+      const int e = exp_s[tl * k + lane];
+      sl_pos[warp][lane] = e >= 0 ? pos_s[tl * k + lane] : -1;
+      sl_g[warp][lane] = e >= 0 ? gq[e] : 0.0f;
+    }
+    __syncwarp();
 #pragma unroll
-    for (int it = 0; it < kMaxUnits; ++it) {
+    for (int it = 0; it < kPermUnits; ++it) {
       const int un = lane + 32 * it;
       if (un >= units) continue;
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) bf16x8_to_f32(raw[it][i], v + 8 * i);
       uint32_t w[4];
-      uint32_t sbytes = 0u;
+      uint32_t sb = 0u;
       uint32_t gbits = 0xFFFFFFFFu;  // a NaN pattern: never equal to a real scale
       for (int j = 0; j < k; ++j) {
-        const int e = exp_s[tl * k + j];
-        if (e < 0) continue;
-        const float g = gq[e];
+        const int pos = sl_pos[warp][j];
+        if (pos < 0) continue;
+        const float g = sl_g[warp][j];
         if (__float_as_uint(g) != gbits) {
           gbits = __float_as_uint(g);
-          sbytes = 0u;
+          sb = 0u;
 #pragma unroll
           for (int b = 0; b < 2; ++b) {
-            float blk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) blk[i] = v[b * 16 + i];
-            sbytes |= quant_block16(blk, g, w[2 * b], w[2 * b + 1]) << (8 * b);
+            const uint4 q0 = raw[it][2 * b], q1 = raw[it][2 * b + 1];
+            const uint32_t xw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            sb |= quant_block16_bf16(xw, g, w[2 * b], w[2 * b + 1]) << (8 * b);
           }
         }
-        const int pos = pos_s[tl * k + j];
         *reinterpret_cast<uint4*>(rep_fp4 + (int64_t)pos * (H / 2) + un * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        const int64_t sfrow = (int64_t)boff[e] + (pos - eoff[e]);
-        *reinterpret_cast<uint16_t*>(rep_sf + sf_offset(sfrow, un * 2, k64)) = (uint16_t)sbytes;
+        *reinterpret_cast<uint16_t*>(lin_sf + (int64_t)pos * k16 + un * 2) = (uint16_t)sb;
       }
     }
+    __syncwarp();
   }
+}
+
+// ------------------------------------------------------------------------------------------------------
+// K3b swizzle_scales: one CTA per GEMM m-tile gm (expert e, 128 routed rows), whose scale rows are atom row block gm
+// of the 128x4 layout (blockscale_offsets[e] / 128 == tile_prefix[e]). Reads the tile's rows of the linear scale
+// buffer [slots, H/16] (contiguous) into shared memory and writes its H/64 atoms of 512 bytes with 16-byte stores
+// (atom row i = the 4 scale bytes of rows i, i+32, i+64, i+96). Rows past the expert's count are written as zero.
+// ------------------------------------------------------------------------------------------------------
+constexpr int kSwzMaxWords = 128 * (48 + 1);   // 128 rows x (H/64 <= 48 words + 1 pad word)
+
+__global__ void __launch_bounds__(256) swizzle_scales_kernel(const uint8_t* __restrict__ lin,
+                                                             const int* __restrict__ tile_prefix,
+                                                             const int* __restrict__ counts,
+                                                             const int* __restrict__ eoff, int E, int H,
+                                                             uint8_t* __restrict__ sf) {
+  __shared__ uint32_t tile[kSwzMaxWords];
+  const int gm = blockIdx.x;
+  if (gm >= tile_prefix[E]) return;
+  int lo = 0, hi = E;  // largest e with tile_prefix[e] <= gm
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (tile_prefix[mid] <= gm) lo = mid; else hi = mid;
+  }
+  const int e = lo;
+  const int mt = gm - tile_prefix[e];
+  const int rows = min(128, counts[e] - mt * 128);
+  const int k64 = H / 64;             // 4-byte words per row
+  const int stride = k64 + 1;         // odd: conflict-free column reads
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(lin + ((int64_t)eoff[e] + mt * 128) * (H / 16));
+  for (int i = threadIdx.x; i < 128 * k64; i += blockDim.x) {
+    const int r = i / k64, c = i - r * k64;
+    tile[r * stride + c] = r < rows ? __ldg(src + i) : 0u;
+  }
+  __syncthreads();
+  uint4* dst = reinterpret_cast<uint4*>(sf + (int64_t)gm * k64 * 512);
+  for (int i = threadIdx.x; i < k64 * 32; i += blockDim.x) {
+    const int kc = i >> 5, q = i & 31;
+    dst[i] = make_uint4(tile[q * stride + kc], tile[(q + 32) * stride + kc], tile[(q + 64) * stride + kc],
+                        tile[(q + 96) * stride + kc]);
+  }
+}
+
+int launch_swizzle_scales(const uint8_t* lin, const int* tile_prefix, const int* counts, const int* eoff, int E, int H,
+                          int64_t slots, uint8_t* sf, cudaStream_t s) {
+  if (slots == 0) return 0;
+  const int64_t max_tiles = slots / 128 + E + 1;
+  swizzle_scales_kernel<<<(unsigned)max_tiles, 256, 0, s>>>(lin, tile_prefix, counts, eoff, E, H, sf);
+  return 0;
 }
 
 // ------------------------------------------------------------------------------------------------------
@@ -496,10 +549,10 @@ int launch_plan(const int* seg_counts, int nseg, int E, int* seg_base, int* coun
 
 int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const int* seg_base,
                          const int* eoff, const int* boff, int m, int H, int E, int k, uint8_t* rep_fp4,
-                         uint8_t* rep_sf, int* c_map, cudaStream_t s) {
+                         uint8_t* lin_sf, int* c_map, cudaStream_t s) {
   const int nseg = (int)ceil_div64(m, kSegTokens);
   if (nseg > 0)
-    permute_quant_kernel<<<nseg, 256, 0, s>>>(a, a1_gscale, ids, seg_base, eoff, boff, m, H, E, k, rep_fp4, rep_sf,
+    permute_quant_kernel<<<nseg, 256, 0, s>>>(a, a1_gscale, ids, seg_base, eoff, boff, m, H, E, k, rep_fp4, lin_sf,
                                               c_map);
   return 0;
 }

@@ -11,9 +11,13 @@ int launch_route(const float* logits, const float* scale, int T, int E, int K, i
 int launch_count(const int* ids, int m, int k, int E, int* seg_counts, int* status, cudaStream_t s);
 int launch_plan(const int* seg_counts, int nseg, int E, int* seg_base, int* counts, int* eoff, int* boff,
                 int* tile_prefix, int* ps1, int* ps2, int n1, int k1, int n2, int k2, cudaStream_t s);
+// The permute kernels write scale bytes to a linear buffer lin_sf [slots, H/16]; launch_swizzle_scales then writes
+// the 128x4 atoms of every m-tile (needs the plan's tile_prefix / counts / expert_offsets).
 int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const int* seg_base,
                          const int* eoff, const int* boff, int m, int H, int E, int k, uint8_t* rep_fp4,
-                         uint8_t* rep_sf, int* c_map, cudaStream_t s);
+                         uint8_t* lin_sf, int* c_map, cudaStream_t s);
+int launch_swizzle_scales(const uint8_t* lin, const int* tile_prefix, const int* counts, const int* eoff, int E, int H,
+                          int64_t slots, uint8_t* sf, cudaStream_t s);
 int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
                    __nv_bfloat16* out, int num_sms, cudaStream_t s);
 int launch_quantize(const void* x, bool f32, int64_t rows, int cols, int group_rows, const float* gscale,
@@ -30,9 +34,8 @@ int launch_ep_pack(const __nv_bfloat16* a, const float* a1_gscale, const int* id
                    uint8_t* records, int* send_map, cudaStream_t s);
 int launch_ep_unpack_meta(const uint8_t* records, int n, int k, int H, int rec_bytes, int* lid, float* lw,
                           cudaStream_t s);
-int launch_ep_permute(const uint8_t* records, const int* lid, const int* seg_base, const int* eoff, const int* boff,
-                      int n, int H, int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* rep_sf, int* c_map,
-                      cudaStream_t s);
+int launch_ep_permute(const uint8_t* records, const int* lid, const int* seg_base, const int* eoff, int n, int H,
+                      int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, cudaStream_t s);
 int launch_ep_combine(const __nv_bfloat16* ret, const int* map, int m, int H, int k, __nv_bfloat16* out, int num_sms,
                       cudaStream_t s);
 

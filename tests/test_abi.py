@@ -39,7 +39,7 @@ def test_workspace_size_matches_layout():
     n = R.workspace_size(m, H, I, E, k)
     slots = m * k
     sfblk = slots // 128 + E + 1
-    expect_min = slots * (H // 2 + I // 2 + 2 * H + 4) + sfblk * (H // 64 + I // 64) * 512
+    expect_min = slots * (H // 2 + H // 16 + I // 2 + 2 * H + 4) + sfblk * (H // 64 + I // 64) * 512
     assert expect_min <= n <= expect_min + 64 * 1024 + 2 * ((m + 127) // 128) * E * 4 + 4096
 
 
