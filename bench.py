@@ -9,8 +9,8 @@ inter 704, 32 packed sequences of lengths U[256, 2048], ~37k tokens) on one B200
 data of that shape (activations N(0,1) bf16, weights N(0,0.02) quantised to NVFP4 on the device).
 
 `value` times the kernels with the inputs resident in HBM (CUDA events, max over ranks); `e2e` times the public
-API call (reax_engine_b200.route + run_moe_nvfp4) with pinned host inputs copied in and the output copied back
-every step. `--impl reference` times the reference path's CPU restatement (oracle/moe_oracle.py, numpy) on the
+API for host-resident batches (reax_engine_b200.HostStreamedMoE: route + run_moe_nvfp4 per token chunk) with the
+pinned host inputs copied in and the output copied back every step, the copies overlapped with the layer. `--impl reference` times the reference path's CPU restatement (oracle/moe_oracle.py, numpy) on the
 host cores on a bounded token sample. With torchrun (N > 1) each rank runs the expert-parallel layer
 (reax_engine_b200.ep) on its own 65,536-token batch.
 """
@@ -31,6 +31,7 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
+E2E_CHUNK = 8192   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
 NOMINAL_FP4_TFLOPS = 9000.0
 
 
@@ -306,17 +307,12 @@ def run_ours(args, wl: dict) -> None:
         x_h = inp["x"].cpu().pin_memory()
         lg_h = inp["logits"].cpu().pin_memory()
         out_h = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-        x_d = torch.empty_like(inp["x"])
-        lg_d = torch.empty_like(inp["logits"])
+        host_layer = R.HostStreamedMoE(H, I, E, k, wl["act"], inp["a1_gscale"], inp["w1p"], inp["w1p_sf"],
+                                       inp["w1_alphas"], inp["a2_gscale"], inp["w2q"], inp["w2sx"], inp["w2_alphas"],
+                                       dev, chunk_tokens=E2E_CHUNK)
 
         def e2e_step():
-            x_d.copy_(x_h, non_blocking=True)
-            lg_d.copy_(lg_h, non_blocking=True)
-            w, ids = R.route(None, lg_d, k)
-            R.run_moe_nvfp4(out, x_d, inp["a1_gscale"], inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"],
-                            inp["w2q"], inp["w2sx"], inp["w2_alphas"], w, ids, wl["act"], w1_prepacked=True,
-                            w2_prepacked=True)
-            out_h.copy_(out, non_blocking=True)
+            host_layer(x_h, lg_h, out_h)
 
         for _ in range(args.warmup):
             e2e_step()
@@ -378,7 +374,9 @@ def run_ours(args, wl: dict) -> None:
                                                   inp["w2s"].numel()) / 1e6)),
                 e2e=None if e2e_value is None else dict(
                     value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * H * 2 + T * E * 4,
-                    d2h_bytes_per_step=T * H * 2),
+                    d2h_bytes_per_step=T * H * 2,
+                    api=f"reax_engine_b200.HostStreamedMoE: pinned host x + logits in, output out, {E2E_CHUNK}-token "
+                        "chunks with the copies overlapped with route + run_moe_nvfp4"),
                 gpu_launches=launches_per_step * args.steps, roofline=roof, layer=layer, kernels=kernels,
                 cpu_baseline=cpu, clocks=clk.summary())
     if rank == 0:
