@@ -31,7 +31,7 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
-E2E_CHUNK = 8192   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
+E2E_CHUNK = 4096   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
 NOMINAL_FP4_TFLOPS = 9000.0
 
 
