@@ -422,7 +422,8 @@ def run_ours_ep(args, wl: dict) -> None:
     for key in ("w1q", "w1s", "w2q", "w2s", "w1p", "w1p_sf", "w2sx"):
         inp.pop(key)
     torch.cuda.empty_cache()
-    layer = R.ep.ExpertParallelMoE(H, I, E, k, wl["act"], inp["a1_gscale"], local_w)
+    layer = R.ep.ExpertParallelMoE(H, I, E, k, wl["act"], inp["a1_gscale"], local_w,
+                                   **({} if args.ep_chunks is None else {"chunks": args.ep_chunks}))
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     s = torch.cuda.current_stream(dev)
 
@@ -523,7 +524,7 @@ def run_ours_ep(args, wl: dict) -> None:
                 ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
                 data="synthetic",
                 config=dict(workload=wl["name"], tokens_per_rank=T, hidden=H, experts=E, topk=k, inter=I,
-                            activation=wl["act"], parallelism=f"ep{world}", experts_per_rank=El,
+                            activation=wl["act"], parallelism=f"ep{world}", experts_per_rank=El, ep_chunks=layer.chunks,
                             l2="inputs larger than L2 (x %.0f MB per rank, local weights %.0f MB); no flush" % (
                                 T * H * 2 / 1e6, weight_bytes / 1e6)),
                 e2e=None if e2e_value is None else dict(
@@ -551,6 +552,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count (profiling)")
+    ap.add_argument("--ep-chunks", type=int, default=None, help="expert-parallel token parts in flight (N > 1)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     wl = workload(args.workload or ("cfg4" if world > 1 else "cfg2"))

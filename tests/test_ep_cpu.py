@@ -134,14 +134,14 @@ class OracleOps:
         self.El = c["E"] // ranks
         self.wc = {}
 
-    def dispatch(self, a, a1_gscale, topk_ids, topk_weights):
+    def dispatch(self, a, a1_gscale, topk_ids, topk_weights, slot=0):
         c = self.c
         d = O.ep_dispatch(a.float().numpy(), topk_ids.numpy(), topk_weights.numpy(), a1_gscale.numpy(), c["E"],
                           self.ranks)
         return (torch.from_numpy(d["send_counts"]), torch.from_numpy(d["send_map"]),
                 torch.from_numpy(d["records"]))
 
-    def expert_forward(self, records, n, local):
+    def expert_forward(self, records, n, local, slot=0):
         c = self.c
         sl = slice(self.rank * self.El, (self.rank + 1) * self.El)
         part = O.ep_expert_forward(records[:n].numpy(), c["H"], c["k"], c["w1q"][sl], c["w1s"][sl],
@@ -153,18 +153,39 @@ class OracleOps:
         output.copy_(torch.from_numpy(O.ep_combine(send_map.numpy(), returned.float().numpy())).bfloat16())
 
 
-def _worker(rank, ranks, port, Ts, local_only, errq):
+def _chunk_bounds(T, n):
+    step = -(-T // n) if T else 0
+    return [(min(T, c * step), min(T, (c + 1) * step)) for c in range(n)]
+
+
+def _chunked_reference(c, ranks, chunks, rank):
+    """The oracle's EP layer run part by part with the same token split as ExpertParallelMoE (so the oracle's
+    per-part expert GEMMs see the same rows)."""
+    outs = []
+    bounds = [_chunk_bounds(x.shape[0], chunks) for x in c["xs"]]
+    for p in range(chunks):
+        sub = dict(c)
+        sub["xs"] = [c["xs"][r][bounds[r][p][0]:bounds[r][p][1]] for r in range(ranks)]
+        sub["ids"] = [c["ids"][r][bounds[r][p][0]:bounds[r][p][1]] for r in range(ranks)]
+        sub["ws"] = [c["ws"][r][bounds[r][p][0]:bounds[r][p][1]] for r in range(ranks)]
+        outs.append(ep_layer(sub, ranks, {})[rank])
+    return np.concatenate(outs, axis=0)
+
+
+def _worker(rank, ranks, port, Ts, local_only, chunks, errq):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=ranks)
         c = oracle_case(Ts, local_only=local_only)
         layer = EP.ExpertParallelMoE(c["H"], c["I"], c["E"], c["k"], "gelu_tanh", torch.from_numpy(c["a1_gscale"]),
-                                     local=None, ops=OracleOps(c, rank, ranks))
+                                     local=None, ops=OracleOps(c, rank, ranks), chunks=chunks)
         x = torch.from_numpy(c["xs"][rank]).bfloat16()
         out = layer(x, torch.from_numpy(c["ws"][rank]), torch.from_numpy(c["ids"][rank]))
-        ref = ep_layer(c, ranks, {})[rank]
+        ref = _chunked_reference(c, ranks, chunks, rank)
         assert np.array_equal(out.float().numpy(), ref), f"rank {rank}: exchange result differs from the oracle"
+        from moe_cases import tol_check
+        tol_check(out.float().numpy(), ep_layer(c, ranks, {})[rank])    # and the unsplit layer, within tolerance
         send, recv = layer.last_counts
         # the counts each rank sends equal what the peers receive
         allsend = [None] * ranks
@@ -183,10 +204,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("Ts,local_only", [([37, 29], None), ([41, 0], None), ([48, 20], (0, 2))])
-def test_expert_parallel_exchange_gloo_world2(Ts, local_only):
+@pytest.mark.parametrize("Ts,local_only,chunks", [([37, 29], None, 1), ([37, 29], None, 3), ([41, 0], None, 2),
+                                                   ([48, 20], (0, 2), 4)])
+def test_expert_parallel_exchange_gloo_world2(Ts, local_only, chunks):
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
-    mp.start_processes(_worker, args=(2, _free_port(), Ts, local_only, errq), nprocs=2, join=True,
+    mp.start_processes(_worker, args=(2, _free_port(), Ts, local_only, chunks, errq), nprocs=2, join=True,
                        start_method="spawn")
     assert errq.empty(), errq.get()
