@@ -10,8 +10,9 @@ data of that shape (activations N(0,1) bf16, weights N(0,0.02) quantised to NVFP
 
 `value` times the kernels with the inputs resident in HBM (CUDA events, max over ranks); `e2e` times the public
 API for host-resident batches (reax_engine_b200.HostStreamedMoE: route + run_moe_nvfp4 per token chunk) with the
-pinned host inputs copied in and the output copied back every step, the copies overlapped with the layer. `--impl reference` times the reference path's CPU restatement (oracle/moe_oracle.py, numpy) on the
-host cores on a bounded token sample. With torchrun (N > 1) each rank runs the expert-parallel layer
+pinned host inputs copied in and the output copied back every step, the copies overlapped with the layer.
+`--impl reference` times the reference path's CPU restatement (oracle/moe_oracle.py, numpy) on the host cores on a
+bounded token sample. With torchrun (N > 1) each rank runs the expert-parallel layer
 (reax_engine_b200.ep) on its own 65,536-token batch.
 """
 from __future__ import annotations
@@ -33,6 +34,10 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
 E2E_CHUNK = 4096   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
 NOMINAL_FP4_TFLOPS = 9000.0
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
+# workload summarised in profiles/dram_traffic_cfg2.md; None where no capture covers the workload.
+NCU_TRAFFIC = {"cfg2": {"gemm_w13": 957_964_000, "gemm_w2": 1_868_524_000, "permute_quant": 602_162_000,
+                        "combine": 1_792_187_000}}
 
 
 def load_peaks() -> dict:
@@ -50,7 +55,7 @@ def workload(name: str):
     if name == "cfg2":
         lens = packed_lengths(32, 256, 2048, seed=0)
         return dict(name="cfg2: 26B-A4B-shaped MoE layer, 32 packed seqs U[256,2048]", T=sum(lens), H=2816, E=128,
-                    k=8, I=704, act="gelu_tanh", skew=None, lens=lens)
+                    k=8, I=704, act="gelu_tanh", skew=None, lens=lens, key="cfg2")
     if name == "cfg1":
         lens = [64, 96, 160, 192]
         return dict(name="cfg1: H2048 E64 top4 I1024 SiLU, 4 packed seqs", T=512, H=2048, E=64, k=4, I=1024,
@@ -350,7 +355,8 @@ def run_ours(args, wl: dict) -> None:
     dom = max(names, key=lambda n: per_ms[n])
     kd = kernels[dom]
     roof = dict(kernel=dom, bound="tensor" if dom in flops else "hbm", achieved=kd["achieved"],
-                peak=fp4_peak if dom in flops else peaks["hbm_gbs"], unit=kd["unit"], frac=kd["frac"], traffic=None,
+                peak=fp4_peak if dom in flops else peaks["hbm_gbs"], unit=kd["unit"], frac=kd["frac"],
+                traffic=NCU_TRAFFIC.get(wl.get("key"), {}).get(dom),
                 peak_basis=("4 x measured cuBLAS bf16 dense (nominal dense FP4:BF16 = 4:1; "
                             f"{peaks['source']} bf16 {peaks['bf16']} TFLOP/s), nominal FP4 9000")
                 if dom in flops else f"{peaks['source']} HBM copy bandwidth")
@@ -363,7 +369,7 @@ def run_ours(args, wl: dict) -> None:
         rate, n, t = cpu_sample(wl, cpu_in, args.cpu_tokens)
         cpu = dict(value=rate, unit="tokens/s", cores=os.cpu_count(), kind="port",
                    sample=f"first {n} tokens of the workload, numpy oracle, {t:.2f} s")
-    launches_per_step = 7   # route, count, plan, permute_quant, gemm_w13, gemm_w2, combine
+    launches_per_step = 8   # route, count, plan, permute_quant, swizzle_scales, gemm_w13, gemm_w2, combine
     line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
                 ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
                 data="synthetic",
@@ -519,7 +525,9 @@ def run_ours_ep(args, wl: dict) -> None:
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
         e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
 
-    launches_per_step = 13   # route; dispatch 4; expert forward 7 (unpack, count, plan, permute, w13, w2, combine); combine
+    # route; dispatch 4 (rank ids, count, plan, pack); expert forward 8 (unpack, count, plan, permute, swizzle, w13,
+    # w2, combine); combine -- per token part
+    launches_per_step = 1 + 13 * layer.chunks
     line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
                 ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
                 data="synthetic",
@@ -557,7 +565,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     wl = workload(args.workload or ("cfg4" if world > 1 else "cfg2"))
     if args.tokens is not None:
-        wl = dict(wl, T=args.tokens, name=wl["name"] + f" [tokens overridden to {args.tokens}]")
+        wl = dict(wl, T=args.tokens, name=wl["name"] + f" [tokens overridden to {args.tokens}]", key=None)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
