@@ -335,6 +335,31 @@ def run_ours(args, wl: dict) -> None:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
         e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
 
+    # ---- the fused Gemma-4 router + top-k (reax_engine_b200.router_topk) on the same x: outside the step, whose
+    # metric starts from router logits; one launch at a time, L2 flushed before each
+    router = None
+    if world == 1 and not args.no_router and inp["gate"] is not None:
+        rw = inp["gate"].bfloat16()
+        rs = torch.ones(H, dtype=torch.bfloat16, device=dev)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        for _ in range(3):
+            R.router_topk(inp["x"], rs, rw, k)
+        rts = []
+        for _ in range(10):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            R.router_topk(inp["x"], rs, rw, k)
+            b.record(s)
+            torch.cuda.synchronize(dev)
+            rts.append(a.elapsed_time(b))
+        r_ms = statistics.median(rts)
+        r_bytes = T * H * 2 + E * H * 2 + T * k * 8
+        router = dict(us=r_ms * 1000.0, bytes=r_bytes, achieved=r_bytes / (r_ms / 1000.0) / 1e9, unit="GB/s",
+                      bound="hbm", note="x read from HBM once, re-read from L2 once; weight re-read from L2 per "
+                                        "128-token tile")
+        del flush
+
     # ---- roofline of the dominant kernel and per-kernel figures
     peaks = load_peaks()
     slots = T * k
@@ -360,6 +385,8 @@ def run_ours(args, wl: dict) -> None:
                 peak_basis=("4 x measured cuBLAS bf16 dense (nominal dense FP4:BF16 = 4:1; "
                             f"{peaks['source']} bf16 {peaks['bf16']} TFLOP/s), nominal FP4 9000")
                 if dom in flops else f"{peaks['source']} HBM copy bandwidth")
+    if router is not None:
+        router["frac"] = router["achieved"] / peaks["hbm_gbs"]
     layer_flop = flops["gemm_w13"] + flops["gemm_w2"]
     layer = dict(tflops=layer_flop / (ms_step / 1000.0) / 1e12,
                  frac_fp4=layer_flop / (ms_step / 1000.0) / 1e12 / fp4_peak)
@@ -384,6 +411,7 @@ def run_ours(args, wl: dict) -> None:
                     api=f"reax_engine_b200.HostStreamedMoE: pinned host x + logits in, output out, {E2E_CHUNK}-token "
                         "chunks with the copies overlapped with route + run_moe_nvfp4"),
                 gpu_launches=launches_per_step * args.steps, roofline=roof, layer=layer, kernels=kernels,
+                router_topk=router,
                 cpu_baseline=cpu, clocks=clk.summary())
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -559,6 +587,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--no-router", action="store_true", help="skip the fused router measurement (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count (profiling)")
     ap.add_argument("--ep-chunks", type=int, default=None, help="expert-parallel token parts in flight (N > 1)")
     args = ap.parse_args()

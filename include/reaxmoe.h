@@ -14,6 +14,8 @@
  *     vllm/model_executor/layers/fused_moe/experts/cutlass_moe.py:481-664)      -> reaxmoe_forward
  *   - Gemma-4 routing function (vllm/model_executor/models/gemma4.py:95-203, called from
  *     gemma4.py:332-345)                                                          -> reaxmoe_route
+ *   - Gemma4Router.forward (gemma4.py:251-298; champion router GEMM blink_rgemm.cu:44-56) + the routing
+ *     function, fused                                                             -> reaxmoe_router_topk
  *   - get_cutlass_moe_mm_data / blink _fplan (champions/uid240/opt/blink/blink_moe.py:271-299)
  *                                                                                 -> reaxmoe_plan
  *   - scaled_fp4_experts_quant of the m rows + _tscatter (blink_moe.py:301-323, :402-421)
@@ -102,6 +104,19 @@ int reaxmoe_forward(const reaxmoe_forward_args* args, void* workspace, size_t wo
  * ids [tokens, topk] int32; weights [tokens, topk] fp32. (gemma4.py:183-203) */
 int reaxmoe_route(const float* logits, const float* per_expert_scale, int32_t tokens, int32_t experts,
                   int32_t topk, int32_t* topk_ids, float* topk_weights, void* stream);
+
+/* Gemma-4 router fused with its routing (Gemma4Router.forward, vllm/model_executor/models/gemma4.py:251-298, as the
+ * champion's router GEMM champions/uid240/opt/blink/blink_rgemm.cu:44-56 runs it, followed by gemma4.py:183-203):
+ * u = bf16(bf16(bf16(rmsnorm(x)) * bf16(hidden^-1/2)) * router_scale) with rmsnorm = x * rsqrt(mean(x^2) + eps) in
+ * fp32 (no weight; vllm/ir/ops/layernorm.py:10-21), logits = u . router_weight^T (bf16 products, fp32 accumulation
+ * on the tensor cores), then top-k and weights exactly as reaxmoe_route from those logits. The logits stay on chip;
+ * pass a [tokens, experts] fp32 buffer as `logits` to also store them (NULL: not stored). hidden_states [tokens,
+ * hidden] bf16; router_scale [hidden] bf16; router_weight [experts, hidden] bf16; experts 32, 64 or 128; hidden % 128
+ * == 0, <= 3072. `status` (NULL-able) receives REAXMOE_ERR_DEVICE_TIMEOUT if a bounded device wait expires. */
+int reaxmoe_router_topk(const void* hidden_states, const void* router_scale, const void* router_weight,
+                        const float* per_expert_scale, float eps, int32_t tokens, int32_t hidden, int32_t experts,
+                        int32_t topk, int32_t* topk_ids, float* topk_weights, float* logits, int32_t* status,
+                        void* stream);
 
 /* Routing data (get_cutlass_moe_mm_data; blink_moe.py:271-299). Writes, inside the workspace, the per-expert
  * counts, expert_offsets[E+1], blockscale_offsets[E+1] and GEMM tile tables, and copies them out to the

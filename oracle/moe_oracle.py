@@ -9,7 +9,8 @@ It restates, in numpy, the reference's arithmetic for the path:
 * NVFP4 quantisation and the 128x4 swizzled scale layout: ``engine/fp4.py:11-52`` and the
   static-scale Triton quantiser ``engine/fp4_triton.py:16-40`` (same numerics: IEEE division).
 * Gemma-4 routing: vLLM ``model_executor/models/gemma4.py:183-203`` (torch form; softmax over all
-  experts, top-k on logits, renormalise, x per_expert_scale).
+  experts, top-k on logits, renormalise, x per_expert_scale), and the router that makes its logits,
+  ``Gemma4Router.forward`` (``gemma4.py:251-298``).
 * Routing data: vLLM ``get_cutlass_moe_mm_data`` (expert offsets, 128-row block-scale offsets,
   problem sizes), restated in ``champions/uid240/opt/blink/blink_moe.py:271-299`` (``_fplan``); the
   slot order inside an expert is token-major (the canonical stable order, where the reference's
@@ -205,6 +206,28 @@ def route(logits: np.ndarray, topk: int, per_expert_scale: np.ndarray | None = N
     w = (np.take_along_axis(gate, ids.astype(np.int64), 1) / renorm).astype(np.float32)
     w = (w * np.asarray(per_expert_scale, dtype=np.float32)[ids]).astype(np.float32)
     return w, ids
+
+
+def gemma4_router(x: np.ndarray, scale: np.ndarray, router_w: np.ndarray, eps: float = 1e-6):
+    """Gemma-4 router input and logits (vLLM ``Gemma4Router.forward``, ``models/gemma4.py:293-298``):
+    rmsnorm without weight in fp32 and cast to bf16 (``vllm/ir/ops/layernorm.py:13-21``), times
+    bf16(hidden^-1/2) (``gemma4.py:277-281``: an fp32 tensor cast to bf16) and times bf16(scale), each product
+    rounded to bf16; then the bf16 x bf16 -> fp32 projection (``GateLinear`` with ``out_dtype=float32``,
+    ``fused_moe/router/gate_linear.py``: ``torch.mm(x, W.T, out_dtype=float32)`` on Hopper / Blackwell).
+    ``x`` [T, H], ``scale`` [H], ``router_w`` [E, H] are bf16 values as floats. The mean square is summed in
+    float64 and rounded once (torch's fp32 reduction order is unspecified); the logits are the float64 sums of the
+    exact bf16 products rounded once to fp32. Returns (u [T, H] float32 holding bf16 values, logits [T, E])."""
+    x = np.asarray(x, dtype=np.float32)
+    T, H = x.shape
+    var = np.float32((x.astype(np.float64) ** 2).mean(axis=1, keepdims=True))
+    r = (1.0 / np.sqrt((var + np.float32(eps)).astype(np.float32).astype(np.float64))).astype(np.float32)
+    n = bf16_round((x * r).astype(np.float32))
+    root = bf16_round(np.float32(float(H) ** -0.5))
+    u = bf16_round((n * root).astype(np.float32))
+    u = bf16_round((u * bf16_round(np.asarray(scale, dtype=np.float32))[None, :]).astype(np.float32))
+    w = bf16_round(np.asarray(router_w, dtype=np.float32)).astype(np.float64)
+    logits = (u.astype(np.float64) @ w.T).astype(np.float32)
+    return u, logits
 
 
 def plan(ids: np.ndarray, num_experts: int) -> dict:

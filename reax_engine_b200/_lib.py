@@ -58,6 +58,8 @@ SIGNATURES = {
     "reaxmoe_workspace_size": (ctypes.c_size_t, [_PP]),
     "reaxmoe_forward": (ctypes.c_int, [ctypes.POINTER(ForwardArgs), _P, ctypes.c_size_t, _P]),
     "reaxmoe_route": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P]),
+    "reaxmoe_router_topk": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, _I32, _I32, _I32, _I32, _P, _P, _P, _P,
+                                           _P]),
     "reaxmoe_plan": (ctypes.c_int, [_PP, _P, _P, ctypes.c_size_t, _P, _P, _P, _P, _P]),
     "reaxmoe_permute_quant": (ctypes.c_int, [_PP, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P, _P]),
     "reaxmoe_gemm_w13": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P]),

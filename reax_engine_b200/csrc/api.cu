@@ -293,6 +293,46 @@ int reaxmoe_route(const float* logits, const float* per_expert_scale, int32_t to
   return cuda_check("route");
 }
 
+int reaxmoe_router_topk(const void* hidden_states, const void* router_scale, const void* router_weight,
+                        const float* per_expert_scale, float eps, int32_t tokens, int32_t hidden, int32_t experts,
+                        int32_t topk, int32_t* topk_ids, float* topk_weights, float* logits, int32_t* status,
+                        void* stream) {
+  if (experts != 32 && experts != 64 && experts != 128)
+    return fail(REAXMOE_ERR_UNSUPPORTED, "router_topk: experts=%d (32, 64 or 128)", experts);
+  if (topk < 1 || topk > kMaxTopk || topk > experts)
+    return fail(REAXMOE_ERR_TOO_MANY_EXPERTS, "router_topk: topk=%d outside [1, min(%d, experts)]", topk, kMaxTopk);
+  if (hidden < 128 || hidden > 3072 || hidden % 128 != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "router_topk: hidden=%d must be a multiple of 128 in [128, 3072]", hidden);
+  if (tokens < 0) return fail(REAXMOE_ERR_BAD_SHAPE, "router_topk: tokens=%d < 0", tokens);
+  if (tokens == 0) return 0;
+  if (!hidden_states || !router_scale || !router_weight || !topk_ids || !topk_weights)
+    return fail(REAXMOE_ERR_NULL, "router_topk: NULL pointer");
+  if (!aligned16(hidden_states) || !aligned16(router_weight) || (logits != nullptr && !aligned16(logits)))
+    return fail(REAXMOE_ERR_MISALIGNED, "router_topk: hidden_states, router_weight and logits must be 16-byte aligned");
+  RouterLaunch r;
+  memset(&r, 0, sizeof(r));
+  r.x = hidden_states;
+  r.scale = router_scale;
+  r.w = router_weight;
+  r.pes = per_expert_scale;
+  // the reference multiplies by root_size.to(bf16), root_size = torch.tensor(hidden**-0.5) (fp32)
+  r.root = __bfloat162float(__float2bfloat16_rn((float)(1.0 / sqrt((double)hidden))));
+  r.eps = eps;
+  r.T = tokens;
+  r.H = hidden;
+  r.E = experts;
+  r.K = topk;
+  r.ids = topk_ids;
+  r.wts = topk_weights;
+  r.logits = logits;
+  r.status = status;
+  r.timeout_ns = device_timeout_ns();
+  r.num_sms = num_sms();
+  const int rc = launch_router_topk(r, static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "router_topk launch failed: %s", cudaGetErrorString(cudaPeekAtLastError()));
+  return cuda_check("router_topk");
+}
+
 int reaxmoe_plan(const reaxmoe_problem* p, const int32_t* topk_ids, void* workspace, size_t workspace_bytes,
                  int32_t* expert_offsets, int32_t* blockscale_offsets, int32_t* problem_sizes1,
                  int32_t* problem_sizes2, void* stream) {

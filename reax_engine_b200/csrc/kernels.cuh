@@ -61,4 +61,22 @@ struct GemmLaunch {
 };
 int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s);
 
+// Fused Gemma-4 router + top-k (router_sm100.cu).
+struct RouterLaunch {
+  const void* x;       // [T, H] bf16
+  const void* scale;   // [H] bf16 learned router input scale
+  const void* w;       // [E, H] bf16 router weight
+  const float* pes;    // [E] per-expert scale of the routing weights, or null
+  float root;          // bf16(H^-1/2) as a float
+  float eps;
+  int T, H, E, K;
+  int* ids;            // [T, K]
+  float* wts;          // [T, K]
+  float* logits;       // optional [T, E] fp32
+  int* status;
+  unsigned long long timeout_ns;
+  int num_sms;         // the persistent grid's upper bound
+};
+int launch_router_topk(const RouterLaunch& r, cudaStream_t s);
+
 }  // namespace reaxmoe

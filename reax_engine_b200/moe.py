@@ -75,6 +75,31 @@ def route(hidden_states: torch.Tensor | None, gating_output: torch.Tensor, topk:
     return w, ids
 
 
+def router_topk(hidden_states: torch.Tensor, router_scale: torch.Tensor, router_weight: torch.Tensor, topk: int,
+                eps: float = 1e-6, per_expert_scale: torch.Tensor | None = None, return_logits: bool = False,
+                status: torch.Tensor | None = None):
+    """Gemma-4 router fused with its routing (vLLM ``Gemma4Router.forward``, ``models/gemma4.py:251-298``, then the
+    routing function): rmsnorm (no weight) -> x hidden^-1/2 -> x router_scale -> logits = . router_weight^T (fp32)
+    -> top-k and renormalised weights. The logits never leave the chip unless ``return_logits``.
+    Returns (topk_weights fp32 [T, k], topk_ids int32 [T, k]) [+ logits fp32 [T, E]]. ``status``: an optional int32
+    device tensor that receives a device-timeout code."""
+    _require_cuda(hidden_states, router_scale, router_weight)
+    x = hidden_states.contiguous()
+    assert x.dtype == torch.bfloat16, "hidden_states must be bf16"
+    T, H = x.shape
+    E = router_weight.shape[0]
+    sc = router_scale.to(torch.bfloat16).contiguous()
+    w = router_weight.to(torch.bfloat16).contiguous()
+    ids = torch.empty(T, topk, dtype=torch.int32, device=x.device)
+    wts = torch.empty(T, topk, dtype=torch.float32, device=x.device)
+    logits = torch.empty(T, E, dtype=torch.float32, device=x.device) if return_logits else None
+    pes = None if per_expert_scale is None else per_expert_scale.contiguous().float()
+    L.check(L.lib().reaxmoe_router_topk(x.data_ptr(), sc.data_ptr(), w.data_ptr(), _ptr(pes), float(eps), T, H, E,
+                                        topk, ids.data_ptr(), wts.data_ptr(), _ptr(logits), _ptr(status),
+                                        _stream(x.device)))
+    return (wts, ids, logits) if return_logits else (wts, ids)
+
+
 # ---------------------------------------------------------------------------------------------------- NVFP4
 
 def quantize_nvfp4(x: torch.Tensor, gscale: torch.Tensor, group_rows: int | None = None):

@@ -12,6 +12,9 @@ What it runs, and what each fixture pins:
 * ``e4m3_golden.npz``   -- torch's float32 -> float8_e4m3fn conversion (used by ``engine/fp4.py:47``).
 * ``route_golden.npz``  -- vLLM ``gemma4_routing_function_torch`` (``models/gemma4.py:183-203``), the
   Gemma-4 routing semantics the reference's MoE models run.
+* ``router_golden.npz`` -- vLLM's ``Gemma4Router`` module (``models/gemma4.py:251-298``): its projection
+  input (rmsnorm without weight, x hidden^-1/2, x scale, in vLLM's own code), the exact fp32 logits of that
+  input, and vLLM's routing of them.
 * ``layer_golden.npz``  -- a small MoE layer composed on CPU from the reference's pieces: weights and
   activations quantised by ``engine/fp4.py``, routing by vLLM's torch function, and the stock
   ``run_cutlass_moe_fp4`` arithmetic (vLLM ``fused_moe/experts/cutlass_moe.py:562-664``: bf16 GEMM
@@ -185,13 +188,63 @@ def layer_case(fp4, route_fn, activation: str, seed: int):
     }
 
 
+def router_cases(route_fn):
+    """vLLM's own Gemma4Router module (models/gemma4.py:251-298) run on CPU. Its CPU projection rounds the logits
+    to bf16 (GateLinear falls back to a bf16 linear there), so the fixture keeps the module's projection INPUT u
+    (captured by a forward hook: rmsnorm, root_size and scale, all vLLM's code) and the exact logits u . W^T
+    (float64 sums rounded once to fp32), which is what the fp32-output GEMM that GateLinear runs on Hopper /
+    Blackwell computes up to its fp32 accumulation order. ids / weights: vLLM's routing function on those logits."""
+    import types
+
+    from vllm.config import DeviceConfig, VllmConfig, set_current_vllm_config
+    from vllm.distributed import init_distributed_environment, initialize_model_parallel
+    from vllm.model_executor.models.gemma4 import Gemma4Router
+
+    out = {}
+    vc = VllmConfig(device_config=DeviceConfig(device="cpu"))
+    with set_current_vllm_config(vc):
+        init_distributed_environment(world_size=1, rank=0, distributed_init_method="tcp://127.0.0.1:29533",
+                                     local_rank=0, backend="gloo")
+        initialize_model_parallel(1, 1)
+        for name, (T, H, E, k, seed) in {"h256e32": (64, 256, 32, 4, 11), "h2816e128": (37, 2816, 128, 8, 12),
+                                         "h1024e64": (130, 1024, 64, 6, 13)}.items():
+            gen = torch.Generator().manual_seed(seed)
+            cfg = types.SimpleNamespace(hidden_size=H, rms_norm_eps=1e-6, num_experts=E)
+            mod = Gemma4Router(cfg).to(torch.bfloat16)
+            x = (torch.randn(T, H, generator=gen) * 3).bfloat16()
+            x[0] = 0.0                       # an all-zero row: rsqrt(eps), u = 0, all logits 0 (ties to low ids)
+            with torch.no_grad():
+                mod.scale.copy_((1 + 0.2 * torch.randn(H, generator=gen)).bfloat16())
+                mod.proj.weight.copy_((torch.randn(E, H, generator=gen) * 0.05).bfloat16())
+            seen = {}
+            hook = mod.proj.register_forward_pre_hook(lambda m, a: seen.__setitem__("u", a[0].detach().clone()))
+            with torch.no_grad():
+                mod(x)
+            hook.remove()
+            u = seen["u"]
+            assert u.dtype == torch.bfloat16
+            w = mod.proj.weight.detach()
+            logits = (u.double() @ w.double().t()).float()
+            pes = torch.rand(E, generator=gen) + 0.5
+            tw, tid = route_fn(logits, k, pes)
+            out.update({f"{name}_x": x.float().numpy(), f"{name}_scale": mod.scale.detach().float().numpy(),
+                        f"{name}_w": w.float().numpy(), f"{name}_u": u.float().numpy(),
+                        f"{name}_logits": logits.numpy(), f"{name}_pes": pes.numpy(),
+                        f"{name}_ids": tid.to(torch.int32).numpy(), f"{name}_wts": tw.float().numpy()})
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("REAX_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=["router"], default=None, help="regenerate one fixture file")
     args = ap.parse_args()
-    fp4 = load_fp4(args.reference)
     from vllm.model_executor.models.gemma4 import gemma4_routing_function_torch as route_fn
 
+    np.savez_compressed(os.path.join(HERE, "router_golden.npz"), **router_cases(route_fn))
+    if args.only == "router":
+        return
+    fp4 = load_fp4(args.reference)
     np.savez_compressed(os.path.join(HERE, "quant_golden.npz"), **quant_cases(fp4))
     np.savez_compressed(os.path.join(HERE, "e4m3_golden.npz"), **e4m3_cases())
     np.savez_compressed(os.path.join(HERE, "route_golden.npz"), **route_cases(route_fn))

@@ -83,6 +83,18 @@ def test_route_rejects_unsupported():
     assert lib.reaxmoe_route(None, None, 0, 128, 8, None, None, None) == L.OK
 
 
+def test_router_topk_rejects_unsupported():
+    lib = L.lib()
+    f = lib.reaxmoe_router_topk
+    assert f(None, None, None, None, 1e-6, 4, 2816, 48, 8, None, None, None, None, None) == L.ERR_UNSUPPORTED
+    assert f(None, None, None, None, 1e-6, 4, 2816, 128, 17, None, None, None, None, None) == L.ERR_TOO_MANY_EXPERTS
+    assert f(None, None, None, None, 1e-6, 4, 2816, 32, 33, None, None, None, None, None) == L.ERR_TOO_MANY_EXPERTS
+    assert f(None, None, None, None, 1e-6, 4, 2880, 128, 8, None, None, None, None, None) == L.ERR_BAD_SHAPE
+    assert f(None, None, None, None, 1e-6, 4, 3200, 128, 8, None, None, None, None, None) == L.ERR_BAD_SHAPE
+    assert f(None, None, None, None, 1e-6, 4, 2816, 128, 8, None, None, None, None, None) == L.ERR_NULL
+    assert f(None, None, None, None, 1e-6, 0, 2816, 128, 8, None, None, None, None, None) == L.OK
+
+
 def test_quantize_and_prepack_reject_bad_args():
     lib = L.lib()
     assert lib.reaxmoe_quantize(None, 0, 4, 100, 4, None, None, None, None) == L.ERR_BAD_SHAPE

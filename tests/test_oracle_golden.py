@@ -45,6 +45,25 @@ def test_route_matches_vllm_torch(name):
     np.testing.assert_allclose(w, d[f"{name}_w"], rtol=2e-6, atol=1e-7)
 
 
+ROUTER_CASES = ["h256e32", "h2816e128", "h1024e64"]
+
+
+@pytest.mark.parametrize("name", ROUTER_CASES)
+def test_router_matches_vllm_gemma4_router(name):
+    """The oracle's router input u (rmsnorm, x hidden^-1/2, x scale) equals what vLLM's Gemma4Router module feeds
+    its projection, bit for bit; the logits are the same exact sums. Routing agrees except on the all-zero row 0,
+    whose logits all tie: torch.topk returns tied experts in an unspecified order, the oracle in increasing id."""
+    d = load("router_golden.npz")
+    u, logits = O.gemma4_router(d[f"{name}_x"], d[f"{name}_scale"], d[f"{name}_w"], 1e-6)
+    assert np.array_equal(u, d[f"{name}_u"])
+    assert np.array_equal(logits, d[f"{name}_logits"])
+    k = d[f"{name}_ids"].shape[1]
+    w, ids = O.route(logits, k, d[f"{name}_pes"])
+    assert np.array_equal(ids[1:], d[f"{name}_ids"][1:])
+    np.testing.assert_allclose(w[1:], d[f"{name}_wts"][1:], rtol=2e-6, atol=1e-7)
+    assert (logits[0] == 0).all() and ids[0].tolist() == list(range(k))
+
+
 @pytest.mark.parametrize("act", ["gelu_tanh", "silu"])
 def test_layer_matches_reference_composition(act):
     d = load("layer_golden.npz")
@@ -82,3 +101,23 @@ def test_combine_order_top8():
     assert O.combine_order(8) == [[0, 4], [1, 5], [2, 6], [3, 7]]
     assert O.combine_order(4) == [[0], [1], [2], [3]]
     assert O.combine_order(2) == [[0], [1]]
+
+
+def test_router_mean_square_order_only_moves_rsqrt_by_an_ulp():
+    """The fused router kernel sums a row's squares in another fp32 order than the oracle (float64, rounded once);
+    in the few rows whose rsqrt moves by an ulp, u differs by at most 4 bf16 ulps in the elements that flip (one in
+    the rounding of x * r, carried through the two bf16 products after it)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("router_t", os.path.join(os.path.dirname(__file__),
+                                                                          "test_gpu_router.py"))
+    t = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(t)
+    rng = np.random.default_rng(3)
+    x = O.bf16_round((rng.standard_normal((512, 2816)) * rng.uniform(0.1, 10, (512, 1))).astype(np.float32))
+    sc = O.bf16_round((1 + 0.2 * rng.standard_normal(2816)).astype(np.float32))
+    uk = t.kernel_u(x, sc, 1e-6)
+    u, _ = O.gemma4_router(x, sc, np.zeros((32, 2816), np.float32), 1e-6)
+    d = uk != u
+    assert d.any(axis=1).mean() < 0.1
+    ulp = 2.0 ** (np.floor(np.log2(np.abs(u[d]))) - 7)
+    assert (np.abs(uk - u)[d] <= 4 * ulp).all()
