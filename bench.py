@@ -33,6 +33,7 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
 E2E_CHUNK = 4096   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
+DECISION_PROMPTS, DECISION_WARMUP, DECISION_STEPS = 64, 2, 3   # config 3 decision forward
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
 # workload summarised in profiles/dram_traffic_cfg2.md; None where no capture covers the workload.
@@ -170,6 +171,55 @@ def build_inputs(wl: dict, device, seed: int = 0):
     inp["w2sx"] = R.expand_scales(w2s, H, I)
     torch.cuda.synchronize(device)
     return inp
+
+
+def decision_leg(args, dev, world: int, rank: int) -> dict | None:
+    """the full prefill decision forward of a random-init 26B-A4B-shaped model
+    (reax_engine_b200.decision), 64 prompts of lengths U[512, 4096] per rank (seed = rank), option probabilities at
+    each prompt's last position. N GPUs run N replicas on their own batches; the time is the max over ranks."""
+    if args.no_decision:
+        return None
+    import torch
+    import torch.distributed as dist
+
+    from reax_engine_b200.decision import DecisionConfig, DecisionModel, synthetic_prompts
+    cfg = DecisionConfig()
+    t0 = time.perf_counter()
+    model = DecisionModel(cfg, dev, seed=0)
+    ids, cu = synthetic_prompts(DECISION_PROMPTS, 512, 4096, cfg.vocab, seed=rank, device=dev)
+    opts = torch.tensor([1000, 2000, 3000, 4000], device=dev)    # four fixed option-token ids
+    model.calibrate(ids, cu)
+    init_s = time.perf_counter() - t0
+    for _ in range(DECISION_WARMUP):
+        model.forward(ids, cu, opts)
+    torch.cuda.synchronize(dev)
+    s = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    a.record(s)
+    for _ in range(DECISION_STEPS):
+        p = model.forward(ids, cu, opts)
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([a.elapsed_time(b) / DECISION_STEPS], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    tokens = int(ids.numel())
+    out = dict(metric="decisions/s", value=world * DECISION_PROMPTS / (ms / 1000.0), unit="decisions/s",
+               ms_per_forward=ms, prompts_per_gpu=DECISION_PROMPTS, tokens_per_gpu=tokens,
+               prefill_tokens_per_s=world * tokens / (ms / 1000.0), steps=DECISION_STEPS, warmup=DECISION_WARMUP,
+               init_s=init_s, scaling="weak (replicas: one model and batch per GPU)",
+               config=dict(workload="cfg3", layers=cfg.layers, hidden=cfg.hidden, heads=cfg.heads,
+                           kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, window=cfg.window,
+                           pattern="alternating sliding / global", dense_inter=cfg.dense_inter, experts=cfg.experts,
+                           topk=cfg.topk, moe_inter=cfg.moe_inter, vocab=cfg.vocab, prompt_len="U[512,4096]"),
+               finite=bool(torch.isfinite(p).all().item()))
+    del model
+    torch.cuda.empty_cache()
+    return out
 
 
 def cpu_sample(wl: dict, inp_cpu: dict, n_tokens: int, reps: int = 1):
@@ -360,6 +410,8 @@ def run_ours(args, wl: dict) -> None:
                                         "128-token tile")
         del flush
 
+    decision = decision_leg(args, dev, world, rank)
+
     # ---- roofline of the dominant kernel and per-kernel figures
     peaks = load_peaks()
     slots = T * k
@@ -411,7 +463,7 @@ def run_ours(args, wl: dict) -> None:
                     api=f"reax_engine_b200.HostStreamedMoE: pinned host x + logits in, output out, {E2E_CHUNK}-token "
                         "chunks with the copies overlapped with route + run_moe_nvfp4"),
                 gpu_launches=launches_per_step * args.steps, roofline=roof, layer=layer, kernels=kernels,
-                router_topk=router,
+                router_topk=router, decision=decision,
                 cpu_baseline=cpu, clocks=clk.summary())
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -553,6 +605,8 @@ def run_ours_ep(args, wl: dict) -> None:
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
         e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
 
+    decision = decision_leg(args, dev, world, rank)
+
     # route; dispatch 4 (rank ids, count, plan, pack); expert forward 8 (unpack, count, plan, permute, swizzle, w13,
     # w2, combine); combine -- per token part
     launches_per_step = 1 + 13 * layer.chunks
@@ -570,7 +624,7 @@ def run_ours_ep(args, wl: dict) -> None:
                 phases_ms={n: v for n, v in phase_ms.items()},
                 exchange=dict(records_sent=send, records_received=recv, record_bytes=rec,
                               nvlink_bytes_per_direction=float(nvl.item())),
-                cpu_baseline=None, clocks=clk.summary())
+                decision=decision, cpu_baseline=None, clocks=clk.summary())
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -588,6 +642,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--no-router", action="store_true", help="skip the fused router measurement (profiling runs)")
+    ap.add_argument("--no-decision", action="store_true", help="skip the config-3 decision forward (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count (profiling)")
     ap.add_argument("--ep-chunks", type=int, default=None, help="expert-parallel token parts in flight (N > 1)")
     args = ap.parse_args()

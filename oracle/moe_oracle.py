@@ -208,6 +208,22 @@ def route(logits: np.ndarray, topk: int, per_expert_scale: np.ndarray | None = N
     return w, ids
 
 
+def route_weights(logits: np.ndarray, ids: np.ndarray, per_expert_scale: np.ndarray | None = None) -> np.ndarray:
+    """The Gemma-4 routing weights (``gemma4.py:183-203``, as in ``route``) for given expert ids: softmax over all
+    experts, taken at ``ids``, renormalised, times per_expert_scale[id]."""
+    logits = np.asarray(logits, dtype=np.float32)
+    ids = np.asarray(ids).astype(np.int64)
+    ex = np.exp(logits - logits.max(axis=1, keepdims=True)).astype(np.float32)
+    p = (ex / ex.sum(axis=1, keepdims=True, dtype=np.float32)).astype(np.float32)
+    g = np.take_along_axis(p, ids, 1)
+    renorm = g.sum(axis=1, keepdims=True, dtype=np.float32)
+    renorm = np.where(renorm > 0, renorm, np.float32(1.0)).astype(np.float32)
+    w = (g / renorm).astype(np.float32)
+    if per_expert_scale is not None:
+        w = (w * np.asarray(per_expert_scale, dtype=np.float32)[ids]).astype(np.float32)
+    return w
+
+
 def gemma4_router(x: np.ndarray, scale: np.ndarray, router_w: np.ndarray, eps: float = 1e-6):
     """Gemma-4 router input and logits (vLLM ``Gemma4Router.forward``, ``models/gemma4.py:293-298``):
     rmsnorm without weight in fp32 and cast to bf16 (``vllm/ir/ops/layernorm.py:13-21``), times
