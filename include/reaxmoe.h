@@ -16,6 +16,9 @@
  *     gemma4.py:332-345)                                                          -> reaxmoe_route
  *   - Gemma4Router.forward (gemma4.py:251-298; champion router GEMM blink_rgemm.cu:44-56) + the routing
  *     function, fused                                                             -> reaxmoe_router_topk
+ *   - the decision forward's element-wise steps around the MoE block (Gemma4DecoderLayer.forward, gemma4.py:696-771:
+ *     RMSNorm + bf16 adds, q/k/v norms + RoPE, GELU-tanh * up)  -> reaxmoe_rmsnorm, reaxmoe_qkv_norm_rope,
+ *                                                                    reaxmoe_gelu_tanh_mul
  *   - get_cutlass_moe_mm_data / blink _fplan (champions/uid240/opt/blink/blink_moe.py:271-299)
  *                                                                                 -> reaxmoe_plan
  *   - scaled_fp4_experts_quant of the m rows + _tscatter (blink_moe.py:301-323, :402-421)
@@ -117,6 +120,26 @@ int reaxmoe_router_topk(const void* hidden_states, const void* router_scale, con
                         const float* per_expert_scale, float eps, int32_t tokens, int32_t hidden, int32_t experts,
                         int32_t topk, int32_t* topk_ids, float* topk_weights, float* logits, int32_t* status,
                         void* stream);
+
+/* ---- The decision forward's fused element-wise steps (the Gemma-4 layer around the MoE block,
+ * vllm/model_executor/models/gemma4.py:696-771), each at vLLM's bf16 rounding points. All tensors bf16, contiguous,
+ * 16-byte aligned; stream-ordered.
+ *
+ * out = bf16(bf16(s * rsqrt(mean(s^2) + eps)) * weight) [+ residual] with s = bf16(a [+ b]) (vLLM rms_norm,
+ * vllm/ir/ops/layernorm.py:10-21, plus the bf16 adds around it). b, weight, residual may be NULL (weight NULL: no
+ * scale). rows x cols, cols a multiple of 256 and <= 4096. */
+int reaxmoe_rmsnorm(const void* a, const void* b, const void* weight, const void* residual, float eps, int64_t rows,
+                    int32_t cols, void* out, void* stream);
+/* qkv [tokens, (q_heads + 2 kv_heads) * head_dim] -> q [tokens, q_heads, head_dim], k, v [tokens, kv_heads,
+ * head_dim]: per-head RMSNorm of q and k with their weights [head_dim], of v without (Gemma4Attention.forward,
+ * gemma4.py:512-535), then NeoX rotate-half of q and k with bf16 tables cos / sin [max_position, head_dim / 2]
+ * indexed by positions [tokens] (int64), one bf16 rounding per operation (rotary_embedding/base.py). head_dim 64,
+ * 128 or 256. */
+int reaxmoe_qkv_norm_rope(const void* qkv, const void* q_weight, const void* k_weight, const void* cos_table,
+                          const void* sin_table, const int64_t* positions, float eps, int64_t tokens, int32_t q_heads,
+                          int32_t kv_heads, int32_t head_dim, void* q, void* k, void* v, void* stream);
+/* gate_up [rows, 2 inter] -> out [rows, inter] = bf16(bf16(gelu_tanh(gate)) * up) (GeluAndMul native form). */
+int reaxmoe_gelu_tanh_mul(const void* gate_up, int64_t rows, int32_t inter, void* out, void* stream);
 
 /* Routing data (get_cutlass_moe_mm_data; blink_moe.py:271-299). Writes, inside the workspace, the per-expert
  * counts, expert_offsets[E+1], blockscale_offsets[E+1] and GEMM tile tables, and copies them out to the

@@ -60,6 +60,10 @@ SIGNATURES = {
     "reaxmoe_route": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P]),
     "reaxmoe_router_topk": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, _I32, _I32, _I32, _I32, _P, _P, _P, _P,
                                            _P]),
+    "reaxmoe_rmsnorm": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, ctypes.c_int64, _I32, _P, _P]),
+    "reaxmoe_qkv_norm_rope": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, ctypes.c_float, ctypes.c_int64, _I32, _I32, _I32,
+                                             _P, _P, _P, _P]),
+    "reaxmoe_gelu_tanh_mul": (ctypes.c_int, [_P, ctypes.c_int64, _I32, _P, _P]),
     "reaxmoe_plan": (ctypes.c_int, [_PP, _P, _P, ctypes.c_size_t, _P, _P, _P, _P, _P]),
     "reaxmoe_permute_quant": (ctypes.c_int, [_PP, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P, _P]),
     "reaxmoe_gemm_w13": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P]),

@@ -333,6 +333,48 @@ int reaxmoe_router_topk(const void* hidden_states, const void* router_scale, con
   return cuda_check("router_topk");
 }
 
+int reaxmoe_rmsnorm(const void* a, const void* b, const void* weight, const void* residual, float eps, int64_t rows,
+                    int32_t cols, void* out, void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 256 != 0 || cols > 4096)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "rmsnorm: rows=%lld cols=%d (cols a multiple of 256, <= 4096)",
+                (long long)rows, cols);
+  if (rows == 0) return 0;
+  if (!a || !out) return fail(REAXMOE_ERR_NULL, "rmsnorm: NULL input or output");
+  if (!aligned16(a) || !aligned16(out) || (b && !aligned16(b)) || (weight && !aligned16(weight)) ||
+      (residual && !aligned16(residual)))
+    return fail(REAXMOE_ERR_MISALIGNED, "rmsnorm: tensors must be 16-byte aligned");
+  const int rc = launch_rmsnorm(a, b, weight, residual, eps, rows, cols, out, static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "rmsnorm launch failed: %s", cudaGetErrorString(cudaPeekAtLastError()));
+  return cuda_check("rmsnorm");
+}
+
+int reaxmoe_qkv_norm_rope(const void* qkv, const void* q_weight, const void* k_weight, const void* cos_table,
+                          const void* sin_table, const int64_t* positions, float eps, int64_t tokens, int32_t q_heads,
+                          int32_t kv_heads, int32_t head_dim, void* q, void* k, void* v, void* stream) {
+  if (tokens < 0 || q_heads <= 0 || kv_heads <= 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256))
+    return fail(REAXMOE_ERR_BAD_SHAPE, "qkv_norm_rope: tokens=%lld heads=%d/%d head_dim=%d (64, 128 or 256)",
+                (long long)tokens, q_heads, kv_heads, head_dim);
+  if (tokens == 0) return 0;
+  if (!qkv || !q_weight || !k_weight || !cos_table || !sin_table || !positions || !q || !k || !v)
+    return fail(REAXMOE_ERR_NULL, "qkv_norm_rope: NULL pointer");
+  const int rc = launch_qkv_norm_rope(qkv, q_weight, k_weight, cos_table, sin_table, positions, eps, tokens, q_heads,
+                                      kv_heads, head_dim, q, k, v, static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "qkv_norm_rope launch failed: %s", cudaGetErrorString(cudaPeekAtLastError()));
+  return cuda_check("qkv_norm_rope");
+}
+
+int reaxmoe_gelu_tanh_mul(const void* gate_up, int64_t rows, int32_t inter, void* out, void* stream) {
+  if (rows < 0 || inter <= 0 || inter % 8 != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "gelu_tanh_mul: rows=%lld inter=%d (a multiple of 8)", (long long)rows, inter);
+  if (rows == 0) return 0;
+  if (!gate_up || !out) return fail(REAXMOE_ERR_NULL, "gelu_tanh_mul: NULL pointer");
+  if (!aligned16(gate_up) || !aligned16(out))
+    return fail(REAXMOE_ERR_MISALIGNED, "gelu_tanh_mul: tensors must be 16-byte aligned");
+  const int rc = launch_gelu_tanh_mul(gate_up, rows, inter, out, static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "gelu_tanh_mul launch failed: %s", cudaGetErrorString(cudaPeekAtLastError()));
+  return cuda_check("gelu_tanh_mul");
+}
+
 int reaxmoe_plan(const reaxmoe_problem* p, const int32_t* topk_ids, void* workspace, size_t workspace_bytes,
                  int32_t* expert_offsets, int32_t* blockscale_offsets, int32_t* problem_sizes1,
                  int32_t* problem_sizes2, void* stream) {

@@ -1,0 +1,274 @@
+// decision_ops.cu -- the element-wise steps of the config-3 decision forward around the MoE block, fused so that each
+// reads its inputs and writes its output once (HBM-bound). Each reproduces, at the same bf16 rounding points, the vLLM
+// code it replaces:
+//   rmsnorm      out = bf16(bf16(s * rsqrt(mean(s^2) + eps)) * w) [+ residual], s = bf16(a [+ b])
+//                (vllm/ir/ops/layernorm.py:10-21; the sums and residual adds of Gemma4DecoderLayer.forward,
+//                vllm/model_executor/models/gemma4.py:696-771, are bf16 tensor adds)
+//   qkv_norm_rope  per head: RMSNorm of q and k with their learned weights, of v without (gemma4.py:512-535), then
+//                NeoX rotate-half of q and k with a bf16 cos / sin table, one bf16 rounding per operation
+//                (vllm/model_executor/layers/rotary_embedding/base.py forward_static)
+//   gelu_tanh_mul  h = bf16(bf16(gelu_tanh(gate)) * up) (GeluAndMul native form: F.gelu(approximate="tanh") on the
+//                bf16 gate, then a bf16 product; vllm/model_executor/layers/activation.py)
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace reaxmoe {
+namespace dops {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// bf16 add of two bf16 words (2 lanes each): fp32 sum rounded to bf16, as a torch bf16 tensor add
+__device__ __forceinline__ uint32_t bf2_add(uint32_t x, uint32_t y) {
+  const float lo = __uint_as_float(x << 16) + __uint_as_float(y << 16);
+  const float hi = __uint_as_float(x & 0xFFFF0000u) + __uint_as_float(y & 0xFFFF0000u);
+  return pack_bf16x2(lo, hi);
+}
+
+// One 128-thread CTA per row; thread i holds the 8-element pieces i, i + 128, ... (up to 4: cols <= 4096). Every input
+// of the row, the residual included, is loaded before the reduction, so a row costs one memory round trip.
+constexpr int RN_THREADS = 128;
+constexpr int RN_PIECES = 4;
+
+__global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const __nv_bfloat16* __restrict__ a,
+                                                             const __nv_bfloat16* __restrict__ b,
+                                                             const __nv_bfloat16* __restrict__ w,
+                                                             const __nv_bfloat16* __restrict__ res, float eps,
+                                                             int cols, __nv_bfloat16* __restrict__ out) {
+  __shared__ float part[RN_THREADS / 32];
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int pieces = cols >> 3;
+  const uint4* pa = reinterpret_cast<const uint4*>(a + row * cols);
+  const uint4* pb = b ? reinterpret_cast<const uint4*>(b + row * cols) : nullptr;
+  const uint4* pr = res ? reinterpret_cast<const uint4*>(res + row * cols) : nullptr;
+  uint4 s[RN_PIECES], rv[RN_PIECES];
+#pragma unroll
+  for (int j = 0; j < RN_PIECES; ++j) {
+    const int i = tid + j * RN_THREADS;
+    if (i < pieces) {
+      s[j] = __ldg(pa + i);
+      if (pb) {
+        const uint4 u = __ldg(pb + i);
+        s[j] = make_uint4(bf2_add(s[j].x, u.x), bf2_add(s[j].y, u.y), bf2_add(s[j].z, u.z), bf2_add(s[j].w, u.w));
+      }
+      if (pr) rv[j] = __ldg(pr + i);
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < RN_PIECES; ++j) {
+    if (tid + j * RN_THREADS < pieces) {
+      float f[8];
+      bf16x8_to_f32(s[j], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) part[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int k = 0; k < RN_THREADS / 32; ++k) tot += part[k];
+  const float r = rsqrtf(tot / (float)cols + eps);
+  const uint4* pw = w ? reinterpret_cast<const uint4*>(w) : nullptr;
+  uint4* po = reinterpret_cast<uint4*>(out + row * cols);
+#pragma unroll
+  for (int j = 0; j < RN_PIECES; ++j) {
+    const int i = tid + j * RN_THREADS;
+    if (i < pieces) {
+      float f[8];
+      bf16x8_to_f32(s[j], f);
+      float wf[8];
+      if (pw) bf16x8_to_f32(__ldg(pw + i), wf);
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float y0 = bf16r(f[2 * q] * r), y1 = bf16r(f[2 * q + 1] * r);
+        if (pw) {
+          y0 = bf16r(y0 * wf[2 * q]);        // bf16 x bf16: exact in fp32, one rounding
+          y1 = bf16r(y1 * wf[2 * q + 1]);
+        }
+        o[q] = pack_bf16x2(y0, y1);
+      }
+      uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+      if (pr) ov = make_uint4(bf2_add(ov.x, rv[j].x), bf2_add(ov.y, rv[j].y), bf2_add(ov.z, rv[j].z),
+                              bf2_add(ov.w, rv[j].w));
+      po[i] = ov;
+    }
+  }
+}
+
+// PER consecutive bf16 <-> floats with one vector access (PER = 2, 4 or 8; the address is PER*2-byte aligned)
+template <int PER>
+__device__ __forceinline__ void load_bf16(const __nv_bfloat16* p, float* f) {
+  uint32_t w[PER / 2];
+  if constexpr (PER == 8) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (PER == 4) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+  }
+#pragma unroll
+  for (int i = 0; i < PER / 2; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+template <int PER>
+__device__ __forceinline__ void store_bf16(__nv_bfloat16* p, const float* f) {
+  uint32_t w[PER / 2];
+#pragma unroll
+  for (int i = 0; i < PER / 2; ++i) w[i] = pack_bf16x2(f[2 * i], f[2 * i + 1]);
+  if constexpr (PER == 8) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else if constexpr (PER == 4) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+  } else {
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+  }
+}
+
+// One CTA per token, its warps taking the token's heads in turn; D / 32 elements per lane (D = 64, 128 or 256);
+// rotate-half partner of element i is i +- D/2, i.e. lane l +- 16.
+template <int D>
+__global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                            const __nv_bfloat16* __restrict__ qw,
+                                                            const __nv_bfloat16* __restrict__ kw,
+                                                            const __nv_bfloat16* __restrict__ cos_t,
+                                                            const __nv_bfloat16* __restrict__ sin_t,
+                                                            const int64_t* __restrict__ pos, float eps, int64_t n,
+                                                            int hq, int hk, __nv_bfloat16* __restrict__ q,
+                                                            __nv_bfloat16* __restrict__ k,
+                                                            __nv_bfloat16* __restrict__ v) {
+  constexpr int PER = D / 32;                        // elements per lane
+  const int lane = threadIdx.x & 31;
+  const int heads = hq + 2 * hk;
+  const int64_t t = blockIdx.x;
+  const int64_t p = pos[t];
+  for (int h = threadIdx.x >> 5; h < heads; h += blockDim.x >> 5) {
+  float f[PER];
+  load_bf16<PER>(qkv + t * (int64_t)heads * D + (int64_t)h * D + lane * PER, f);
+  float ss = 0.0f;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) ss = fmaf(f[e], f[e], ss);
+  const float r = rsqrtf(warp_sum(ss) / (float)D + eps);
+  const bool is_q = h < hq, is_k = !is_q && h < hq + hk;
+  const __nv_bfloat16* wt = is_q ? qw : (is_k ? kw : nullptr);
+  float y[PER];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) y[e] = bf16r(f[e] * r);
+  __nv_bfloat16* dst;
+  if (is_q) {
+    dst = q + (t * hq + h) * (int64_t)D;
+  } else if (is_k) {
+    dst = k + (t * hk + (h - hq)) * (int64_t)D;
+  } else {
+    dst = v + (t * hk + (h - hq - hk)) * (int64_t)D;
+  }
+  if (wt) {
+    float wf[PER];
+    load_bf16<PER>(wt + lane * PER, wf);
+#pragma unroll
+    for (int e = 0; e < PER; ++e) y[e] = bf16r(y[e] * wf[e]);
+    // rotate half: x1 = elements [0, D/2) (lanes 0..15), x2 = [D/2, D) (lanes 16..31)
+    const bool first = lane < 16;
+    const int fi0 = (first ? lane : lane - 16) * PER;     // frequency index of this lane's first element
+    float cs[PER], sn[PER];
+    load_bf16<PER>(cos_t + p * (D / 2) + fi0, cs);
+    load_bf16<PER>(sin_t + p * (D / 2) + fi0, sn);
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, y[e], 16);
+      // first half: x1 cos - x2 sin; second half: x2 cos + x1 sin -- each product and the sum rounded to bf16
+      const float a1 = bf16r(y[e] * cs[e]), a2 = bf16r(other * sn[e]);
+      y[e] = first ? bf16r(a1 - a2) : bf16r(a1 + a2);
+    }
+  }
+  store_bf16<PER>(dst + lane * PER, y);
+  }
+}
+
+// gate = gu[:, :I], up = gu[:, I:]; 8 columns per thread.
+__global__ void __launch_bounds__(256) gelu_tanh_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t rows,
+                                                            int inter, __nv_bfloat16* __restrict__ h) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = inter >> 3;
+  if (i >= rows * per_row) return;
+  const int64_t row = i / per_row;
+  const int c = (int)(i - row * per_row);
+  const uint4 g = __ldg(reinterpret_cast<const uint4*>(gu + row * 2 * inter) + c);
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(gu + row * 2 * inter + inter) + c);
+  float gf[8], uf[8];
+  bf16x8_to_f32(g, gf);
+  bf16x8_to_f32(u, uf);
+  const float kBeta = 0.7978845608028654f;          // sqrt(2 / pi)
+  const float kKappa = 0.044715f;
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float y[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float x = gf[2 * j + e];
+      const float inner = kBeta * (x + kKappa * (x * x * x));
+      const float act = bf16r(0.5f * x * (1.0f + tanhf(inner)));
+      y[e] = act * uf[2 * j + e];
+    }
+    o[j] = pack_bf16x2(y[0], y[1]);
+  }
+  reinterpret_cast<uint4*>(h + row * inter)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+}  // namespace dops
+
+int launch_rmsnorm(const void* a, const void* b, const void* w, const void* res, float eps, int64_t rows, int cols,
+                   void* out, cudaStream_t s) {
+  if (rows == 0) return 0;
+  if (rows > 0x7FFFFFFFLL) return REAXMOE_ERR_BAD_SHAPE;
+  dops::rmsnorm_kernel<<<(unsigned)rows, dops::RN_THREADS, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
+      static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(res), eps, cols,
+      static_cast<__nv_bfloat16*>(out));
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
+}
+
+int launch_qkv_norm_rope(const void* qkv, const void* qw, const void* kw, const void* cos_t, const void* sin_t,
+                         const int64_t* pos, float eps, int64_t n, int hq, int hk, int d, void* q, void* k, void* v,
+                         cudaStream_t s) {
+  if (n == 0) return 0;
+  if (n > 0x7FFFFFFFLL) return REAXMOE_ERR_BAD_SHAPE;
+  const int warps = 8;
+  const unsigned grid = (unsigned)n;
+#define REAXMOE_QKV(DD)                                                                                          \
+  dops::qkv_norm_rope_kernel<DD><<<grid, warps * 32, 0, s>>>(                                                    \
+      static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(qw),                            \
+      static_cast<const __nv_bfloat16*>(kw), static_cast<const __nv_bfloat16*>(cos_t),                          \
+      static_cast<const __nv_bfloat16*>(sin_t), pos, eps, n, hq, hk, static_cast<__nv_bfloat16*>(q),             \
+      static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v))
+  switch (d) {
+    case 64: REAXMOE_QKV(64); break;
+    case 128: REAXMOE_QKV(128); break;
+    case 256: REAXMOE_QKV(256); break;
+    default: return REAXMOE_ERR_UNSUPPORTED;
+  }
+#undef REAXMOE_QKV
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
+}
+
+int launch_gelu_tanh_mul(const void* gu, int64_t rows, int inter, void* h, cudaStream_t s) {
+  const int64_t items = rows * (inter / 8);
+  if (items == 0) return 0;
+  dops::gelu_tanh_mul_kernel<<<(unsigned)ceil_div64(items, 256), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(gu), rows, inter, static_cast<__nv_bfloat16*>(h));
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
+}
+
+}  // namespace reaxmoe

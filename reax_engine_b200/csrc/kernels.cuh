@@ -79,4 +79,12 @@ struct RouterLaunch {
 };
 int launch_router_topk(const RouterLaunch& r, cudaStream_t s);
 
+// decision_ops.cu: the decision forward's fused element-wise steps
+int launch_rmsnorm(const void* a, const void* b, const void* w, const void* res, float eps, int64_t rows, int cols,
+                   void* out, cudaStream_t s);
+int launch_qkv_norm_rope(const void* qkv, const void* qw, const void* kw, const void* cos_t, const void* sin_t,
+                         const int64_t* pos, float eps, int64_t n, int hq, int hk, int d, void* q, void* k, void* v,
+                         cudaStream_t s);
+int launch_gelu_tanh_mul(const void* gu, int64_t rows, int inter, void* h, cudaStream_t s);
+
 }  // namespace reaxmoe

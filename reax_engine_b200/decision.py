@@ -31,8 +31,8 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
 
+from . import _lib as L
 from . import moe as M
 
 
@@ -92,14 +92,38 @@ class LayerWeights:
 NORMS = ("input", "post_attention", "pre_ff", "post_ff", "post_ff_1", "pre_ff_2", "post_ff_2")
 
 
-def rms_norm(x: torch.Tensor, w: torch.Tensor | None, eps: float) -> torch.Tensor:
-    """vLLM ``rms_norm`` (``vllm/ir/ops/layernorm.py:10-21``): fp32 normalise, cast to the weight's dtype, times the
-    weight, back to the input dtype."""
-    xf = x.float()
-    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    if w is None:
-        return y.to(x.dtype)
-    return (y.to(w.dtype) * w).to(x.dtype)
+def rms_norm(a: torch.Tensor, w: torch.Tensor | None, eps: float, b: torch.Tensor | None = None,
+             residual: torch.Tensor | None = None) -> torch.Tensor:
+    """vLLM ``rms_norm`` (``vllm/ir/ops/layernorm.py:10-21``) of bf16(a [+ b]), times w, [+ residual], one fused
+    kernel (``reaxmoe_rmsnorm``) at the same bf16 rounding points."""
+    a = a.contiguous()
+    out = torch.empty_like(a)
+    rows = a.numel() // a.shape[-1]
+    L.check(L.lib().reaxmoe_rmsnorm(a.data_ptr(), M._ptr(b), M._ptr(w), M._ptr(residual), float(eps), rows,
+                                    a.shape[-1], out.data_ptr(), M._stream(a.device)))
+    return out
+
+
+def qkv_norm_rope(qkv: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                  pos: torch.Tensor, eps: float, hq: int, hk: int, d: int):
+    """Per-head q / k (weighted) and v RMSNorm, then NeoX RoPE of q and k (``reaxmoe_qkv_norm_rope``)."""
+    n = qkv.shape[0]
+    q = torch.empty(n, hq, d, dtype=qkv.dtype, device=qkv.device)
+    k = torch.empty(n, hk, d, dtype=qkv.dtype, device=qkv.device)
+    v = torch.empty(n, hk, d, dtype=qkv.dtype, device=qkv.device)
+    L.check(L.lib().reaxmoe_qkv_norm_rope(qkv.contiguous().data_ptr(), q_w.data_ptr(), k_w.data_ptr(),
+                                          cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), float(eps), n, hq, hk, d,
+                                          q.data_ptr(), k.data_ptr(), v.data_ptr(), M._stream(qkv.device)))
+    return q, k, v
+
+
+def gelu_tanh_mul(gu: torch.Tensor) -> torch.Tensor:
+    """bf16(bf16(gelu_tanh(gate)) * up) of gu = [gate | up] (``reaxmoe_gelu_tanh_mul``)."""
+    rows, two_i = gu.shape
+    h = torch.empty(rows, two_i // 2, dtype=gu.dtype, device=gu.device)
+    L.check(L.lib().reaxmoe_gelu_tanh_mul(gu.contiguous().data_ptr(), rows, two_i // 2, h.data_ptr(),
+                                          M._stream(gu.device)))
+    return h
 
 
 class DecisionModel:
@@ -193,35 +217,20 @@ class DecisionModel:
             self._rope_cache[kind] = (f.cos().to(torch.bfloat16).to(self.dev), f.sin().to(torch.bfloat16).to(self.dev))
         self.max_positions = max_len
 
-    def _rope(self, x: torch.Tensor, pos: torch.Tensor, kind: str) -> torch.Tensor:
-        """NeoX rotate-half over the whole head with the bf16 cache, in bf16 arithmetic (one rounding per operation),
-        as vLLM's rotary op computes it."""
-        cos_t, sin_t = self._rope_cache[kind]
-        cos, sin = cos_t[pos][:, None, :], sin_t[pos][:, None, :]
-        h = x.shape[-1] // 2
-        x1, x2 = x[..., :h], x[..., h:]
-        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
-
     def _attention(self, lw: LayerWeights, layer: int, xn: torch.Tensor, pos: torch.Tensor, cu: torch.Tensor,
                    max_len: int, last: torch.Tensor | None) -> torch.Tensor:
         c = self.cfg
-        n = xn.shape[0]
         qkv = xn @ lw.wqkv.t()
-        q, k, v = qkv.split([c.heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
-        k = rms_norm(k.reshape(n, c.kv_heads, c.head_dim), lw.k_norm, c.eps)
-        v = rms_norm(v.reshape(n, c.kv_heads, c.head_dim), None, c.eps)
         kind = "local" if c.sliding(layer) else "global"
-        k = self._rope(k, pos, kind)
+        cos, sin = self._rope_cache[kind]
+        q, k, v = qkv_norm_rope(qkv, lw.q_norm, lw.k_norm, cos, sin, pos, c.eps, c.heads, c.kv_heads, c.head_dim)
         win = (c.window - 1, 0) if c.sliding(layer) else (-1, -1)
         if last is None:
-            q = self._rope(rms_norm(q.reshape(n, c.heads, c.head_dim), lw.q_norm, c.eps), pos, kind)
             o = self._fa(q, k, v, cu, cu, max_len, max_len, softmax_scale=1.0, causal=True, window_size=win)
         else:
             # only the last query row of each prompt; the causal mask is aligned to the end of the keys
-            ql = self._rope(rms_norm(q[last].reshape(last.numel(), c.heads, c.head_dim), lw.q_norm, c.eps),
-                            pos[last], kind)
             cu_q = torch.arange(last.numel() + 1, dtype=torch.int32, device=self.dev)
-            o = self._fa(ql, k, v, cu_q, cu, 1, max_len, softmax_scale=1.0, causal=True, window_size=win)
+            o = self._fa(q[last], k, v, cu_q, cu, 1, max_len, softmax_scale=1.0, causal=True, window_size=win)
         return o.reshape(o.shape[0], c.heads * c.head_dim) @ lw.wo.t()
 
     def _moe(self, lw: LayerWeights, r: torch.Tensor) -> torch.Tensor:
@@ -241,8 +250,7 @@ class DecisionModel:
     def _dense(self, lw: LayerWeights, r: torch.Tensor) -> torch.Tensor:
         c = self.cfg
         gu = rms_norm(r, lw.norms["pre_ff"], c.eps) @ lw.w_gate_up.t()
-        h = F.gelu(gu[:, :c.dense_inter], approximate="tanh") * gu[:, c.dense_inter:]
-        return rms_norm(h @ lw.w_down.t(), lw.norms["post_ff_1"], c.eps)
+        return rms_norm(gelu_tanh_mul(gu) @ lw.w_down.t(), lw.norms["post_ff_1"], c.eps)
 
     # ------------------------------------------------------------------------------------------ forward
     _record = None
@@ -270,7 +278,7 @@ class DecisionModel:
             is_last = i == c.layers - 1
             rows = last if is_last else None
             a = self._attention(lw, i, rms_norm(x, lw.norms["input"], c.eps), pos, cu, max_len, rows)
-            r = rms_norm(a, lw.norms["post_attention"], c.eps) + (x[last] if is_last else x)
+            r = rms_norm(a, lw.norms["post_attention"], c.eps, residual=x[last] if is_last else x)
             # the MoE block on its own stream, in parallel with the dense MLP
             self.moe_stream.wait_stream(cur)
             with torch.cuda.stream(self.moe_stream):
@@ -280,7 +288,7 @@ class DecisionModel:
             m.record_stream(cur)
             if self.layer_log is not None:
                 self.layer_log.append(dict(x=x.clone(), r=r.clone(), d=d.clone(), m=m.clone()))
-            x = rms_norm(d + m, lw.norms["post_ff"], c.eps) + r
+            x = rms_norm(d, lw.norms["post_ff"], c.eps, b=m, residual=r)
             if lw.layer_scalar != 1.0:
                 x = x * lw.layer_scalar
         if self.layer_log is not None:

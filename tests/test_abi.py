@@ -95,6 +95,19 @@ def test_router_topk_rejects_unsupported():
     assert f(None, None, None, None, 1e-6, 0, 2816, 128, 8, None, None, None, None, None) == L.OK
 
 
+def test_decision_ops_reject_bad_args():
+    lib = L.lib()
+    assert lib.reaxmoe_rmsnorm(None, None, None, None, 1e-6, 4, 100, None, None) == L.ERR_BAD_SHAPE
+    assert lib.reaxmoe_rmsnorm(None, None, None, None, 1e-6, 4, 8192, None, None) == L.ERR_BAD_SHAPE
+    assert lib.reaxmoe_rmsnorm(None, None, None, None, 1e-6, 4, 2816, None, None) == L.ERR_NULL
+    assert lib.reaxmoe_rmsnorm(None, None, None, None, 1e-6, 0, 2816, None, None) == L.OK
+    f = lib.reaxmoe_qkv_norm_rope
+    assert f(None, None, None, None, None, None, 1e-6, 4, 16, 8, 96, None, None, None, None) == L.ERR_BAD_SHAPE
+    assert f(None, None, None, None, None, None, 1e-6, 4, 16, 8, 256, None, None, None, None) == L.ERR_NULL
+    assert lib.reaxmoe_gelu_tanh_mul(None, 4, 7, None, None) == L.ERR_BAD_SHAPE
+    assert lib.reaxmoe_gelu_tanh_mul(None, 4, 704, None, None) == L.ERR_NULL
+
+
 def test_quantize_and_prepack_reject_bad_args():
     lib = L.lib()
     assert lib.reaxmoe_quantize(None, 0, 4, 100, 4, None, None, None, None) == L.ERR_BAD_SHAPE
