@@ -102,6 +102,15 @@ size_t reaxmoe_workspace_size(const reaxmoe_problem* p);
  * (run_cutlass_moe_fp4, cutlass_moe.py:481-664; blink_moe.py:434-567). */
 int reaxmoe_forward(const reaxmoe_forward_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same layer on token rows quantised upstream (reaxmoe_rmsnorm_nvfp4; the quant-once path of
+ * blink_moe.py:353-363 with the norm fused, engine/fp4_triton.py:68-90): args->a points to packed e2m1 rows
+ * [tokens, hidden / 2], a_scales to their linear e4m3 block scales [tokens, hidden / 16], made with the quant-side
+ * scale a_gscale. Every expert must quantise with that scale (a1_gscale[e] == a_gscale; a routed expert that differs
+ * sets REAXMOE_ERR_UNSUPPORTED in the device status word). hidden a multiple of 256, <= 4096. Same output as
+ * reaxmoe_forward on the bf16 rows those bytes were made from. */
+int reaxmoe_forward_prequant(const reaxmoe_forward_args* args, const void* a_scales, float a_gscale,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* Gemma-4 routing: ids = top-k of logits (descending, ties to the lower expert id), weights = softmax over all
  * experts renormalised over the top-k, times per_expert_scale[id] (NULL = 1). logits [tokens, experts] fp32;
  * ids [tokens, topk] int32; weights [tokens, topk] fp32. (gemma4.py:183-203) */
@@ -130,6 +139,14 @@ int reaxmoe_router_topk(const void* hidden_states, const void* router_scale, con
  * scale). rows x cols, cols a multiple of 256 and <= 4096. */
 int reaxmoe_rmsnorm(const void* a, const void* b, const void* weight, const void* residual, float eps, int64_t rows,
                     int32_t cols, void* out, void* stream);
+/* reaxmoe_rmsnorm followed by the static NVFP4 quantisation of its bf16 output with the quant-side global scale
+ * `gscale` (1 / g): packed [rows, cols / 2] e2m1 (low nibble = even column) and linear e4m3 block scales
+ * [rows, cols / 16], the bytes permute_quant would make from the bf16 output (the add + RMSNorm + quant fusion of
+ * engine/fp4_triton.py:68-90, with vLLM's norm arithmetic). `out` (bf16, NULL-able) receives the bf16 output too.
+ * Feeds reaxmoe_forward_prequant. */
+int reaxmoe_rmsnorm_nvfp4(const void* a, const void* b, const void* weight, const void* residual, float eps,
+                          int64_t rows, int32_t cols, float gscale, void* out, void* packed, void* scales,
+                          void* stream);
 /* qkv [tokens, (q_heads + 2 kv_heads) * head_dim] -> q [tokens, q_heads, head_dim], k, v [tokens, kv_heads,
  * head_dim]: per-head RMSNorm of q and k with their weights [head_dim], of v without (Gemma4Attention.forward,
  * gemma4.py:512-535), then NeoX rotate-half of q and k with bf16 tables cos / sin [max_position, head_dim / 2]

@@ -64,6 +64,10 @@ SIGNATURES = {
     "reaxmoe_qkv_norm_rope": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, ctypes.c_float, ctypes.c_int64, _I32, _I32, _I32,
                                              _P, _P, _P, _P]),
     "reaxmoe_gelu_tanh_mul": (ctypes.c_int, [_P, ctypes.c_int64, _I32, _P, _P]),
+    "reaxmoe_rmsnorm_nvfp4": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, ctypes.c_int64, _I32, ctypes.c_float,
+                                             _P, _P, _P, _P]),
+    "reaxmoe_forward_prequant": (ctypes.c_int, [ctypes.POINTER(ForwardArgs), _P, ctypes.c_float, _P, ctypes.c_size_t,
+                                                _P]),
     "reaxmoe_plan": (ctypes.c_int, [_PP, _P, _P, ctypes.c_size_t, _P, _P, _P, _P, _P]),
     "reaxmoe_permute_quant": (ctypes.c_int, [_PP, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P, _P]),
     "reaxmoe_gemm_w13": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P]),

@@ -348,6 +348,25 @@ int reaxmoe_rmsnorm(const void* a, const void* b, const void* weight, const void
   return cuda_check("rmsnorm");
 }
 
+int reaxmoe_rmsnorm_nvfp4(const void* a, const void* b, const void* weight, const void* residual, float eps,
+                          int64_t rows, int32_t cols, float gscale, void* out, void* packed, void* scales,
+                          void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 256 != 0 || cols > 4096)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "rmsnorm_nvfp4: rows=%lld cols=%d (cols a multiple of 256, <= 4096)",
+                (long long)rows, cols);
+  if (!(gscale > 0.0f)) return fail(REAXMOE_ERR_BAD_SHAPE, "rmsnorm_nvfp4: gscale must be > 0");
+  if (rows == 0) return 0;
+  if (!a || !packed || !scales) return fail(REAXMOE_ERR_NULL, "rmsnorm_nvfp4: NULL input or output");
+  if (!aligned16(a) || !aligned16(packed) || !aligned16(scales) || (out && !aligned16(out)) || (b && !aligned16(b)) ||
+      (weight && !aligned16(weight)) || (residual && !aligned16(residual)))
+    return fail(REAXMOE_ERR_MISALIGNED, "rmsnorm_nvfp4: tensors must be 16-byte aligned");
+  const int rc = launch_rmsnorm_nvfp4(a, b, weight, residual, eps, rows, cols, gscale, out,
+                                      static_cast<uint8_t*>(packed), static_cast<uint8_t*>(scales),
+                                      static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "rmsnorm_nvfp4 launch failed: %s", cudaGetErrorString(cudaPeekAtLastError()));
+  return cuda_check("rmsnorm_nvfp4");
+}
+
 int reaxmoe_qkv_norm_rope(const void* qkv, const void* q_weight, const void* k_weight, const void* cos_table,
                           const void* sin_table, const int64_t* positions, float eps, int64_t tokens, int32_t q_heads,
                           int32_t kv_heads, int32_t head_dim, void* q, void* k, void* v, void* stream) {
@@ -494,6 +513,45 @@ int reaxmoe_forward(const reaxmoe_forward_args* args, void* workspace, size_t wo
   launch_combine(w.c3, w.c_map, args->topk_weights, p->tokens, p->hidden, p->topk,
                  static_cast<__nv_bfloat16*>(args->output), sms, s);
   return cuda_check("forward");
+}
+
+int reaxmoe_forward_prequant(const reaxmoe_forward_args* args, const void* a_scales, float a_gscale,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (args == nullptr) return fail(REAXMOE_ERR_NULL, "forward_prequant: args is NULL");
+  const reaxmoe_problem* p = &args->p;
+  int rc = check_problem(p);
+  if (rc) return rc;
+  if (p->hidden > 4096 || p->hidden % 256 != 0)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "forward_prequant: hidden=%d (a multiple of 256, <= 4096)", p->hidden);
+  if (!(a_gscale > 0.0f)) return fail(REAXMOE_ERR_BAD_SHAPE, "forward_prequant: a_gscale must be > 0");
+  Layout L;
+  if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
+  if (p->tokens == 0) return 0;
+  if (!args->a || !a_scales || !args->a1_gscale || !args->w1_fp4 || !args->w1_sf || !args->w1_alphas ||
+      !args->a2_gscale || !args->w2_fp4 || !args->w2_sf || !args->w2_alphas || !args->topk_weights ||
+      !args->topk_ids || !args->output)
+    return fail(REAXMOE_ERR_NULL, "forward_prequant: NULL pointer in args");
+  if (!aligned16(args->a) || !aligned16(a_scales) || !aligned16(args->w1_fp4) || !aligned16(args->w1_sf) ||
+      !aligned16(args->w2_fp4) || !aligned16(args->w2_sf) || !aligned16(args->output))
+    return fail(REAXMOE_ERR_MISALIGNED, "forward_prequant: activations, weights and output must be 16-byte aligned");
+  const WS w = carve(workspace, L);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = do_plan(p, args->topk_ids, w, nullptr, nullptr, s))) return rc;
+  launch_permute_fp4(static_cast<const uint8_t*>(args->a), static_cast<const uint8_t*>(a_scales), a_gscale,
+                     args->a1_gscale, args->topk_ids, w.seg_base, w.eoff, p->tokens, p->hidden, p->experts, p->topk,
+                     w.rep_fp4, w.lin_sf, w.c_map, w.status, s);
+  launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
+                        (int64_t)p->tokens * p->topk, w.rep_sf, s);
+  if ((rc = cuda_check("permute_fp4"))) return rc;
+  const int sms = num_sms();
+  GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, args->w1_fp4, args->w1_sf, args->w1_alphas, args->a2_gscale,
+                             w.int_fp4, w.int_sf);
+  if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "forward_prequant: gemm_w13 launch failed");
+  GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, args->w2_fp4, args->w2_sf, args->w2_alphas, w.c3);
+  if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "forward_prequant: gemm_w2 launch failed");
+  launch_combine(w.c3, w.c_map, args->topk_weights, p->tokens, p->hidden, p->topk,
+                 static_cast<__nv_bfloat16*>(args->output), sms, s);
+  return cuda_check("forward_prequant");
 }
 
 int reaxmoe_quantize(const void* x, int32_t x_is_fp32, int64_t rows, int32_t cols, int32_t group_rows,

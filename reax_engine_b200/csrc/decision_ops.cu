@@ -103,6 +103,96 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const __nv_bfloat16
   }
 }
 
+// rmsnorm followed by the static-scale NVFP4 quantisation of its bf16 output (the add + RMSNorm + quant fusion of
+// engine/fp4_triton.py:68-90, here with vLLM's Gemma-4 norm arithmetic), for a MoE block's input: the quantiser is the
+// one permute_quant applies per routed row (quant_block16_bf16 with g = 1 / gscale), so the bytes are identical to
+// quantising the bf16 norm output. Thread i holds pieces i, i + 128, ...; a 16-element block is the two pieces of an
+// even / odd thread pair, joined with one shuffle. Writes packed [rows, cols / 2] e2m1, linear block scales
+// [rows, cols / 16] e4m3 and, when out is not null, the bf16 output too.
+__global__ void __launch_bounds__(RN_THREADS) rmsnorm_nvfp4_kernel(const __nv_bfloat16* __restrict__ a,
+                                                                   const __nv_bfloat16* __restrict__ b,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   const __nv_bfloat16* __restrict__ res, float eps,
+                                                                   int cols, float g, __nv_bfloat16* __restrict__ out,
+                                                                   uint8_t* __restrict__ packed,
+                                                                   uint8_t* __restrict__ scales) {
+  __shared__ float part[RN_THREADS / 32];
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int pieces = cols >> 3;
+  const uint4* pa = reinterpret_cast<const uint4*>(a + row * cols);
+  const uint4* pb = b ? reinterpret_cast<const uint4*>(b + row * cols) : nullptr;
+  const uint4* pr = res ? reinterpret_cast<const uint4*>(res + row * cols) : nullptr;
+  uint4 s[RN_PIECES], rv[RN_PIECES];
+#pragma unroll
+  for (int j = 0; j < RN_PIECES; ++j) {
+    const int i = tid + j * RN_THREADS;
+    if (i < pieces) {
+      s[j] = __ldg(pa + i);
+      if (pb) {
+        const uint4 u = __ldg(pb + i);
+        s[j] = make_uint4(bf2_add(s[j].x, u.x), bf2_add(s[j].y, u.y), bf2_add(s[j].z, u.z), bf2_add(s[j].w, u.w));
+      }
+      if (pr) rv[j] = __ldg(pr + i);
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < RN_PIECES; ++j) {
+    if (tid + j * RN_THREADS < pieces) {
+      float f[8];
+      bf16x8_to_f32(s[j], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) part[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int k = 0; k < RN_THREADS / 32; ++k) tot += part[k];
+  const float r = rsqrtf(tot / (float)cols + eps);
+  const uint4* pw = w ? reinterpret_cast<const uint4*>(w) : nullptr;
+#pragma unroll
+  for (int j = 0; j < RN_PIECES; ++j) {
+    const int i = tid + j * RN_THREADS;
+    const bool live = i < pieces;            // pieces is a multiple of 32: both threads of a pair agree
+    uint4 ov = make_uint4(0u, 0u, 0u, 0u);
+    if (live) {
+      float f[8];
+      bf16x8_to_f32(s[j], f);
+      float wf[8];
+      if (pw) bf16x8_to_f32(__ldg(pw + i), wf);
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float y0 = bf16r(f[2 * q] * r), y1 = bf16r(f[2 * q + 1] * r);
+        if (pw) {
+          y0 = bf16r(y0 * wf[2 * q]);
+          y1 = bf16r(y1 * wf[2 * q + 1]);
+        }
+        o[q] = pack_bf16x2(y0, y1);
+      }
+      ov = make_uint4(o[0], o[1], o[2], o[3]);
+      if (pr) ov = make_uint4(bf2_add(ov.x, rv[j].x), bf2_add(ov.y, rv[j].y), bf2_add(ov.z, rv[j].z),
+                              bf2_add(ov.w, rv[j].w));
+      if (out) reinterpret_cast<uint4*>(out + row * cols)[i] = ov;
+    }
+    // the odd thread's piece completes the even thread's 16-element block
+    const uint32_t n0 = __shfl_xor_sync(0xffffffffu, ov.x, 1), n1 = __shfl_xor_sync(0xffffffffu, ov.y, 1);
+    const uint32_t n2 = __shfl_xor_sync(0xffffffffu, ov.z, 1), n3 = __shfl_xor_sync(0xffffffffu, ov.w, 1);
+    if (live && (tid & 1) == 0) {
+      const uint32_t xw[8] = {ov.x, ov.y, ov.z, ov.w, n0, n1, n2, n3};
+      uint32_t lo, hi;
+      const uint32_t sb = quant_block16_bf16(xw, g, lo, hi);
+      const int blk = i >> 1;
+      *reinterpret_cast<uint2*>(packed + row * (cols / 2) + blk * 8) = make_uint2(lo, hi);
+      scales[row * (cols / 16) + blk] = (uint8_t)sb;
+    }
+  }
+}
+
 // PER consecutive bf16 <-> floats with one vector access (PER = 2, 4 or 8; the address is PER*2-byte aligned)
 template <int PER>
 __device__ __forceinline__ void load_bf16(const __nv_bfloat16* p, float* f) {
@@ -237,6 +327,17 @@ int launch_rmsnorm(const void* a, const void* b, const void* w, const void* res,
       static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
       static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(res), eps, cols,
       static_cast<__nv_bfloat16*>(out));
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
+}
+
+int launch_rmsnorm_nvfp4(const void* a, const void* b, const void* w, const void* res, float eps, int64_t rows,
+                         int cols, float gscale, void* out, uint8_t* packed, uint8_t* scales, cudaStream_t s) {
+  if (rows == 0) return 0;
+  if (rows > 0x7FFFFFFFLL) return REAXMOE_ERR_BAD_SHAPE;
+  dops::rmsnorm_nvfp4_kernel<<<(unsigned)rows, dops::RN_THREADS, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
+      static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(res), eps, cols,
+      1.0f / gscale, static_cast<__nv_bfloat16*>(out), packed, scales);   // IEEE division, as permute_quant
   return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
 }
 

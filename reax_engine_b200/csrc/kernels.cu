@@ -267,6 +267,59 @@ __global__ void __launch_bounds__(256, 3) permute_quant_kernel(
 }
 
 // ------------------------------------------------------------------------------------------------------
+// K3a' permute_fp4: the same slot assignment as permute_quant, for token rows that are already NVFP4 (a fused
+// norm + quantise upstream, e.g. add + RMSNorm + quant in one kernel as engine/fp4_triton.py:68-90 does): each slot
+// receives a byte copy of its token's FP4 row and linear scale row. The copy is exact only if every slot's expert
+// quantises with the scale the rows were made with (a1_gscale[e] == in_gscale); a slot whose expert differs flags
+// REAXMOE_ERR_UNSUPPORTED in the status word and is copied all the same.
+// ------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) permute_fp4_kernel(
+    const uint8_t* __restrict__ a_fp4, const uint8_t* __restrict__ a_sf, float in_gscale,
+    const float* __restrict__ a1_gscale, const int* __restrict__ ids, const int* __restrict__ seg_base,
+    const int* __restrict__ eoff, int m, int H, int E, int k, uint8_t* __restrict__ rep_fp4,
+    uint8_t* __restrict__ lin_sf, int* __restrict__ c_map, int* status) {
+  __shared__ int run[kMaxExperts];
+  __shared__ uint32_t mask[kMaxExperts];
+  __shared__ int pos_s[kSegTokens * kMaxTopk];
+  __shared__ short exp_s[kSegTokens * kMaxTopk];
+  const int seg = blockIdx.x;
+  const int64_t t0 = (int64_t)seg * kSegTokens;
+  const int nt = (int)(kSegTokens < m - t0 ? (int64_t)kSegTokens : m - t0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    run[e] = eoff[e] + seg_base[(int64_t)seg * E + e];
+    mask[e] = 0u;
+  }
+  __syncthreads();
+  if (warp == 0) segment_slots(ids, t0, nt, k, E, run, mask, pos_s, exp_s, c_map);
+  __syncthreads();
+  const int row16 = H / 32;          // 16-byte pieces of an FP4 row
+  const int sf16 = H / 256;          // 16-byte pieces of a linear scale row
+  constexpr int kMaxRow = 4;         // H <= 4096: <= 128 pieces, 4 per lane
+  for (int tl = warp; tl < nt; tl += blockDim.x >> 5) {
+    const int64_t t = t0 + tl;
+    const uint4* src = reinterpret_cast<const uint4*>(a_fp4 + t * (H / 2));
+    uint4 row[kMaxRow];
+#pragma unroll
+    for (int i = 0; i < kMaxRow; ++i)
+      if (lane + 32 * i < row16) row[i] = __ldg(src + lane + 32 * i);
+    uint4 sfv = make_uint4(0u, 0u, 0u, 0u);
+    if (lane < sf16) sfv = __ldg(reinterpret_cast<const uint4*>(a_sf + t * (H / 16)) + lane);
+    for (int j = 0; j < k; ++j) {
+      const int e = exp_s[tl * k + j];
+      if (e < 0) continue;
+      const int64_t pos = pos_s[tl * k + j];
+      if (lane == 0 && a1_gscale[e] != in_gscale) set_status(status, REAXMOE_ERR_UNSUPPORTED);
+      uint4* dst = reinterpret_cast<uint4*>(rep_fp4 + pos * (H / 2));
+#pragma unroll
+      for (int i = 0; i < kMaxRow; ++i)
+        if (lane + 32 * i < row16) dst[lane + 32 * i] = row[i];
+      if (lane < sf16) reinterpret_cast<uint4*>(lin_sf + pos * (H / 16))[lane] = sfv;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------
 // K3b swizzle_scales: one CTA per GEMM m-tile gm (expert e, 128 routed rows), whose scale rows are atom row block gm
 // of the 128x4 layout (blockscale_offsets[e] / 128 == tile_prefix[e]). Reads the tile's rows of the linear scale
 // buffer [slots, H/16] (contiguous) into shared memory and writes its H/64 atoms of 512 bytes with 16-byte stores
@@ -554,6 +607,16 @@ int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const i
   if (nseg > 0)
     permute_quant_kernel<<<nseg, 256, 0, s>>>(a, a1_gscale, ids, seg_base, eoff, boff, m, H, E, k, rep_fp4, lin_sf,
                                               c_map);
+  return 0;
+}
+
+int launch_permute_fp4(const uint8_t* a_fp4, const uint8_t* a_sf, float in_gscale, const float* a1_gscale,
+                       const int* ids, const int* seg_base, const int* eoff, int m, int H, int E, int k,
+                       uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, int* status, cudaStream_t s) {
+  const int nseg = (int)ceil_div64(m, kSegTokens);
+  if (nseg > 0)
+    permute_fp4_kernel<<<nseg, 256, 0, s>>>(a_fp4, a_sf, in_gscale, a1_gscale, ids, seg_base, eoff, m, H, E, k,
+                                            rep_fp4, lin_sf, c_map, status);
   return 0;
 }
 

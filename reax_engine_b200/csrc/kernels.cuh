@@ -86,5 +86,10 @@ int launch_qkv_norm_rope(const void* qkv, const void* qw, const void* kw, const 
                          const int64_t* pos, float eps, int64_t n, int hq, int hk, int d, void* q, void* k, void* v,
                          cudaStream_t s);
 int launch_gelu_tanh_mul(const void* gu, int64_t rows, int inter, void* h, cudaStream_t s);
+int launch_rmsnorm_nvfp4(const void* a, const void* b, const void* w, const void* res, float eps, int64_t rows,
+                         int cols, float gscale, void* out, uint8_t* packed, uint8_t* scales, cudaStream_t s);
+int launch_permute_fp4(const uint8_t* a_fp4, const uint8_t* a_sf, float in_gscale, const float* a1_gscale,
+                       const int* ids, const int* seg_base, const int* eoff, int m, int H, int E, int k,
+                       uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, int* status, cudaStream_t s);
 
 }  // namespace reaxmoe

@@ -83,6 +83,7 @@ class LayerWeights:
     w2_sfx: torch.Tensor
     w2_g: torch.Tensor
     a1_gscale: torch.Tensor = None   # [experts] quant-side input scale (1 / g), set by calibrate()
+    a1_gs: float = 0.0                # the same value on the host
     a2_gscale: torch.Tensor = None
     w1_alphas: torch.Tensor = None
     w2_alphas: torch.Tensor = None
@@ -102,6 +103,18 @@ def rms_norm(a: torch.Tensor, w: torch.Tensor | None, eps: float, b: torch.Tenso
     L.check(L.lib().reaxmoe_rmsnorm(a.data_ptr(), M._ptr(b), M._ptr(w), M._ptr(residual), float(eps), rows,
                                     a.shape[-1], out.data_ptr(), M._stream(a.device)))
     return out
+
+
+def rms_norm_nvfp4(a: torch.Tensor, w: torch.Tensor | None, eps: float, gscale: float) -> M.NVFP4Rows:
+    """:func:`rms_norm` fused with the static NVFP4 quantisation of its output (quant-side scale ``gscale``), one
+    kernel (``reaxmoe_rmsnorm_nvfp4``): the MoE block's input never exists in bf16."""
+    a = a.contiguous()
+    rows, cols = a.shape
+    packed = torch.empty(rows, cols // 2, dtype=torch.uint8, device=a.device)
+    scales = torch.empty(rows, cols // 16, dtype=torch.uint8, device=a.device)
+    L.check(L.lib().reaxmoe_rmsnorm_nvfp4(a.data_ptr(), None, M._ptr(w), None, float(eps), rows, cols, float(gscale),
+                                          None, packed.data_ptr(), scales.data_ptr(), M._stream(a.device)))
+    return M.NVFP4Rows(packed, scales, float(gscale))
 
 
 def qkv_norm_rope(qkv: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
@@ -183,7 +196,8 @@ class DecisionModel:
         a2_g = c.a2_amax / 2688.0
         for lw, a in zip(self.layers, amax):
             a1_g = max(float(a), 1e-6) / 2688.0
-            lw.a1_gscale = torch.full((c.experts,), 1.0 / a1_g, dtype=torch.float32, device=self.dev)
+            lw.a1_gs = float(torch.tensor(1.0 / a1_g, dtype=torch.float32))     # the fp32 value, on the host
+            lw.a1_gscale = torch.full((c.experts,), lw.a1_gs, dtype=torch.float32, device=self.dev)
             lw.a2_gscale = torch.full((c.experts,), 1.0 / a2_g, dtype=torch.float32, device=self.dev)
             lw.w1_alphas = (lw.w1_g * a1_g).float()
             lw.w2_alphas = (lw.w2_g * a2_g).float()
@@ -239,10 +253,13 @@ class DecisionModel:
                                per_expert_scale=lw.per_expert_scale)
         if self.routing_log is not None:
             self.routing_log.append(ids.clone())
-        x2 = rms_norm(r, lw.norms["pre_ff_2"], c.eps)
         if self._record is not None:
+            x2 = rms_norm(r, lw.norms["pre_ff_2"], c.eps)
             self._record.append(float(x2.float().abs().max()))
-        out = torch.empty_like(x2)
+        else:
+            # pre_feedforward_layernorm_2 fused with the NVFP4 quantisation of the experts' input
+            x2 = rms_norm_nvfp4(r, lw.norms["pre_ff_2"], c.eps, lw.a1_gs)
+        out = torch.empty(r.shape, dtype=r.dtype, device=r.device)
         M.run_moe_nvfp4(out, x2, lw.a1_gscale, lw.w1p, lw.w1p_sf, lw.w1_alphas, lw.a2_gscale, lw.w2_fp4, lw.w2_sfx,
                         lw.w2_alphas, w, ids, "gelu_tanh", w1_prepacked=True, w2_prepacked=True)
         return rms_norm(out, lw.norms["post_ff_2"], c.eps)

@@ -17,6 +17,7 @@ import ctypes
 import enum
 import threading
 import weakref
+from typing import NamedTuple
 
 import torch
 
@@ -213,6 +214,16 @@ class Workspace:
 
 # ---------------------------------------------------------------------------------------------------- operator
 
+class NVFP4Rows(NamedTuple):
+    """Token rows already quantised to NVFP4 (e.g. by a fused norm + quantise upstream), accepted by
+    :func:`run_moe_nvfp4` in place of the bf16 ``a``: packed [m, k/2] uint8 (e2m1, low nibble = even column), scales
+    [m, k/16] uint8 (e4m3, one per 16-element block, row-major), and the quant-side global scale they were made
+    with -- every expert's ``a1_gscale`` must equal it."""
+    packed: torch.Tensor
+    scales: torch.Tensor
+    gscale: float
+
+
 def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor, w1_fp4: torch.Tensor,
                   w1_blockscale: torch.Tensor, w1_alphas: torch.Tensor, a2_gscale: torch.Tensor,
                   w2_fp4: torch.Tensor, w2_blockscale: torch.Tensor, w2_alphas: torch.Tensor,
@@ -222,7 +233,8 @@ def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor
                   w2_prepacked: bool = False, workspace: torch.Tensor | None = None) -> None:
     """NVFP4 MoE experts, result written into ``output`` [m, k] (vLLM ``run_cutlass_moe_fp4`` contract).
 
-    a [m, k] bf16; a1_gscale / a2_gscale [e] fp32 quant-side scales; w1_fp4 [e, 2n, k/2] uint8 (gate rows then up
+    a [m, k] bf16, or :class:`NVFP4Rows` of the same rows quantised upstream; a1_gscale / a2_gscale [e] fp32
+    quant-side scales; w1_fp4 [e, 2n, k/2] uint8 (gate rows then up
     rows, or the interleaved layout when ``w1_prepacked``); w1_blockscale [e, 2n, k/16] e4m3 in 128x4 atoms per
     expert; w2_fp4 [e, k, n/2]; w2_blockscale [e, k, n/16]; w*_alphas [e]; topk_weights / topk_ids [m, topk].
     ``workspace13`` / ``workspace2`` are accepted for signature compatibility; the library's workspace comes from
@@ -231,12 +243,20 @@ def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor
     tensors with ``w1_prepacked`` / ``w2_prepacked``.
     """
     act = MoEActivation.parse(activation)
+    pre = a if isinstance(a, NVFP4Rows) else None
+    if pre is not None:
+        assert pre.packed.dtype == torch.uint8 and pre.scales.dtype == torch.uint8, "NVFP4Rows are uint8"
+        assert pre.scales.shape == (pre.packed.shape[0], pre.packed.shape[1] // 8), "one scale per 16 elements"
+        assert not apply_router_weight_on_input, "apply_router_weight_on_input needs bf16 rows"
+        a = pre.packed
     _require_cuda(output, a, a1_gscale, w1_fp4, w1_blockscale, w1_alphas, a2_gscale, w2_fp4, w2_blockscale,
                   w2_alphas, topk_weights, topk_ids)
     assert topk_weights.shape == topk_ids.shape, "topk shape mismatch"
     assert w1_fp4.dtype == torch.uint8 and w2_fp4.dtype == torch.uint8, "weights must be uint8 (packed e2m1)"
     assert w1_fp4.ndim == 3 and w2_fp4.ndim == 3, "weights must be rank 3"
     m_a, k_a = a.shape
+    if pre is not None:
+        k_a *= 2
     e_w1, w1_n, half_k = w1_fp4.shape
     e_w2, k_w2, half_n = w2_fp4.shape
     e = e_w1 if e is None else e
@@ -247,8 +267,8 @@ def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor
     assert k_a == half_k * 2 and k == k_w2, "hidden size mismatch between a, w1 and w2"
     assert w1_n == 2 * n and half_n * 2 == n, "mismatch in expected n (gated activations only)"
     assert m == m_a, "input shape mismatch"
-    assert a.dtype == torch.bfloat16, "a must be bf16"
-    assert output.dtype == a.dtype and tuple(output.shape) == (m, k), "output must be bf16 [m, k]"
+    assert pre is not None or a.dtype == torch.bfloat16, "a must be bf16"
+    assert output.dtype == torch.bfloat16 and tuple(output.shape) == (m, k), "output must be bf16 [m, k]"
     topk = topk_ids.size(1)
     if m == 0:
         return
@@ -280,8 +300,13 @@ def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor
     args = L.ForwardArgs(p, a.data_ptr(), a1.data_ptr(), w1p.data_ptr(), w1p_sf.data_ptr(), al1.data_ptr(),
                          a2.data_ptr(), w2_fp4.contiguous().data_ptr(), w2_sf.data_ptr(), al2.data_ptr(),
                          tw.data_ptr(), ids.data_ptr(), out.data_ptr())
-    L.check(L.lib().reaxmoe_forward(ctypes.byref(args), ws.data_ptr(), ws.numel() * ws.element_size(),
-                                    _stream(a.device)))
+    if pre is None:
+        L.check(L.lib().reaxmoe_forward(ctypes.byref(args), ws.data_ptr(), ws.numel() * ws.element_size(),
+                                        _stream(a.device)))
+    else:
+        sc = pre.scales.contiguous()
+        L.check(L.lib().reaxmoe_forward_prequant(ctypes.byref(args), sc.data_ptr(), float(pre.gscale), ws.data_ptr(),
+                                                 ws.numel() * ws.element_size(), _stream(a.device)))
     if out is not output:
         output.copy_(out)
 

@@ -104,6 +104,9 @@ def test_decision_ops_reject_bad_args():
     f = lib.reaxmoe_qkv_norm_rope
     assert f(None, None, None, None, None, None, 1e-6, 4, 16, 8, 96, None, None, None, None) == L.ERR_BAD_SHAPE
     assert f(None, None, None, None, None, None, 1e-6, 4, 16, 8, 256, None, None, None, None) == L.ERR_NULL
+    assert lib.reaxmoe_rmsnorm_nvfp4(None, None, None, None, 1e-6, 4, 2816, 0.0, None, None, None, None) == \
+        L.ERR_BAD_SHAPE
+    assert lib.reaxmoe_rmsnorm_nvfp4(None, None, None, None, 1e-6, 4, 2816, 1.0, None, None, None, None) == L.ERR_NULL
     assert lib.reaxmoe_gelu_tanh_mul(None, 4, 7, None, None) == L.ERR_BAD_SHAPE
     assert lib.reaxmoe_gelu_tanh_mul(None, 4, 704, None, None) == L.ERR_NULL
 
