@@ -226,63 +226,119 @@ __device__ __forceinline__ void store_bf16(__nv_bfloat16* p, const float* f) {
   }
 }
 
-// One CTA per token, its warps taking the token's heads in turn; D / 32 elements per lane (D = 64, 128 or 256);
-// rotate-half partner of element i is i +- D/2, i.e. lane l +- 16.
+// Grid (token, group of 32 heads): 8 warps, each taking 4 heads whose rows it loads up front as raw words, then
+// normalises and rotates them one by one. Lane l holds the rotation pairs themselves -- elements
+// [l * D/64, (l + 1) * D/64) of each half of the head -- so the rotate-half needs no exchange between lanes and
+// the only shuffles are the 5 of the row reduction (shuffles go through the MIO pipe, which a per-pair exchange
+// saturated). D = 64, 128 or 256.
+constexpr int QKV_WARPS = 8;
+constexpr int QKV_HPW = 4;                 // heads per warp
+constexpr int QKV_HEADS_PER_CTA = QKV_WARPS * QKV_HPW;
+
+template <int N>
+__device__ __forceinline__ void load_raw_bf16(const __nv_bfloat16* p, uint32_t (&w)[(N + 1) / 2]) {
+  if constexpr (N == 4) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    w[0] = v.x; w[1] = v.y;
+  } else if constexpr (N == 2) {
+    w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+  } else {
+    w[0] = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p));
+  }
+}
+template <int N>
+__device__ __forceinline__ void unpack_bf16(const uint32_t (&w)[(N + 1) / 2], float* f) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) f[i] = __uint_as_float((i & 1) ? (w[i / 2] & 0xFFFF0000u) : (w[i / 2] << 16));
+}
+template <int N>
+__device__ __forceinline__ void store_half(__nv_bfloat16* p, const float* f) {
+  if constexpr (N == 4) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]));
+  } else if constexpr (N == 2) {
+    *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(f[0], f[1]);
+  } else {
+    *p = __float2bfloat16_rn(f[0]);
+  }
+}
+
 template <int D>
-__global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                                            const __nv_bfloat16* __restrict__ qw,
-                                                            const __nv_bfloat16* __restrict__ kw,
-                                                            const __nv_bfloat16* __restrict__ cos_t,
-                                                            const __nv_bfloat16* __restrict__ sin_t,
-                                                            const int64_t* __restrict__ pos, float eps, int64_t n,
-                                                            int hq, int hk, __nv_bfloat16* __restrict__ q,
-                                                            __nv_bfloat16* __restrict__ k,
-                                                            __nv_bfloat16* __restrict__ v) {
-  constexpr int PER = D / 32;                        // elements per lane
+__global__ void __launch_bounds__(QKV_WARPS * 32) qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                                       const __nv_bfloat16* __restrict__ qw,
+                                                                       const __nv_bfloat16* __restrict__ kw,
+                                                                       const __nv_bfloat16* __restrict__ cos_t,
+                                                                       const __nv_bfloat16* __restrict__ sin_t,
+                                                                       const int64_t* __restrict__ pos, float eps,
+                                                                       int hq, int hk, __nv_bfloat16* __restrict__ q,
+                                                                       __nv_bfloat16* __restrict__ k,
+                                                                       __nv_bfloat16* __restrict__ v) {
+  constexpr int H2 = D / 64;                         // elements per lane in each half
+  constexpr int NW = (H2 + 1) / 2;
   const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int heads = hq + 2 * hk;
   const int64_t t = blockIdx.x;
-  const int64_t p = pos[t];
-  for (int h = threadIdx.x >> 5; h < heads; h += blockDim.x >> 5) {
-  float f[PER];
-  load_bf16<PER>(qkv + t * (int64_t)heads * D + (int64_t)h * D + lane * PER, f);
-  float ss = 0.0f;
+  const int hbase = blockIdx.y * QKV_HEADS_PER_CTA + warp;     // heads hbase, hbase + 8, ...
+  const int e0 = lane * H2;                          // this lane's first element in each half
+  uint32_t r1[QKV_HPW][NW], r2[QKV_HPW][NW];
 #pragma unroll
-  for (int e = 0; e < PER; ++e) ss = fmaf(f[e], f[e], ss);
-  const float r = rsqrtf(warp_sum(ss) / (float)D + eps);
-  const bool is_q = h < hq, is_k = !is_q && h < hq + hk;
-  const __nv_bfloat16* wt = is_q ? qw : (is_k ? kw : nullptr);
-  float y[PER];
-#pragma unroll
-  for (int e = 0; e < PER; ++e) y[e] = bf16r(f[e] * r);
-  __nv_bfloat16* dst;
-  if (is_q) {
-    dst = q + (t * hq + h) * (int64_t)D;
-  } else if (is_k) {
-    dst = k + (t * hk + (h - hq)) * (int64_t)D;
-  } else {
-    dst = v + (t * hk + (h - hq - hk)) * (int64_t)D;
-  }
-  if (wt) {
-    float wf[PER];
-    load_bf16<PER>(wt + lane * PER, wf);
-#pragma unroll
-    for (int e = 0; e < PER; ++e) y[e] = bf16r(y[e] * wf[e]);
-    // rotate half: x1 = elements [0, D/2) (lanes 0..15), x2 = [D/2, D) (lanes 16..31)
-    const bool first = lane < 16;
-    const int fi0 = (first ? lane : lane - 16) * PER;     // frequency index of this lane's first element
-    float cs[PER], sn[PER];
-    load_bf16<PER>(cos_t + p * (D / 2) + fi0, cs);
-    load_bf16<PER>(sin_t + p * (D / 2) + fi0, sn);
-#pragma unroll
-    for (int e = 0; e < PER; ++e) {
-      const float other = __shfl_xor_sync(0xffffffffu, y[e], 16);
-      // first half: x1 cos - x2 sin; second half: x2 cos + x1 sin -- each product and the sum rounded to bf16
-      const float a1 = bf16r(y[e] * cs[e]), a2 = bf16r(other * sn[e]);
-      y[e] = first ? bf16r(a1 - a2) : bf16r(a1 + a2);
+  for (int i = 0; i < QKV_HPW; ++i) {
+    const int h = hbase + i * QKV_WARPS;
+    if (h < heads) {
+      const __nv_bfloat16* src = qkv + t * (int64_t)heads * D + (int64_t)h * D;
+      load_raw_bf16<H2>(src + e0, r1[i]);
+      load_raw_bf16<H2>(src + D / 2 + e0, r2[i]);
     }
   }
-  store_bf16<PER>(dst + lane * PER, y);
+  const int64_t p = pos[t];
+#pragma unroll
+  for (int i = 0; i < QKV_HPW; ++i) {
+    const int h = hbase + i * QKV_WARPS;
+    if (h < heads) {                                 // uniform across the warp
+      float x1[H2], x2[H2];
+      unpack_bf16<H2>(r1[i], x1);
+      unpack_bf16<H2>(r2[i], x2);
+      float ss = 0.0f;
+#pragma unroll
+      for (int e = 0; e < H2; ++e) ss = fmaf(x1[e], x1[e], fmaf(x2[e], x2[e], ss));
+      const float r = rsqrtf(warp_sum(ss) / (float)D + eps);
+      const bool is_q = h < hq, is_k = !is_q && h < hq + hk;
+      const __nv_bfloat16* wt = is_q ? qw : (is_k ? kw : nullptr);
+#pragma unroll
+      for (int e = 0; e < H2; ++e) {
+        x1[e] = bf16r(x1[e] * r);
+        x2[e] = bf16r(x2[e] * r);
+      }
+      __nv_bfloat16* dst;
+      if (is_q) {
+        dst = q + (t * hq + h) * (int64_t)D;
+      } else if (is_k) {
+        dst = k + (t * hk + (h - hq)) * (int64_t)D;
+      } else {
+        dst = v + (t * hk + (h - hq - hk)) * (int64_t)D;
+      }
+      if (wt) {
+        uint32_t w1[NW], w2[NW], cw[NW], sw[NW];
+        load_raw_bf16<H2>(wt + e0, w1);
+        load_raw_bf16<H2>(wt + D / 2 + e0, w2);
+        load_raw_bf16<H2>(cos_t + p * (D / 2) + e0, cw);
+        load_raw_bf16<H2>(sin_t + p * (D / 2) + e0, sw);
+        float wf1[H2], wf2[H2], cs[H2], sn[H2];
+        unpack_bf16<H2>(w1, wf1);
+        unpack_bf16<H2>(w2, wf2);
+        unpack_bf16<H2>(cw, cs);
+        unpack_bf16<H2>(sw, sn);
+#pragma unroll
+        for (int e = 0; e < H2; ++e) {
+          const float a = bf16r(x1[e] * wf1[e]), b = bf16r(x2[e] * wf2[e]);
+          // x1' = x1 cos - x2 sin, x2' = x2 cos + x1 sin -- each product and the sum rounded to bf16
+          x1[e] = bf16r(bf16r(a * cs[e]) - bf16r(b * sn[e]));
+          x2[e] = bf16r(bf16r(b * cs[e]) + bf16r(a * sn[e]));
+        }
+      }
+      store_half<H2>(dst + e0, x1);
+      store_half<H2>(dst + D / 2 + e0, x2);
+    }
   }
 }
 
@@ -346,13 +402,12 @@ int launch_qkv_norm_rope(const void* qkv, const void* qw, const void* kw, const 
                          cudaStream_t s) {
   if (n == 0) return 0;
   if (n > 0x7FFFFFFFLL) return REAXMOE_ERR_BAD_SHAPE;
-  const int warps = 8;
-  const unsigned grid = (unsigned)n;
+  const dim3 grid((unsigned)n, (unsigned)((hq + 2 * hk + dops::QKV_HEADS_PER_CTA - 1) / dops::QKV_HEADS_PER_CTA));
 #define REAXMOE_QKV(DD)                                                                                          \
-  dops::qkv_norm_rope_kernel<DD><<<grid, warps * 32, 0, s>>>(                                                    \
+  dops::qkv_norm_rope_kernel<DD><<<grid, dops::QKV_WARPS * 32, 0, s>>>(                                          \
       static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(qw),                            \
       static_cast<const __nv_bfloat16*>(kw), static_cast<const __nv_bfloat16*>(cos_t),                          \
-      static_cast<const __nv_bfloat16*>(sin_t), pos, eps, n, hq, hk, static_cast<__nv_bfloat16*>(q),             \
+      static_cast<const __nv_bfloat16*>(sin_t), pos, eps, hq, hk, static_cast<__nv_bfloat16*>(q),                \
       static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v))
   switch (d) {
     case 64: REAXMOE_QKV(64); break;
