@@ -34,6 +34,7 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
 E2E_CHUNK = 4096   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
 DECISION_PROMPTS, DECISION_WARMUP, DECISION_STEPS = 64, 2, 3   # config 3 decision forward
+EP_SM_RESERVE = 0   # SMs the persistent kernels leave to the NCCL exchanges in expert-parallel runs
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
 # workload summarised in profiles/dram_traffic_cfg2.md; None where no capture covers the workload.
@@ -490,6 +491,9 @@ def run_ours_ep(args, wl: dict) -> None:
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
     El = E // world
+    sm_reserve = args.ep_sm_reserve if args.ep_sm_reserve is not None else EP_SM_RESERVE
+    if sm_reserve:
+        R.set_sm_budget(torch.cuda.get_device_properties(dev).multi_processor_count - sm_reserve)
     inp = build_inputs(dict(wl, T=256), dev, seed=0)          # shared weights, gate and static input scale
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     x = torch.randn(T, H, generator=g, device=dev).bfloat16()
@@ -615,6 +619,7 @@ def run_ours_ep(args, wl: dict) -> None:
                 data="synthetic",
                 config=dict(workload=wl["name"], tokens_per_rank=T, hidden=H, experts=E, topk=k, inter=I,
                             activation=wl["act"], parallelism=f"ep{world}", experts_per_rank=El, ep_chunks=layer.chunks,
+                            ep_sm_reserve=sm_reserve,
                             l2="inputs larger than L2 (x %.0f MB per rank, local weights %.0f MB); no flush" % (
                                 T * H * 2 / 1e6, weight_bytes / 1e6)),
                 e2e=None if e2e_value is None else dict(
@@ -645,6 +650,8 @@ def main():
     ap.add_argument("--no-decision", action="store_true", help="skip the config-3 decision forward (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count (profiling)")
     ap.add_argument("--ep-chunks", type=int, default=None, help="expert-parallel token parts in flight (N > 1)")
+    ap.add_argument("--ep-sm-reserve", type=int, default=None,
+                    help="SMs the library's persistent kernels leave free for the exchanges (N > 1)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     wl = workload(args.workload or ("cfg4" if world > 1 else "cfg2"))

@@ -117,6 +117,11 @@ int reaxmoe_forward_prequant(const reaxmoe_forward_args* args, const void* a_sca
 int reaxmoe_route(const float* logits, const float* per_expert_scale, int32_t tokens, int32_t experts,
                   int32_t topk, int32_t* topk_ids, float* topk_weights, void* stream);
 
+/* Caps the grid of this library's persistent kernels (grouped GEMMs, router, combine) at `sms` CTAs, leaving the
+ * other SMs free for kernels that run beside them -- e.g. the NCCL all-to-alls of an overlapped expert-parallel
+ * exchange. 0 (the default) = every SM of the device. Process-wide; set it between calls, not during one. */
+void reaxmoe_set_sm_budget(int32_t sms);
+
 /* Gemma-4 router fused with its routing (Gemma4Router.forward, vllm/model_executor/models/gemma4.py:251-298, as the
  * champion's router GEMM champions/uid240/opt/blink/blink_rgemm.cu:44-56 runs it, followed by gemma4.py:183-203):
  * u = bf16(bf16(bf16(rmsnorm(x)) * bf16(hidden^-1/2)) * router_scale) with rmsnorm = x * rsqrt(mean(x^2) + eps) in

@@ -60,6 +60,7 @@ SIGNATURES = {
     "reaxmoe_route": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P]),
     "reaxmoe_router_topk": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, _I32, _I32, _I32, _I32, _P, _P, _P, _P,
                                            _P]),
+    "reaxmoe_set_sm_budget": (None, [_I32]),
     "reaxmoe_rmsnorm": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, ctypes.c_int64, _I32, _P, _P]),
     "reaxmoe_qkv_norm_rope": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, ctypes.c_float, ctypes.c_int64, _I32, _I32, _I32,
                                              _P, _P, _P, _P]),

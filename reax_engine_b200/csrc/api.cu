@@ -32,11 +32,14 @@ static int cuda_check(const char* what) {
   return 0;
 }
 
+static int g_sm_budget = 0;   // 0: every SM (reaxmoe_set_sm_budget)
+
 static int num_sms() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
+  if (n <= 0) n = 148;
+  return (g_sm_budget > 0 && g_sm_budget < n) ? g_sm_budget : n;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -292,6 +295,8 @@ int reaxmoe_route(const float* logits, const float* per_expert_scale, int32_t to
                static_cast<cudaStream_t>(stream));
   return cuda_check("route");
 }
+
+void reaxmoe_set_sm_budget(int32_t sms) { g_sm_budget = sms > 0 ? sms : 0; }
 
 int reaxmoe_router_topk(const void* hidden_states, const void* router_scale, const void* router_weight,
                         const float* per_expert_scale, float eps, int32_t tokens, int32_t hidden, int32_t experts,

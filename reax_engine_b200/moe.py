@@ -58,6 +58,12 @@ def _require_cuda(*ts: torch.Tensor) -> None:
 
 # ---------------------------------------------------------------------------------------------------- routing
 
+def set_sm_budget(sms: int) -> None:
+    """Cap the library's persistent kernels at ``sms`` CTAs (0: every SM), leaving the rest of the device to work
+    that runs beside them, such as overlapped NCCL exchanges. Process-wide."""
+    L.lib().reaxmoe_set_sm_budget(int(sms))
+
+
 def route(hidden_states: torch.Tensor | None, gating_output: torch.Tensor, topk: int, renormalize: bool = True,
           per_expert_scale: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Gemma-4 routing: top-k of the fp32 router logits (ties to the lower expert id), softmax over all experts
