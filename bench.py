@@ -35,6 +35,7 @@ METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
 E2E_CHUNK = 4096   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
 DECISION_PROMPTS, DECISION_WARMUP, DECISION_STEPS = 64, 2, 3   # config 3 decision forward
 EP_SM_RESERVE = 0   # SMs the persistent kernels leave to the NCCL exchanges in expert-parallel runs
+EP_TRANSPORT = "nccl"   # expert-parallel exchange: "nccl" (two all-to-alls) or "p2p" (the kernels' own NVLink stores)
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
 # workload summarised in profiles/dram_traffic_cfg2.md; None where no capture covers the workload.
@@ -492,6 +493,7 @@ def run_ours_ep(args, wl: dict) -> None:
     T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
     El = E // world
     sm_reserve = args.ep_sm_reserve if args.ep_sm_reserve is not None else EP_SM_RESERVE
+    transport = args.ep_transport or EP_TRANSPORT
     if sm_reserve:
         R.set_sm_budget(torch.cuda.get_device_properties(dev).multi_processor_count - sm_reserve)
     inp = build_inputs(dict(wl, T=256), dev, seed=0)          # shared weights, gate and static input scale
@@ -513,6 +515,7 @@ def run_ours_ep(args, wl: dict) -> None:
         inp.pop(key)
     torch.cuda.empty_cache()
     layer = R.ep.ExpertParallelMoE(H, I, E, k, wl["act"], inp["a1_gscale"], local_w,
+                                   transport=transport,
                                    **({} if args.ep_chunks is None else {"chunks": args.ep_chunks}))
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     s = torch.cuda.current_stream(dev)
@@ -524,8 +527,9 @@ def run_ours_ep(args, wl: dict) -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
-    if layer.ops.status() != 0:
-        raise SystemExit(f"rank {rank}: device status {layer.ops.status()} after warm-up")
+    st0 = layer.status()
+    if st0 != 0:
+        raise SystemExit(f"rank {rank}: device status {st0} after warm-up")
     dist.barrier()
     torch.cuda.synchronize(dev)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -612,14 +616,14 @@ def run_ours_ep(args, wl: dict) -> None:
     decision = decision_leg(args, dev, world, rank)
 
     # route; dispatch 4 (rank ids, count, plan, pack); expert forward 8 (unpack, count, plan, permute, swizzle, w13,
-    # w2, combine); combine -- per token part
-    launches_per_step = 1 + 13 * layer.chunks
+    # w2, combine); combine -- per token part; p2p adds the three signals
+    launches_per_step = 1 + 13 * layer.chunks + (3 if transport == "p2p" else 0)
     line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
                 ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
                 data="synthetic",
                 config=dict(workload=wl["name"], tokens_per_rank=T, hidden=H, experts=E, topk=k, inter=I,
                             activation=wl["act"], parallelism=f"ep{world}", experts_per_rank=El, ep_chunks=layer.chunks,
-                            ep_sm_reserve=sm_reserve,
+                            ep_sm_reserve=sm_reserve, ep_transport=transport,
                             l2="inputs larger than L2 (x %.0f MB per rank, local weights %.0f MB); no flush" % (
                                 T * H * 2 / 1e6, weight_bytes / 1e6)),
                 e2e=None if e2e_value is None else dict(
@@ -632,6 +636,7 @@ def run_ours_ep(args, wl: dict) -> None:
                 decision=decision, cpu_baseline=None, clocks=clk.summary())
     if rank == 0:
         print(json.dumps(line), flush=True)
+    layer.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -650,6 +655,8 @@ def main():
     ap.add_argument("--no-decision", action="store_true", help="skip the config-3 decision forward (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count (profiling)")
     ap.add_argument("--ep-chunks", type=int, default=None, help="expert-parallel token parts in flight (N > 1)")
+    ap.add_argument("--ep-transport", choices=["nccl", "p2p"], default=None,
+                    help="expert-parallel exchange (N > 1): NCCL all-to-alls or the kernels' NVLink peer stores")
     ap.add_argument("--ep-sm-reserve", type=int, default=None,
                     help="SMs the library's persistent kernels leave free for the exchanges (N > 1)")
     args = ap.parse_args()

@@ -265,6 +265,55 @@ int reaxmoe_ep_expert_forward(const reaxmoe_problem* local, const void* recv_rec
 int reaxmoe_ep_combine(int32_t tokens, int32_t hidden, int32_t topk, const int32_t* send_map, const void* returned,
                        void* output, void* stream);
 
+/* ---- NVLink peer-memory transport of the expert-parallel layer: the same records and rows as above, but the
+ * pack kernel and the receiver's pre-sum kernel store them straight into the destination rank's buffers (CUDA IPC
+ * mappings of the peers' memory over NVLink; no NCCL on the data path, no multicast). It replaces the two
+ * all-to-alls of vLLM's naive EP prepare / finalize (prepare_finalize/naive_dp_ep.py:112-209). One forward on rank r:
+ *   reaxmoe_ep_dispatch_plan -> send_counts; reaxmoe_ep_signal(epoch e, send_counts) -> every rank's count matrix;
+ *   read it on the host; reaxmoe_ep_dispatch_pack (records into the peers); reaxmoe_ep_signal(e + 1);
+ *   reaxmoe_ep_expert_forward_to (rows into the sources); reaxmoe_ep_signal(e + 2); reaxmoe_ep_combine. */
+
+/* Device memory that peers can map: cudaMalloc'd, zeroed, with its 64-byte CUDA IPC handle in `handle`. */
+int reaxmoe_ipc_alloc(size_t bytes, void** ptr, void* handle);
+/* Maps a peer's reaxmoe_ipc_alloc memory (its handle) into this process; unmap with reaxmoe_ipc_close. */
+int reaxmoe_ipc_open(const void* handle, void** ptr);
+int reaxmoe_ipc_close(void* ptr);
+int reaxmoe_ipc_free(void* ptr);
+
+/* Signal block: bytes of each rank's block (from reaxmoe_ipc_alloc). Layout: int32 status at 0 (read it with
+ * reaxmoe_read_status), uint32 flags [64] at 256 (flag s written by rank s), int32 send-count matrix [64][64] at 512
+ * (row s = rank s's send_counts). */
+size_t reaxmoe_ep_signal_bytes(void);
+/* Cross-rank signal on `stream`: blocks [ranks] = every rank's signal block as mapped in this process (this rank's
+ * own at index rank). With send_counts (device [ranks]) it first writes them into row `rank` of every rank's count
+ * matrix. Then it sets flag `rank` of every block to `epoch` (after a system-scope fence that covers the earlier
+ * kernels of the stream) and waits until all of this rank's flags reach `epoch`, at most timeout_ns; a wait that
+ * runs out sets the block's status to REAXMOE_ERR_DEVICE_TIMEOUT. All ranks call it in the same order with the same
+ * epochs (start at 1, one more per call). */
+int reaxmoe_ep_signal(int32_t ranks, int32_t rank, const uint64_t* blocks, uint32_t epoch,
+                      const int32_t* send_counts, uint64_t timeout_ns, void* stream);
+
+/* reaxmoe_ep_dispatch's routing steps alone: send_counts [ranks] and the plan in `workspace`
+ * (reaxmoe_ep_dispatch_workspace_size bytes). */
+int reaxmoe_ep_dispatch_plan(const reaxmoe_problem* p, int32_t ranks, const float* a1_gscale,
+                             const int32_t* topk_ids, void* workspace, size_t workspace_bytes, int32_t* send_counts,
+                             void* stream);
+/* The pack after reaxmoe_ep_dispatch_plan on the same workspace: writes send_map as reaxmoe_ep_dispatch does and
+ * the records for rank d at records[d] (host array [ranks] of device addresses, 16-byte aligned: this rank's first
+ * record in rank d's receive buffer, i.e. base_d + rec_bytes * sum_{s < r} counts[s][d]). */
+int reaxmoe_ep_dispatch_pack(const reaxmoe_problem* p, int32_t ranks, const void* a, const float* a1_gscale,
+                             const int32_t* topk_ids, const float* topk_weights, const void* workspace,
+                             size_t workspace_bytes, int32_t* send_map, const uint64_t* records, void* stream);
+/* reaxmoe_ep_expert_forward with the pre-summed row of received record i stored at
+ * rows[s] + (i - bounds[s]) * hidden * 2 for the source s with bounds[s] <= i < bounds[s + 1] (host arrays:
+ * bounds [ranks + 1] from 0 to local->tokens, non-decreasing; rows [ranks] device addresses, 16-byte aligned:
+ * the row in rank s's return buffer of the first record s sent here). */
+int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
+                                 const void* w1_sf, const float* w1_alphas, const float* a2_gscale,
+                                 const void* w2_fp4, const void* w2_sf, const float* w2_alphas, void* workspace,
+                                 size_t workspace_bytes, int32_t ranks, const int64_t* bounds, const uint64_t* rows,
+                                 void* stream);
+
 /* Synchronises `stream`, returns the device status word of the workspace (0 = ok, else REAXMOE_ERR_*) and
  * clears it when `clear` != 0. Not for the hot path. */
 int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream);

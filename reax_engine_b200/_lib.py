@@ -87,6 +87,16 @@ SIGNATURES = {
     "reaxmoe_ep_expert_forward": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P,
                                                  _P]),
     "reaxmoe_ep_combine": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _P, _P]),
+    "reaxmoe_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "reaxmoe_ipc_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "reaxmoe_ipc_close": (ctypes.c_int, [_P]),
+    "reaxmoe_ipc_free": (ctypes.c_int, [_P]),
+    "reaxmoe_ep_signal_bytes": (ctypes.c_size_t, []),
+    "reaxmoe_ep_signal": (ctypes.c_int, [_I32, _I32, _P, ctypes.c_uint32, _P, ctypes.c_uint64, _P]),
+    "reaxmoe_ep_dispatch_plan": (ctypes.c_int, [_PP, _I32, _P, _P, _P, ctypes.c_size_t, _P, _P]),
+    "reaxmoe_ep_dispatch_pack": (ctypes.c_int, [_PP, _I32, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P]),
+    "reaxmoe_ep_expert_forward_to": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _I32,
+                                                    _P, _P, _P]),
 }
 
 _lock = threading.Lock()

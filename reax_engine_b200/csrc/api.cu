@@ -610,43 +610,92 @@ size_t reaxmoe_ep_dispatch_workspace_size(const reaxmoe_problem* p, int32_t rank
   return ep_dispatch_layout(p, ranks).total;
 }
 
-int reaxmoe_ep_dispatch(const reaxmoe_problem* p, int32_t ranks, const void* a, const float* a1_gscale,
-                        const int32_t* topk_ids, const float* topk_weights, void* workspace, size_t workspace_bytes,
-                        int32_t* send_counts, int32_t* send_map, void* send_records, void* stream) {
+// The dispatch's routing steps (rank ids, counts, plan) into the workspace; send_counts [ranks] on the device.
+static int ep_dispatch_plan(const reaxmoe_problem* p, int ranks, const float* a1_gscale, const int32_t* topk_ids,
+                            void* workspace, size_t workspace_bytes, int32_t* send_counts, cudaStream_t s,
+                            const char* who) {
   int rc = check_ep(p, ranks);
   if (rc) return rc;
   const EpDispatchLayout L = ep_dispatch_layout(p, ranks);
-  if (workspace == nullptr) return fail(REAXMOE_ERR_WORKSPACE, "ep_dispatch: workspace is NULL");
-  if (!aligned16(workspace)) return fail(REAXMOE_ERR_MISALIGNED, "ep_dispatch: workspace not 16-byte aligned");
+  if (workspace == nullptr) return fail(REAXMOE_ERR_WORKSPACE, "%s: workspace is NULL", who);
+  if (!aligned16(workspace)) return fail(REAXMOE_ERR_MISALIGNED, "%s: workspace not 16-byte aligned", who);
   if (workspace_bytes < L.total)
-    return fail(REAXMOE_ERR_WORKSPACE, "ep_dispatch: workspace %zu bytes < required %zu", workspace_bytes, L.total);
-  if (send_counts == nullptr) return fail(REAXMOE_ERR_NULL, "ep_dispatch: send_counts is NULL");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return fail(REAXMOE_ERR_WORKSPACE, "%s: workspace %zu bytes < required %zu", who, workspace_bytes, L.total);
+  if (send_counts == nullptr) return fail(REAXMOE_ERR_NULL, "%s: send_counts is NULL", who);
   uint8_t* b = static_cast<uint8_t*>(workspace);
-  int* status = reinterpret_cast<int*>(b + L.status);
-  cudaMemsetAsync(status, 0, sizeof(int), s);
+  cudaMemsetAsync(b + L.status, 0, sizeof(int), s);
   if (p->tokens == 0) {
     cudaMemsetAsync(send_counts, 0, (size_t)ranks * 4, s);
-    return cuda_check("ep_dispatch");
+    return 0;
   }
-  if (!a || !a1_gscale || !topk_ids || !topk_weights || !send_map || !send_records)
-    return fail(REAXMOE_ERR_NULL, "ep_dispatch: NULL pointer");
-  if (!aligned16(a) || !aligned16(send_records))
-    return fail(REAXMOE_ERR_MISALIGNED, "ep_dispatch: a and send_records must be 16-byte aligned");
+  if (!a1_gscale || !topk_ids) return fail(REAXMOE_ERR_NULL, "%s: NULL pointer", who);
   const int El = p->experts / ranks;
-  const int rec = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
   int* rid = reinterpret_cast<int*>(b + L.rid);
   int* seg_counts = reinterpret_cast<int*>(b + L.seg_counts);
-  int* seg_base = reinterpret_cast<int*>(b + L.seg_base);
-  int* roff = reinterpret_cast<int*>(b + L.roff);
-  launch_ep_rank_ids(topk_ids, p->tokens, p->topk, p->experts, El, a1_gscale, rid, status, s);
-  launch_count(rid, p->tokens, p->topk, ranks, seg_counts, status, s);
-  launch_plan(seg_counts, (int)ceil_div64(p->tokens, kSegTokens), ranks, seg_base, send_counts, roff,
-              reinterpret_cast<int*>(b + L.boff), reinterpret_cast<int*>(b + L.tile_prefix), nullptr, nullptr, 0, 0, 0,
-              0, s);
-  launch_ep_pack(static_cast<const __nv_bfloat16*>(a), a1_gscale, topk_ids, topk_weights, rid, seg_base, roff,
-                 p->tokens, p->hidden, p->experts, El, p->topk, rec, static_cast<uint8_t*>(send_records), send_map, s);
+  launch_ep_rank_ids(topk_ids, p->tokens, p->topk, p->experts, El, a1_gscale, rid,
+                     reinterpret_cast<int*>(b + L.status), s);
+  launch_count(rid, p->tokens, p->topk, ranks, seg_counts, reinterpret_cast<int*>(b + L.status), s);
+  launch_plan(seg_counts, (int)ceil_div64(p->tokens, kSegTokens), ranks, reinterpret_cast<int*>(b + L.seg_base),
+              send_counts, reinterpret_cast<int*>(b + L.roff), reinterpret_cast<int*>(b + L.boff),
+              reinterpret_cast<int*>(b + L.tile_prefix), nullptr, nullptr, 0, 0, 0, 0, s);
+  return 0;
+}
+
+int reaxmoe_ep_dispatch(const reaxmoe_problem* p, int32_t ranks, const void* a, const float* a1_gscale,
+                        const int32_t* topk_ids, const float* topk_weights, void* workspace, size_t workspace_bytes,
+                        int32_t* send_counts, int32_t* send_map, void* send_records, void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = ep_dispatch_plan(p, ranks, a1_gscale, topk_ids, workspace, workspace_bytes, send_counts, s,
+                            "ep_dispatch");
+  if (rc) return rc;
+  if (p->tokens == 0) return cuda_check("ep_dispatch");
+  if (!a || !topk_weights || !send_map || !send_records) return fail(REAXMOE_ERR_NULL, "ep_dispatch: NULL pointer");
+  if (!aligned16(a) || !aligned16(send_records))
+    return fail(REAXMOE_ERR_MISALIGNED, "ep_dispatch: a and send_records must be 16-byte aligned");
+  const EpDispatchLayout L = ep_dispatch_layout(p, ranks);
+  const int El = p->experts / ranks;
+  const int rec = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
+  uint8_t* b = static_cast<uint8_t*>(workspace);
+  launch_ep_pack(static_cast<const __nv_bfloat16*>(a), a1_gscale, topk_ids, topk_weights,
+                 reinterpret_cast<const int*>(b + L.rid), reinterpret_cast<const int*>(b + L.seg_base),
+                 reinterpret_cast<const int*>(b + L.roff), p->tokens, p->hidden, p->experts, El, p->topk, rec,
+                 static_cast<uint8_t*>(send_records), send_map, s);
   return cuda_check("ep_dispatch");
+}
+
+int reaxmoe_ep_dispatch_plan(const reaxmoe_problem* p, int32_t ranks, const float* a1_gscale,
+                             const int32_t* topk_ids, void* workspace, size_t workspace_bytes, int32_t* send_counts,
+                             void* stream) {
+  int rc = ep_dispatch_plan(p, ranks, a1_gscale, topk_ids, workspace, workspace_bytes, send_counts,
+                            static_cast<cudaStream_t>(stream), "ep_dispatch_plan");
+  return rc ? rc : cuda_check("ep_dispatch_plan");
+}
+
+int reaxmoe_ep_dispatch_pack(const reaxmoe_problem* p, int32_t ranks, const void* a, const float* a1_gscale,
+                             const int32_t* topk_ids, const float* topk_weights, const void* workspace,
+                             size_t workspace_bytes, int32_t* send_map, const uint64_t* records, void* stream) {
+  int rc = check_ep(p, ranks);
+  if (rc) return rc;
+  const EpDispatchLayout L = ep_dispatch_layout(p, ranks);
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(REAXMOE_ERR_WORKSPACE, "ep_dispatch_pack: workspace missing or smaller than %zu bytes", L.total);
+  if (p->tokens == 0) return 0;
+  if (!a || !a1_gscale || !topk_ids || !topk_weights || !send_map || !records)
+    return fail(REAXMOE_ERR_NULL, "ep_dispatch_pack: NULL pointer");
+  const int rec = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
+  PeerPtrs dst{};
+  for (int d = 0; d < ranks; ++d) {
+    if (records[d] == 0 || records[d] % 16 != 0)
+      return fail(REAXMOE_ERR_MISALIGNED, "ep_dispatch_pack: records[%d] is NULL or not 16-byte aligned", d);
+    dst.p[d] = records[d];
+  }
+  if (!aligned16(a)) return fail(REAXMOE_ERR_MISALIGNED, "ep_dispatch_pack: a must be 16-byte aligned");
+  const uint8_t* b = static_cast<const uint8_t*>(workspace);
+  launch_ep_pack_peer(static_cast<const __nv_bfloat16*>(a), a1_gscale, topk_ids, topk_weights,
+                      reinterpret_cast<const int*>(b + L.rid), reinterpret_cast<const int*>(b + L.seg_base),
+                      reinterpret_cast<const int*>(b + L.roff), p->tokens, p->hidden, p->experts,
+                      p->experts / ranks, p->topk, rec, dst, send_map, static_cast<cudaStream_t>(stream));
+  return cuda_check("ep_dispatch_pack");
 }
 
 size_t reaxmoe_ep_expert_workspace_size(const reaxmoe_problem* local) {
@@ -654,32 +703,33 @@ size_t reaxmoe_ep_expert_workspace_size(const reaxmoe_problem* local) {
   return ep_expert_total(local, layout(local));
 }
 
-int reaxmoe_ep_expert_forward(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
-                              const void* w1_sf, const float* w1_alphas, const float* a2_gscale, const void* w2_fp4,
-                              const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes,
-                              void* partial, void* stream) {
+// The receiver's steps; the pre-summed rows go to `partial` (route == nullptr) or along `route`.
+static int ep_expert_forward(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
+                             const void* w1_sf, const float* w1_alphas, const float* a2_gscale, const void* w2_fp4,
+                             const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes,
+                             void* partial, const RowRoute* route, cudaStream_t s, const char* who) {
   const reaxmoe_problem* p = local;
   int rc = check_problem(p, true);
   if (rc) return rc;
   const Layout L = layout(p);
   const size_t need = ep_expert_total(p, L);
-  if (workspace == nullptr) return fail(REAXMOE_ERR_WORKSPACE, "ep_expert_forward: workspace is NULL");
-  if (!aligned16(workspace)) return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_forward: workspace not 16-byte aligned");
+  if (workspace == nullptr) return fail(REAXMOE_ERR_WORKSPACE, "%s: workspace is NULL", who);
+  if (!aligned16(workspace)) return fail(REAXMOE_ERR_MISALIGNED, "%s: workspace not 16-byte aligned", who);
   if (workspace_bytes < need)
-    return fail(REAXMOE_ERR_WORKSPACE, "ep_expert_forward: workspace %zu bytes < required %zu", workspace_bytes, need);
+    return fail(REAXMOE_ERR_WORKSPACE, "%s: workspace %zu bytes < required %zu", who, workspace_bytes, need);
   if (p->tokens == 0) return 0;
-  if (!recv_records || !w1_fp4 || !w1_sf || !w1_alphas || !a2_gscale || !w2_fp4 || !w2_sf || !w2_alphas || !partial)
-    return fail(REAXMOE_ERR_NULL, "ep_expert_forward: NULL pointer");
+  if (!recv_records || !w1_fp4 || !w1_sf || !w1_alphas || !a2_gscale || !w2_fp4 || !w2_sf || !w2_alphas ||
+      (!partial && !route))
+    return fail(REAXMOE_ERR_NULL, "%s: NULL pointer", who);
   if (!aligned16(recv_records) || !aligned16(w1_fp4) || !aligned16(w1_sf) || !aligned16(w2_fp4) ||
-      !aligned16(w2_sf) || !aligned16(partial))
-    return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_forward: records, weights and partial must be 16-byte aligned");
+      !aligned16(w2_sf) || (partial && !aligned16(partial)))
+    return fail(REAXMOE_ERR_MISALIGNED, "%s: records, weights and partial must be 16-byte aligned", who);
   const WS w = carve(workspace, L);
   uint8_t* b = static_cast<uint8_t*>(workspace);
   int* lid = reinterpret_cast<int*>(b + ep_expert_lid(L));
   float* lw = reinterpret_cast<float*>(b + ep_expert_lw(p, L));
   const uint8_t* rec = static_cast<const uint8_t*>(recv_records);
   const int rec_bytes = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   launch_ep_unpack_meta(rec, p->tokens, p->topk, p->hidden, rec_bytes, lid, lw, s);
   if ((rc = do_plan(p, lid, w, nullptr, nullptr, s))) return rc;
   launch_ep_permute(rec, lid, w.seg_base, w.eoff, p->tokens, p->hidden, p->experts, p->topk, rec_bytes, w.rep_fp4,
@@ -689,11 +739,50 @@ int reaxmoe_ep_expert_forward(const reaxmoe_problem* local, const void* recv_rec
   if ((rc = cuda_check("ep_permute"))) return rc;
   const int sms = num_sms();
   GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4, w.int_sf);
-  if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "ep_expert_forward: gemm_w13 launch failed");
+  if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "%s: gemm_w13 launch failed", who);
   GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, w2_fp4, w2_sf, w2_alphas, w.c3);
-  if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "ep_expert_forward: gemm_w2 launch failed");
-  launch_combine(w.c3, w.c_map, lw, p->tokens, p->hidden, p->topk, static_cast<__nv_bfloat16*>(partial), sms, s);
-  return cuda_check("ep_expert_forward");
+  if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "%s: gemm_w2 launch failed", who);
+  if (route != nullptr)
+    launch_combine_routed(w.c3, w.c_map, lw, p->tokens, p->hidden, p->topk, *route, sms, s);
+  else
+    launch_combine(w.c3, w.c_map, lw, p->tokens, p->hidden, p->topk, static_cast<__nv_bfloat16*>(partial), sms, s);
+  return cuda_check(who);
+}
+
+int reaxmoe_ep_expert_forward(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
+                              const void* w1_sf, const float* w1_alphas, const float* a2_gscale, const void* w2_fp4,
+                              const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes,
+                              void* partial, void* stream) {
+  return ep_expert_forward(local, recv_records, w1_fp4, w1_sf, w1_alphas, a2_gscale, w2_fp4, w2_sf, w2_alphas,
+                           workspace, workspace_bytes, partial, nullptr, static_cast<cudaStream_t>(stream),
+                           "ep_expert_forward");
+}
+
+int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
+                                 const void* w1_sf, const float* w1_alphas, const float* a2_gscale,
+                                 const void* w2_fp4, const void* w2_sf, const float* w2_alphas, void* workspace,
+                                 size_t workspace_bytes, int32_t ranks, const int64_t* bounds, const uint64_t* rows,
+                                 void* stream) {
+  if (ranks < 1 || ranks > kMaxRanks) return fail(REAXMOE_ERR_BAD_SHAPE, "ep_expert_forward_to: ranks=%d", ranks);
+  if (local == nullptr || bounds == nullptr || rows == nullptr)
+    return fail(REAXMOE_ERR_NULL, "ep_expert_forward_to: NULL pointer");
+  if (bounds[0] != 0 || bounds[ranks] != local->tokens)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "ep_expert_forward_to: bounds must run from 0 to tokens=%d", local->tokens);
+  RowRoute route{};
+  route.ranks = ranks;
+  for (int q = 0; q <= ranks; ++q) {
+    if (q > 0 && bounds[q] < bounds[q - 1])
+      return fail(REAXMOE_ERR_BAD_SHAPE, "ep_expert_forward_to: bounds decrease at %d", q);
+    route.bound[q] = bounds[q];
+  }
+  for (int q = 0; q < ranks; ++q) {
+    if (bounds[q + 1] > bounds[q] && (rows[q] == 0 || rows[q] % 16 != 0))
+      return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_forward_to: rows[%d] is NULL or not 16-byte aligned", q);
+    route.p[q] = rows[q];
+  }
+  return ep_expert_forward(local, recv_records, w1_fp4, w1_sf, w1_alphas, a2_gscale, w2_fp4, w2_sf, w2_alphas,
+                           workspace, workspace_bytes, nullptr, &route, static_cast<cudaStream_t>(stream),
+                           "ep_expert_forward_to");
 }
 
 int reaxmoe_ep_combine(int32_t tokens, int32_t hidden, int32_t topk, const int32_t* send_map, const void* returned,
@@ -706,6 +795,63 @@ int reaxmoe_ep_combine(int32_t tokens, int32_t hidden, int32_t topk, const int32
   launch_ep_combine(static_cast<const __nv_bfloat16*>(returned), send_map, tokens, hidden, topk,
                     static_cast<__nv_bfloat16*>(output), num_sms(), static_cast<cudaStream_t>(stream));
   return cuda_check("ep_combine");
+}
+
+size_t reaxmoe_ep_signal_bytes(void) { return up256(kSigBytes); }
+
+int reaxmoe_ep_signal(int32_t ranks, int32_t rank, const uint64_t* blocks, uint32_t epoch,
+                      const int32_t* send_counts, uint64_t timeout_ns, void* stream) {
+  if (ranks < 1 || ranks > kMaxRanks || rank < 0 || rank >= ranks)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "ep_signal: rank=%d ranks=%d", rank, ranks);
+  if (blocks == nullptr) return fail(REAXMOE_ERR_NULL, "ep_signal: blocks is NULL");
+  PeerPtrs b{};
+  for (int d = 0; d < ranks; ++d) {
+    if (blocks[d] == 0 || blocks[d] % 256 != 0)
+      return fail(REAXMOE_ERR_MISALIGNED, "ep_signal: blocks[%d] is NULL or not 256-byte aligned", d);
+    b.p[d] = blocks[d];
+  }
+  launch_ep_signal(b, rank, ranks, epoch, send_counts, (unsigned long long)timeout_ns,
+                   static_cast<cudaStream_t>(stream));
+  return cuda_check("ep_signal");
+}
+
+int reaxmoe_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr || bytes == 0) return fail(REAXMOE_ERR_NULL, "ipc_alloc: bad argument");
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess)
+    return fail(REAXMOE_ERR_CUDA, "ipc_alloc: cudaMalloc(%zu): %s", bytes, cudaGetErrorString(cudaGetLastError()));
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    const cudaError_t e = cudaGetLastError();
+    cudaFree(p);
+    return fail(REAXMOE_ERR_CUDA, "ipc_alloc: %s", cudaGetErrorString(e));
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return 0;
+}
+
+int reaxmoe_ipc_open(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return fail(REAXMOE_ERR_NULL, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return fail(REAXMOE_ERR_CUDA, "ipc_open: %s", cudaGetErrorString(cudaGetLastError()));
+  return 0;
+}
+
+int reaxmoe_ipc_close(void* ptr) {
+  if (ptr != nullptr && cudaIpcCloseMemHandle(ptr) != cudaSuccess)
+    return fail(REAXMOE_ERR_CUDA, "ipc_close: %s", cudaGetErrorString(cudaGetLastError()));
+  return 0;
+}
+
+int reaxmoe_ipc_free(void* ptr) {
+  if (ptr != nullptr && cudaFree(ptr) != cudaSuccess)
+    return fail(REAXMOE_ERR_CUDA, "ipc_free: %s", cudaGetErrorString(cudaGetLastError()));
+  return 0;
 }
 
 int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream) {

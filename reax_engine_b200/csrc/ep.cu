@@ -54,12 +54,18 @@ __global__ void __launch_bounds__(256) ep_rank_ids_kernel(const int* __restrict_
 // (token, rank) its record index, token-major inside a rank's contiguous range; send_map [m, k] gets the record
 // index at that pair and -1 elsewhere. Phase B quantises each token row once per distinct rank scale and writes its
 // records.
+//
+// kPeer: the records go straight to their destinations, dst.p[r] being the address of this rank's first record in
+// rank r's receive buffer (a peer's memory over NVLink, or this GPU's own); `records` is unused. Every thread fences
+// its stores at system scope before it exits, so a following ep_signal_kernel publishes them.
+template <bool kPeer>
 __global__ void __launch_bounds__(256, 3) ep_pack_kernel(
     const __nv_bfloat16* __restrict__ a, const float* __restrict__ a1_gscale, const int* __restrict__ ids,
     const float* __restrict__ topk_w, const int* __restrict__ rid, const int* __restrict__ seg_base,
     const int* __restrict__ roff, int m, int H, int E, int El, int k, int rec_bytes, uint8_t* __restrict__ records,
-    int* __restrict__ send_map) {
+    int* __restrict__ send_map, const PeerPtrs dst) {
   __shared__ int run[kMaxRanks];
+  __shared__ int roff_s[kMaxRanks];
   __shared__ uint32_t mask[kMaxRanks];
   __shared__ float gq[kMaxRanks];
   __shared__ int pos_s[kSegTokens * kMaxTopk];
@@ -70,6 +76,7 @@ __global__ void __launch_bounds__(256, 3) ep_pack_kernel(
   const int nt = (int)(kSegTokens < m - t0 ? (int64_t)kSegTokens : m - t0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    roff_s[r] = roff[r];
     run[r] = roff[r] + seg_base[(int64_t)seg * R + r];
     mask[r] = 0u;
     gq[r] = __fdiv_rn(1.0f, a1_gscale[r * El]);
@@ -103,7 +110,8 @@ __global__ void __launch_bounds__(256, 3) ep_pack_kernel(
     for (int j = 0; j < k; ++j) {
       const int r = rank_s[tl * k + j];
       if (r < 0) continue;
-      uint8_t* rec = records + (int64_t)pos_s[tl * k + j] * rec_bytes;
+      uint8_t* rec = kPeer ? reinterpret_cast<uint8_t*>(dst.p[r]) + (int64_t)(pos_s[tl * k + j] - roff_s[r]) * rec_bytes
+                           : records + (int64_t)pos_s[tl * k + j] * rec_bytes;
       if (lane < k) {
         const int lid = ((unsigned)my_id < (unsigned)E && my_id / El == r) ? my_id - r * El : -1;
         reinterpret_cast<int*>(rec + meta)[lane] = lid;
@@ -131,12 +139,58 @@ __global__ void __launch_bounds__(256, 3) ep_pack_kernel(
             sbytes |= quant_block16_bf16(xw, g, w[2 * b], w[2 * b + 1]) << (8 * b);
           }
         }
-        uint8_t* rec = records + (int64_t)pos_s[tl * k + j] * rec_bytes;
+        uint8_t* rec = kPeer ? reinterpret_cast<uint8_t*>(dst.p[r]) +
+                                   (int64_t)(pos_s[tl * k + j] - roff_s[r]) * rec_bytes
+                             : records + (int64_t)pos_s[tl * k + j] * rec_bytes;
         *reinterpret_cast<uint4*>(rec + un * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         *reinterpret_cast<uint16_t*>(rec + H / 2 + un * 2) = (uint16_t)sbytes;
       }
     }
   }
+  if (kPeer) __threadfence_system();
+}
+
+__device__ __forceinline__ uint64_t clock_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Cross-rank signal (a barrier with an optional payload), one CTA of kMaxRanks threads. Thread d < ranks: when
+// `counts` is given, writes this rank's send counts [ranks] into row `rank` of rank d's count matrix; then, after a
+// system-scope fence (which also covers the stores of the kernels before this one in the stream, e.g. the peer
+// pack), releases flag `rank` of rank d's block with `epoch`. Then thread d waits, with acquire loads and at most
+// timeout_ns, until this rank's flag d reaches `epoch` (compared modulo 2^32); a wait that runs out sets this rank's
+// status word to REAXMOE_ERR_DEVICE_TIMEOUT and returns. Every rank calls the signals in the same order with the
+// same epochs, so when the kernel ends every peer has passed its matching signal and its earlier stores to this GPU
+// are visible.
+__global__ void __launch_bounds__(kMaxRanks) ep_signal_kernel(const PeerPtrs blocks, int rank, int ranks,
+                                                              uint32_t epoch, const int* __restrict__ counts,
+                                                              unsigned long long timeout_ns) {
+  const int d = threadIdx.x;
+  __threadfence_system();
+  if (d < ranks) {
+    uint8_t* peer = reinterpret_cast<uint8_t*>(blocks.p[d]);
+    if (counts != nullptr) {
+      int* row = reinterpret_cast<int*>(peer + kSigCounts) + rank * kMaxRanks;
+      for (int i = 0; i < ranks; ++i) row[i] = counts[i];
+    }
+    uint32_t* flag = reinterpret_cast<uint32_t*>(peer + kSigFlags) + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
+    uint8_t* own = reinterpret_cast<uint8_t*>(blocks.p[rank]);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(own + kSigFlags) + d;
+    const uint64_t t0 = clock_ns();
+    for (uint32_t n = 0;; ++n) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if ((n & 15u) == 15u && clock_ns() - t0 > timeout_ns) {
+        set_status(reinterpret_cast<int*>(own + kSigStatus), REAXMOE_ERR_DEVICE_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
 }
 
 // Receiver: local expert ids and weights of every received record, as contiguous [n, k] arrays.
@@ -262,8 +316,24 @@ int launch_ep_pack(const __nv_bfloat16* a, const float* a1_gscale, const int* id
                    uint8_t* records, int* send_map, cudaStream_t s) {
   const int nseg = (int)ceil_div64(m, kSegTokens);
   if (nseg > 0)
-    ep_pack_kernel<<<nseg, 256, 0, s>>>(a, a1_gscale, ids, w, rid, seg_base, roff, m, H, E, El, k, rec_bytes, records,
-                                        send_map);
+    ep_pack_kernel<false><<<nseg, 256, 0, s>>>(a, a1_gscale, ids, w, rid, seg_base, roff, m, H, E, El, k, rec_bytes,
+                                               records, send_map, PeerPtrs{});
+  return 0;
+}
+
+int launch_ep_pack_peer(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const float* w, const int* rid,
+                        const int* seg_base, const int* roff, int m, int H, int E, int El, int k, int rec_bytes,
+                        const PeerPtrs& records, int* send_map, cudaStream_t s) {
+  const int nseg = (int)ceil_div64(m, kSegTokens);
+  if (nseg > 0)
+    ep_pack_kernel<true><<<nseg, 256, 0, s>>>(a, a1_gscale, ids, w, rid, seg_base, roff, m, H, E, El, k, rec_bytes,
+                                              nullptr, send_map, records);
+  return 0;
+}
+
+int launch_ep_signal(const PeerPtrs& blocks, int rank, int ranks, uint32_t epoch, const int* counts,
+                     unsigned long long timeout_ns, cudaStream_t s) {
+  ep_signal_kernel<<<1, kMaxRanks, 0, s>>>(blocks, rank, ranks, epoch, counts, timeout_ns);
   return 0;
 }
 

@@ -400,11 +400,29 @@ __device__ __forceinline__ uint4 combine_finish(float (&part)[4][8], int k) {
   return o;
 }
 
-template <int K>
+// Where row t goes: PlainRows writes out[t]; RoutedRows sends the row of record t to its source rank's return buffer
+// (RowRoute; a peer's memory over NVLink or this GPU's own) and fences the stores at system scope before the thread
+// exits, so that a following ep_signal_kernel publishes them.
+struct PlainRows {
+  static constexpr bool kPeer = false;
+  __nv_bfloat16* out;
+  __device__ __forceinline__ uint4* row(int64_t t, int H) const { return reinterpret_cast<uint4*>(out + t * H); }
+};
+struct RoutedRows {
+  static constexpr bool kPeer = true;
+  RowRoute r;
+  __device__ __forceinline__ uint4* row(int64_t t, int H) const {
+    int src = 0;
+    for (int q = 1; q < r.ranks; ++q) src += (t >= r.bound[q]) ? 1 : 0;
+    return reinterpret_cast<uint4*>(r.p[src] + (uint64_t)(t - r.bound[src]) * (uint64_t)H * 2u);
+  }
+};
+
+template <int K, class Rows>
 __global__ void __launch_bounds__(256, 3) combine_kernel_k(const __nv_bfloat16* __restrict__ c3,
                                                            const int* __restrict__ c_map,
                                                            const float* __restrict__ topk_w, int m, int H,
-                                                           __nv_bfloat16* __restrict__ out) {
+                                                           const __grid_constant__ Rows out) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int nch = H / 8;
@@ -425,7 +443,7 @@ __global__ void __launch_bounds__(256, 3) combine_kernel_k(const __nv_bfloat16* 
       valid[j] = pj >= 0;  // -1 marks a pair whose expert id was out of range (flagged by the plan)
       rowp[j] = reinterpret_cast<const uint4*>(c3 + (int64_t)(valid[j] ? pj : 0) * H);
     }
-    uint4* orow = reinterpret_cast<uint4*>(out + t * H);
+    uint4* orow = out.row(t, H);
     for (int ch = lane; ch < nch; ch += 32) {
       uint4 v[K];
 #pragma unroll
@@ -436,12 +454,14 @@ __global__ void __launch_bounds__(256, 3) combine_kernel_k(const __nv_bfloat16* 
       orow[ch] = combine_finish(part, K);
     }
   }
+  if (Rows::kPeer) __threadfence_system();
 }
 
+template <class Rows>
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ c3,
                                                       const int* __restrict__ c_map,
                                                       const float* __restrict__ topk_w, int m, int H, int k,
-                                                      __nv_bfloat16* __restrict__ out) {
+                                                      const __grid_constant__ Rows out) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < m; t += warps) {
@@ -468,9 +488,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
           combine_accumulate(v, wb[j], j, part);
         }
       }
-      reinterpret_cast<uint4*>(out + t * H)[ch] = combine_finish(part, k);
+      out.row(t, H)[ch] = combine_finish(part, k);
     }
   }
+  if (Rows::kPeer) __threadfence_system();
 }
 
 // ------------------------------------------------------------------------------------------------------
@@ -620,16 +641,31 @@ int launch_permute_fp4(const uint8_t* a_fp4, const uint8_t* a_sf, float in_gscal
   return 0;
 }
 
+template <class Rows>
+static void launch_combine_rows(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
+                                const Rows& out, unsigned blocks, cudaStream_t s) {
+  if (k == 8) combine_kernel_k<8, Rows><<<blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
+  else if (k == 4) combine_kernel_k<4, Rows><<<blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
+  else if (k == 2) combine_kernel_k<2, Rows><<<blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
+  else if (k == 1) combine_kernel_k<1, Rows><<<blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
+  else combine_kernel<Rows><<<blocks, 256, 0, s>>>(c3, c_map, w, m, H, k, out);
+}
+
 int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
                    __nv_bfloat16* out, int num_sms, cudaStream_t s) {
   if (m == 0) return 0;
   const int64_t want = ceil_div64(m, 8), cap = (int64_t)num_sms * 12;
   const int64_t blocks = want < cap ? want : cap;
-  if (k == 8) combine_kernel_k<8><<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
-  else if (k == 4) combine_kernel_k<4><<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
-  else if (k == 2) combine_kernel_k<2><<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
-  else if (k == 1) combine_kernel_k<1><<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, out);
-  else combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(c3, c_map, w, m, H, k, out);
+  launch_combine_rows(c3, c_map, w, m, H, k, PlainRows{out}, (unsigned)blocks, s);
+  return 0;
+}
+
+int launch_combine_routed(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
+                          const RowRoute& route, int num_sms, cudaStream_t s) {
+  if (m == 0) return 0;
+  const int64_t want = ceil_div64(m, 8), cap = (int64_t)num_sms * 12;
+  const int64_t blocks = want < cap ? want : cap;
+  launch_combine_rows(c3, c_map, w, m, H, k, RoutedRows{route}, (unsigned)blocks, s);
   return 0;
 }
 

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace reaxmoe {
 
 int launch_route(const float* logits, const float* scale, int T, int E, int K, int* ids, float* w, cudaStream_t s);
@@ -38,6 +40,33 @@ int launch_ep_permute(const uint8_t* records, const int* lid, const int* seg_bas
                       int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, cudaStream_t s);
 int launch_ep_combine(const __nv_bfloat16* ret, const int* map, int m, int H, int k, __nv_bfloat16* out, int num_sms,
                       cudaStream_t s);
+
+// Peer-memory (NVLink) transport of the expert-parallel layer. Addresses are device virtual addresses valid in this
+// process: this GPU's own buffers or peers' buffers mapped through CUDA IPC.
+struct PeerPtrs {
+  uint64_t p[kMaxRanks];
+};
+// Destination of the pre-summed row of received record i: rows.p[s] + (i - bound[s]) * row_bytes for the source s
+// with bound[s] <= i < bound[s + 1].
+struct RowRoute {
+  uint64_t p[kMaxRanks];
+  int64_t bound[kMaxRanks + 1];
+  int ranks;
+};
+// Signal block (one per rank, peer-mapped): status word, one flag per source rank, the [ranks, ranks] send-count
+// matrix (row s written by rank s).
+constexpr int kSigStatus = 0;
+constexpr int kSigFlags = 256;
+constexpr int kSigCounts = 512;
+constexpr size_t kSigBytes = 512 + 4 * kMaxRanks * kMaxRanks;
+// pack with records[d] = address of this rank's first record in rank d's receive buffer
+int launch_ep_pack_peer(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const float* w, const int* rid,
+                        const int* seg_base, const int* roff, int m, int H, int E, int El, int k, int rec_bytes,
+                        const PeerPtrs& records, int* send_map, cudaStream_t s);
+int launch_combine_routed(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
+                          const RowRoute& route, int num_sms, cudaStream_t s);
+int launch_ep_signal(const PeerPtrs& blocks, int rank, int ranks, uint32_t epoch, const int* counts,
+                     unsigned long long timeout_ns, cudaStream_t s);
 
 // Grouped NVFP4 GEMM (gemm_sm100.cu). mode 0: out bf16 [slots, N]; mode 1: fused act(gate)*up + NVFP4 quant
 // into q_out [slots, N/4] (N = 2*inter interleaved) and q_sf atoms.

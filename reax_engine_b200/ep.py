@@ -1,5 +1,7 @@
 """Expert-parallel NVFP4 MoE layer: one process per GPU, experts split evenly over the ranks of a
-``torch.distributed`` process group, tokens exchanged with two NCCL all-to-alls.
+``torch.distributed`` process group, tokens exchanged either with two NCCL all-to-alls (``transport="nccl"``) or by
+the kernels themselves over NVLink (``transport="p2p"``: the pack and pre-sum kernels store straight into the peers'
+CUDA-IPC-mapped buffers; :class:`PeerExchange`).
 
 The reference runs this layer with ``ep_size == 1`` only (``champions/uid240/opt/blink/blink_par.py:99``); vLLM
 defines the interface this mirrors: ``FusedMoEPrepareAndFinalize.prepare`` quantises and dispatches the tokens,
@@ -128,6 +130,62 @@ class DeviceOps:
                                                   _stream(self.device)))
         return partial
 
+    # ---- the peer-memory transport's device halves (see PeerExchange)
+    def plan(self, a1_gscale: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+        """Routing steps of the dispatch alone -> send_counts [R] int32 on the device (plan kept in the workspace)."""
+        _require_cuda(a1_gscale, topk_ids)
+        T = topk_ids.shape[0]
+        self._p_disp = L.problem(T, self.H, self.I, self.E, self.k, self.act)
+        need = L.lib().reaxmoe_ep_dispatch_workspace_size(ctypes.byref(self._p_disp), self.R)
+        if need == 0:
+            raise L.ReaxMoEError(L.ERR_BAD_SHAPE, L.last_error())
+        self._ws_disp = self.buf.get("dispatch_ws0", need)
+        counts = torch.empty(self.R, dtype=torch.int32, device=self.device)
+        L.check(L.lib().reaxmoe_ep_dispatch_plan(ctypes.byref(self._p_disp), self.R, a1_gscale.data_ptr(),
+                                                 topk_ids.data_ptr(), self._ws_disp.data_ptr(), self._ws_disp.numel(),
+                                                 counts.data_ptr(), _stream(self.device)))
+        return counts
+
+    def pack_to(self, a: torch.Tensor, a1_gscale: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                records: list[int]) -> torch.Tensor:
+        """The pack after :meth:`plan`: rank d's records go to device address records[d] -> send_map [T, k]."""
+        _require_cuda(a, topk_weights)
+        T = a.shape[0]
+        send_map = torch.empty(T, self.k, dtype=torch.int32, device=self.device)
+        dst = (ctypes.c_uint64 * self.R)(*records)
+        L.check(L.lib().reaxmoe_ep_dispatch_pack(ctypes.byref(self._p_disp), self.R, a.data_ptr(),
+                                                 a1_gscale.data_ptr(), topk_ids.data_ptr(), topk_weights.data_ptr(),
+                                                 self._ws_disp.data_ptr(), self._ws_disp.numel(), send_map.data_ptr(),
+                                                 dst, _stream(self.device)))
+        return send_map
+
+    def expert_forward_to(self, records_ptr: int, n: int, w: LocalExperts, bounds: list[int],
+                          rows: list[int]) -> None:
+        """Local experts over the n records at records_ptr; the row of record i goes to rows[s] + (i - bounds[s]) rows
+        for its source s."""
+        p = L.problem(n, self.H, self.I, self.El, self.k, self.act)
+        need = L.lib().reaxmoe_ep_expert_workspace_size(ctypes.byref(p))
+        if need == 0:
+            raise L.ReaxMoEError(L.ERR_BAD_SHAPE, L.last_error())
+        ws = self.buf.get("expert_ws0", need)
+        if n == 0:
+            return
+        b = (ctypes.c_int64 * (self.R + 1))(*bounds)
+        r = (ctypes.c_uint64 * self.R)(*rows)
+        L.check(L.lib().reaxmoe_ep_expert_forward_to(ctypes.byref(p), records_ptr, w.w1_fp4.data_ptr(),
+                                                     w.w1_sf.data_ptr(), w.w1_alphas.data_ptr(),
+                                                     w.a2_gscale.data_ptr(), w.w2_fp4.data_ptr(), w.w2_sf.data_ptr(),
+                                                     w.w2_alphas.data_ptr(), ws.data_ptr(), ws.numel(), self.R, b, r,
+                                                     _stream(self.device)))
+
+    def signal(self, rank: int, blocks: list[int], epoch: int, counts: torch.Tensor | None,
+               timeout_s: float) -> None:
+        """``reaxmoe_ep_signal`` on the current stream (a barrier with the optional send-count payload)."""
+        bl = (ctypes.c_uint64 * self.R)(*blocks)
+        L.check(L.lib().reaxmoe_ep_signal(self.R, rank, bl, epoch & 0xFFFFFFFF,
+                                          None if counts is None else counts.data_ptr(), int(timeout_s * 1e9),
+                                          _stream(self.device)))
+
     def combine(self, send_map: torch.Tensor, returned: torch.Tensor, output: torch.Tensor) -> None:
         T = send_map.shape[0]
         L.check(L.lib().reaxmoe_ep_combine(T, self.H, self.k, send_map.data_ptr(), returned.data_ptr(),
@@ -141,6 +199,136 @@ class DeviceOps:
                 v = L.lib().reaxmoe_read_status(b.data_ptr(), b.numel(), 1, _stream(self.device))
                 rc = rc or v
         return rc
+
+
+class _DevicePointer:
+    """A raw device allocation as a ``__cuda_array_interface__`` exporter (a torch view of it, no ownership)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+def device_view(ptr: int, nbytes: int, device) -> torch.Tensor:
+    """uint8 [nbytes] tensor over the device memory at ptr (this GPU's own)."""
+    return torch.as_tensor(_DevicePointer(ptr, nbytes), device=device)
+
+
+class PeerMemory:
+    """One device buffer per rank of ``group`` (``reaxmoe_ipc_alloc``), mapped into every rank through CUDA IPC:
+    ``ptrs[q]`` is rank q's buffer as this process addresses it (over NVLink for q != rank). Collective: every rank
+    constructs and closes it at the same point."""
+
+    def __init__(self, nbytes: int, group, device):
+        self.group, self.device, self.nbytes = group, torch.device(device), int(nbytes)
+        self.R, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        L.check(L.lib().reaxmoe_ipc_alloc(self.nbytes, ctypes.byref(own), handle))
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        every = torch.empty(self.R * 64, dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        hs = every.cpu().numpy().reshape(self.R, 64)
+        self.ptrs: list[int] = []
+        self._opened: list[int] = []
+        for q in range(self.R):
+            if q == self.rank:
+                self.ptrs.append(own.value)
+                continue
+            p = ctypes.c_void_p()
+            L.check(L.lib().reaxmoe_ipc_open(hs[q].tobytes(), ctypes.byref(p)))
+            self.ptrs.append(p.value)
+            self._opened.append(p.value)
+        self.own = own.value
+        self.view = device_view(self.own, self.nbytes, self.device)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then (after every rank has) free this rank's own."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            L.check(L.lib().reaxmoe_ipc_close(p))
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.view = None
+        L.check(L.lib().reaxmoe_ipc_free(self.own))
+        self.own = None
+
+
+def p2p_addresses(counts, rank: int, rec_bytes: int, row_bytes: int, recv_base: list[int],
+                  ret_base: list[int]) -> tuple[list[int], list[int], list[int], int, int]:
+    """Where one forward's stores go on ``rank``, from the count matrix counts[s][d] (records rank s sends to rank d;
+    every rank holds the same matrix):
+
+    * records[d] = recv_base[d] + rec_bytes * sum_{s < rank} counts[s][d]: this rank's first record in rank d's
+      receive buffer (sources stacked in rank order, as the records all-to-all would leave them);
+    * bounds[s] = sum_{s' < s} counts[s'][rank] (R + 1 entries): the records received here from source s are
+      [bounds[s], bounds[s + 1]);
+    * rows[s] = ret_base[s] + row_bytes * sum_{d < rank} counts[s][d]: where the row of the first record source s sent
+      here goes in s's return buffer (destinations stacked in rank order, i.e. s's send-record order, as the reverse
+      all-to-all would leave them);
+    * n_recv = bounds[R], n_send = sum_d counts[rank][d]."""
+    R = len(counts)
+    records = [recv_base[d] + rec_bytes * sum(counts[s][d] for s in range(rank)) for d in range(R)]
+    bounds = [0]
+    for s in range(R):
+        bounds.append(bounds[-1] + counts[s][rank])
+    rows = [ret_base[s] + row_bytes * sum(counts[s][d] for d in range(rank)) for s in range(R)]
+    return records, bounds, rows, bounds[R], sum(counts[rank])
+
+
+class PeerExchange:
+    """The NVLink peer-memory transport of :class:`ExpertParallelMoE`: per rank a receive buffer for records, a return
+    buffer for rows and a signal block, all CUDA-IPC mapped by every rank. The pack kernel stores each record straight
+    into its destination's receive buffer and the receiver's pre-sum kernel stores each row straight into its
+    source's return buffer; ``reaxmoe_ep_signal`` (flags in the signal blocks, bounded waits) orders the phases.
+    Buffers grow (collectively: every rank sees the same count matrix, so all decide alike) when a forward needs more
+    than they hold."""
+
+    def __init__(self, ops: "DeviceOps", group, device, timeout_s: float = 10.0, headroom: float = 1.25):
+        self.ops, self.group, self.device = ops, group, torch.device(device)
+        self.R, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.timeout_s, self.headroom = timeout_s, headroom
+        self.epoch = 0
+        self.sig = PeerMemory(int(L.lib().reaxmoe_ep_signal_bytes()), group, device)
+        self.recv: PeerMemory | None = None
+        self.ret: PeerMemory | None = None
+
+    def signal(self, counts: torch.Tensor | None = None) -> None:
+        self.epoch += 1
+        self.ops.signal(self.rank, self.sig.ptrs, self.epoch, counts, self.timeout_s)
+
+    def count_matrix(self) -> list[list[int]]:
+        """Synchronises; the [R, R] send-count matrix of the last signal with counts. Raises on a device status."""
+        head = self.sig.view[:512 + 4 * 64 * self.R].view(torch.int32).cpu()
+        status = int(head[0])
+        if status != 0:
+            raise L.ReaxMoEError(status, f"rank {self.rank}: peer signal status {status} "
+                                         "(a rank did not reach the signal in time)")
+        return head[128:].view(self.R, 64)[:, :self.R].tolist()
+
+    def ensure(self, counts: list[list[int]], rec_bytes: int, row_bytes: int) -> None:
+        """Grow the receive / return buffers to hold this forward's records and rows on every rank."""
+        R = self.R
+        recv_need = max(sum(counts[s][d] for s in range(R)) for d in range(R)) * rec_bytes
+        ret_need = max(sum(counts[s]) for s in range(R)) * row_bytes
+        if self.recv is not None and self.recv.nbytes >= recv_need and self.ret.nbytes >= ret_need:
+            return
+        grow = lambda need, cur: max(int(need * self.headroom), 1 << 20, cur.nbytes if cur is not None else 0)
+        new_recv, new_ret = grow(recv_need, self.recv), grow(ret_need, self.ret)
+        for m in (self.recv, self.ret):
+            if m is not None:
+                m.close()
+        self.recv = PeerMemory(-(-new_recv // 4096) * 4096, self.group, self.device)
+        self.ret = PeerMemory(-(-new_ret // 4096) * 4096, self.group, self.device)
+
+    def close(self) -> None:
+        for m in (self.recv, self.ret, self.sig):
+            if m is not None:
+                m.close()
+        self.recv = self.ret = None
 
 
 def _a2a_rows(out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int], group,
@@ -163,7 +351,8 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, hidden: int, inter: int, experts: int, topk: int, activation, a1_gscale: torch.Tensor,
-                 local: LocalExperts, group=None, ops=None, chunks: int = 1):
+                 local: LocalExperts, group=None, ops=None, chunks: int = 1, transport: str = "nccl",
+                 timeout_s: float = 10.0):
         self.group = group
         self.R = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -179,6 +368,25 @@ class ExpertParallelMoE:
         self.chunks = max(1, int(chunks))
         self.last_counts: tuple[list[int], list[int]] | None = None
         self.marks: list | None = None   # set to [] to collect (phase, CUDA event) pairs during forward
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport must be 'nccl' or 'p2p', got {transport!r}")
+        self.transport = transport
+        self.peer = PeerExchange(self.ops, group, self.device, timeout_s) if transport == "p2p" else None
+
+    def status(self) -> int:
+        """Synchronise; the first non-zero device status of the last forward (kernels, and the peer signals' waits
+        with the p2p transport), cleared; 0 = ok."""
+        rc = self.ops.status()
+        if self.peer is not None:
+            v = L.lib().reaxmoe_read_status(self.peer.sig.own, self.peer.sig.nbytes, 1, _stream(self.device))
+            rc = rc or v
+        return rc
+
+    def close(self) -> None:
+        """Release the peer buffers (collective: every rank calls it at the same point). NCCL transport: no-op."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def _mark(self, name: str) -> None:
         if self.marks is not None and self.device.type == "cuda":
@@ -199,6 +407,8 @@ class ExpertParallelMoE:
         a = a.contiguous()
         ids = topk_ids.to(torch.int32).contiguous()
         tw = topk_weights.float().contiguous()
+        if self.transport == "p2p":
+            return self._forward_p2p(a, tw, ids, output)
         n = self.chunks
         step = -(-T // n) if T else 0
         bounds = [(min(T, c * step), min(T, (c + 1) * step)) for c in range(n)]
@@ -232,6 +442,40 @@ class ExpertParallelMoE:
         for c, (t0, t1) in enumerate(bounds):
             row_work[c].wait()
             self.ops.combine(disp[c][1], rets[c], out[t0:t1])
+        self._mark("combine")
+        return out
+
+    def _forward_p2p(self, a: torch.Tensor, tw: torch.Tensor, ids: torch.Tensor,
+                     output: torch.Tensor | None) -> torch.Tensor:
+        """One forward over the peer-memory transport (rank r):
+
+        1. plan (counts per destination); signal with the counts -> every rank's count matrix; host reads it
+           (the one host synchronisation, as the NCCL transport's count exchange);
+        2. pack: each record stored straight into its destination's receive buffer; signal;
+        3. experts on the received records; each pre-summed row stored straight into its source's return buffer;
+           signal;
+        4. combine from the local return buffer.
+        Bit-identical to the NCCL transport: the same records in the same order, the same rows, the same sums."""
+        px = self.peer
+        T = a.shape[0]
+        self._mark("start")
+        counts = self.ops.plan(self.a1_gscale, ids)
+        px.signal(counts)
+        C = px.count_matrix()
+        rec_bytes, row_bytes = self.ops.rec, self.H * 2
+        px.ensure(C, rec_bytes, row_bytes)
+        records, bounds, rows, n_recv, n_send = p2p_addresses(C, self.rank, rec_bytes, row_bytes, px.recv.ptrs,
+                                                              px.ret.ptrs)
+        self.last_counts = (list(C[self.rank]), [C[s][self.rank] for s in range(self.R)])
+        send_map = self.ops.pack_to(a, self.a1_gscale, ids, tw, records)
+        px.signal()
+        self._mark("dispatch")
+        self.ops.expert_forward_to(px.recv.own, n_recv, self.local, bounds, rows)
+        px.signal()
+        self._mark("experts")
+        out = output if output is not None else torch.empty(T, self.H, dtype=torch.bfloat16, device=a.device)
+        ret = px.ret.view[:n_send * row_bytes].view(torch.bfloat16).view(n_send, self.H)
+        self.ops.combine(send_map, ret, out)
         self._mark("combine")
         return out
 

@@ -148,3 +148,25 @@ def test_ep_entry_points_reject_bad_args():
     assert lib.reaxmoe_ep_combine(4, 2816, 8, None, None, None, None) == L.ERR_NULL
     assert lib.reaxmoe_ep_combine(0, 2816, 8, None, None, None, None) == L.OK
     assert lib.reaxmoe_ep_combine(4, 2800, 8, None, None, None, None) == L.ERR_BAD_SHAPE
+
+
+def test_p2p_entry_points_reject_bad_args():
+    """The peer-memory transport's entries check their arguments before touching the device."""
+    blocks = (ctypes.c_uint64 * 2)(0, 0)
+    assert L.lib().reaxmoe_ep_signal(2, 0, blocks, 1, None, 1000, None) == L.ERR_MISALIGNED
+    assert L.lib().reaxmoe_ep_signal(2, 2, blocks, 1, None, 1000, None) == L.ERR_BAD_SHAPE
+    assert L.lib().reaxmoe_ep_signal(65, 0, blocks, 1, None, 1000, None) == L.ERR_BAD_SHAPE
+    p = L.problem(4, 256, 256, 8, 4, 0)
+    bounds = (ctypes.c_int64 * 3)(0, 3, 3)
+    rows = (ctypes.c_uint64 * 2)(0, 0)
+    args = [None] * 8 + [None, 0]
+    assert L.lib().reaxmoe_ep_expert_forward_to(ctypes.byref(p), *args, 2, bounds, rows, None) == L.ERR_BAD_SHAPE
+    bounds = (ctypes.c_int64 * 3)(0, 3, 2)
+    assert L.lib().reaxmoe_ep_expert_forward_to(ctypes.byref(p), *args, 2, bounds, rows, None) == L.ERR_BAD_SHAPE
+    bounds = (ctypes.c_int64 * 3)(0, 3, 4)
+    assert L.lib().reaxmoe_ep_expert_forward_to(ctypes.byref(p), *args, 2, bounds, rows, None) == L.ERR_MISALIGNED
+    recs = (ctypes.c_uint64 * 2)(16, 8)
+    assert L.lib().reaxmoe_ep_dispatch_pack(ctypes.byref(p), 2, 16, 16, 16, 16, 16, 1 << 20, 16, recs,
+                                            None) == L.ERR_MISALIGNED
+    assert L.lib().reaxmoe_ipc_alloc(0, ctypes.byref(ctypes.c_void_p()), None) == L.ERR_NULL
+    assert L.lib().reaxmoe_ep_signal_bytes() >= 512 + 4 * 64 * 64

@@ -212,3 +212,42 @@ def test_expert_parallel_exchange_gloo_world2(Ts, local_only, chunks):
     mp.start_processes(_worker, args=(2, _free_port(), Ts, local_only, chunks, errq), nprocs=2, join=True,
                        start_method="spawn")
     assert errq.empty(), errq.get()
+
+
+@pytest.mark.parametrize("R,seed", [(2, 0), (3, 1), (4, 2), (8, 3)])
+def test_p2p_addresses_reproduce_the_all_to_all_layout(R, seed):
+    """The peer-memory transport's store addresses (reax_engine_b200.ep.p2p_addresses) leave every receive buffer
+    and every return buffer exactly as the two all-to-alls of the NCCL transport do: records source-major in send
+    order, returned rows in each source's send-record order. Memory is simulated as one flat array per rank with
+    distinct base addresses; a record / row is identified by (source, destination, index)."""
+    rng = np.random.default_rng(seed)
+    C = rng.integers(0, 6, size=(R, R)).tolist()
+    C[0][R - 1] = 0                                   # an empty pair
+    rec, row = 16, 32                                  # bytes; one int64 id at the start of each slot
+    recv_base = [(q + 1) << 24 for q in range(R)]
+    ret_base = [(q + 1) << 28 for q in range(R)]
+    mem: dict[int, int] = {}                           # address -> id
+
+    def ident(s, d, j):
+        return (s * 64 + d) * 4096 + j
+
+    for r in range(R):                                 # dispatch: rank r stores its records for d
+        records, _, _, _, _ = EP.p2p_addresses(C, r, rec, row, recv_base, ret_base)
+        for d in range(R):
+            for j in range(C[r][d]):
+                mem[records[d] + j * rec] = ident(r, d, j)
+    for d in range(R):                                 # receive buffers = the records all-to-all's output
+        expect = [ident(s, d, j) for s in range(R) for j in range(C[s][d])]
+        assert [mem.get(recv_base[d] + i * rec) for i in range(len(expect))] == expect
+    for d in range(R):                                 # expert side: record i's row goes back to its source
+        _, bounds, rows, n_recv, _ = EP.p2p_addresses(C, d, rec, row, recv_base, ret_base)
+        assert n_recv == sum(C[s][d] for s in range(R))
+        for i in range(n_recv):
+            s = max(q for q in range(R) if bounds[q] <= i)
+            rid = mem[recv_base[d] + i * rec]
+            mem[rows[s] + (i - bounds[s]) * row] = -rid
+    for s in range(R):                                 # return buffers = the reverse all-to-all's output
+        _, _, _, _, n_send = EP.p2p_addresses(C, s, rec, row, recv_base, ret_base)
+        expect = [-ident(s, d, j) for d in range(R) for j in range(C[s][d])]
+        assert n_send == len(expect)
+        assert [mem.get(ret_base[s] + i * row) for i in range(n_send)] == expect
