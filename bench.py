@@ -35,7 +35,7 @@ METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
 E2E_CHUNK = 4096   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
 DECISION_PROMPTS, DECISION_WARMUP, DECISION_STEPS = 64, 2, 3   # config 3 decision forward
 EP_SM_RESERVE = 0   # SMs the persistent kernels leave to the NCCL exchanges in expert-parallel runs
-EP_TRANSPORT = "nccl"   # expert-parallel exchange: "nccl" (two all-to-alls) or "p2p" (the kernels' own NVLink stores)
+EP_TRANSPORT = "p2p"    # expert-parallel exchange: "nccl" (two all-to-alls) or "p2p" (the kernels' own NVLink stores)
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
 # workload summarised in profiles/dram_traffic_cfg2.md; None where no capture covers the workload.

@@ -351,7 +351,7 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, hidden: int, inter: int, experts: int, topk: int, activation, a1_gscale: torch.Tensor,
-                 local: LocalExperts, group=None, ops=None, chunks: int = 1, transport: str = "nccl",
+                 local: LocalExperts, group=None, ops=None, chunks: int = 1, transport: str = "auto",
                  timeout_s: float = 10.0):
         self.group = group
         self.R = dist.get_world_size(group)
@@ -368,8 +368,10 @@ class ExpertParallelMoE:
         self.chunks = max(1, int(chunks))
         self.last_counts: tuple[list[int], list[int]] | None = None
         self.marks: list | None = None   # set to [] to collect (phase, CUDA event) pairs during forward
+        if transport == "auto":     # the kernels' own NVLink stores on GPU groups (one node), all-to-alls otherwise
+            transport = "p2p" if (ops is None and dist.get_backend(group) == "nccl") else "nccl"
         if transport not in ("nccl", "p2p"):
-            raise ValueError(f"transport must be 'nccl' or 'p2p', got {transport!r}")
+            raise ValueError(f"transport must be 'auto', 'nccl' or 'p2p', got {transport!r}")
         self.transport = transport
         self.peer = PeerExchange(self.ops, group, self.device, timeout_s) if transport == "p2p" else None
 

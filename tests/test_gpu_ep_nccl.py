@@ -48,7 +48,8 @@ def _worker(rank, world, port, Ts, errq):
                                               w.cpu().numpy(), ids.cpu().numpy(), E // world, world)
         t0 = sum(Ts[:rank])
         t1 = t0 + Ts[rank]
-        layer = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], _local(R, c, rank, world))
+        layer = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], _local(R, c, rank, world),
+                                       transport="nccl")
         out = layer(c["x"][t0:t1], w[t0:t1], ids[t0:t1])
         out2 = layer(c["x"][t0:t1], w[t0:t1], ids[t0:t1])   # buffers reused on the second call
         torch.cuda.synchronize(dev)

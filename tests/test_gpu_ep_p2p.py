@@ -6,8 +6,8 @@
   single-GPU layer's c3 rows recombined in the EP order.
 * The signal kernel: one rank (its own flag), and a wait that runs out (a flag that nothing sets) -> status
   REAXMOE_ERR_DEVICE_TIMEOUT, the context still usable.
-* 2 GPUs (skipped with fewer): one process per GPU, CUDA IPC mappings over NVLink, against the NCCL transport and the
-  recombined c3 rows, including a forward that makes the buffers grow.
+* 2, 4 and 8 GPUs (each skipped with fewer): one process per GPU, CUDA IPC mappings over NVLink, against the NCCL
+  transport and the recombined c3 rows, including a forward that makes the buffers grow.
 """
 import ctypes
 import os
@@ -159,7 +159,7 @@ def _worker(rank, world, port, Ts, errq):
         t0 = sum(Ts[:rank])
         t1 = t0 + Ts[rank]
         loc = _local(R, c, rank, world)
-        nccl = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], loc)
+        nccl = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], loc, transport="nccl")
         p2p = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], loc, transport="p2p",
                                      timeout_s=20.0)
         ref = nccl(c["x"][t0:t1], w[t0:t1], ids[t0:t1])
@@ -192,10 +192,12 @@ def test_expert_parallel_one_rank_p2p():
     assert errq.empty(), errq.get()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("Ts", [[640, 384], [1, 700]])
-def test_expert_parallel_two_gpus_p2p(Ts):
+@pytest.mark.parametrize("Ts", [[640, 384], [1, 700], [300, 1, 517, 128], [64] * 7 + [200]])
+def test_expert_parallel_multi_gpu_p2p(Ts):
+    world = len(Ts)
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
-    mp.start_processes(_worker, args=(2, _free_port(), Ts, errq), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), Ts, errq), nprocs=world, join=True, start_method="spawn")
     assert errq.empty(), errq.get()
