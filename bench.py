@@ -572,9 +572,9 @@ def run_ours_ep(args, wl: dict) -> None:
     flop_rank = 6.0 * slots_local * H * I
     t_tensor = flop_rank / (fp4_peak * 1e12)
     t_nvl = float(nvl.item()) / (nvlink_gbs * 1e9)
-    ex_ms = phase_ms.get("exchange_records", 0.0) + phase_ms.get("exchange_rows", 0.0)
+    # the step against its tighter bound: NVLink bytes per direction, or FP4 tensor work, over the whole step
     roof = dict(kernel="ep_step", bound="nvlink" if t_nvl > t_tensor else "tensor",
-                achieved=(float(nvl.item()) / (ex_ms / 1000.0) / 1e9) if t_nvl > t_tensor and ex_ms > 0
+                achieved=float(nvl.item()) / (ms_step / 1000.0) / 1e9 if t_nvl > t_tensor
                 else flop_rank / (ms_step / 1000.0) / 1e12,
                 peak=nvlink_gbs if t_nvl > t_tensor else fp4_peak,
                 unit="GB/s" if t_nvl > t_tensor else "TFLOP/s", traffic=None,
