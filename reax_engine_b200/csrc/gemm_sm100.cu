@@ -21,9 +21,9 @@
 //               single 128x256b copy of the pre-expanded record (reaxmoe_expand_scales), into one of two buffers.
 //               Copies cost tensor-pipe time in proportion to the (4x replicated) TMEM bytes they write; issued from
 //               this thread they overlap the MMAs, and the MMA thread's barrier waits do not queue behind them.
-//   warps 3..10 epilogue: tcgen05.ld the whole accumulator into registers (each warp owns its 32-lane TMEM quarter
-//               and half of the columns) and release it to the MMA warp at once, then convert / activate /
-//               quantise and store while the next unit's MMAs run.
+//   warps 3..   epilogue (8 for w13, 16 for w2): tcgen05.ld the whole accumulator into registers (each warp owns its
+//               32-lane TMEM quarter and a half / quarter of the columns) and release it to the MMA warp at once,
+//               then convert / activate / quantise and store while the next unit's MMAs run.
 // TMEM: accumulator [0, 256), two B-scale buffers of 32 columns, resident A scales (4 columns per k-chunk).
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records REAXMOE_ERR_DEVICE_TIMEOUT in the
 // status word, raises a CTA-wide abort flag, drains its own in-flight copies and MMAs, frees TMEM and returns.
@@ -52,9 +52,13 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFB_BYTES;
 constexpr int STAGES = 3;
 constexpr int MAX_K_CHUNKS = 48;        // K <= 3072: the resident A scales fit in TMEM
 constexpr int SFA_SMEM_BYTES = MAX_K_CHUNKS * 512;
-constexpr int NUM_EPI_WARPS = 8;
 constexpr int EPI_WARP0 = 3;
-constexpr int THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
+// Epilogue warps: w13 (mode 1) 8, two per TMEM lane quarter, each half of the tile's columns; w2 (mode 0) 16, four
+// per quarter, each a quarter of the columns (its epilogue is bound by the bf16 stores: more warps keep more of them
+// in flight; w13's activation + quantisation measured slower with 16, its extra issue pressure landing on the
+// single-thread producer / MMA / copy warps).
+__host__ __device__ constexpr int epi_warps(int mode) { return mode == 0 ? 16 : 8; }
+__host__ __device__ constexpr int threads_for(int mode) { return (EPI_WARP0 + epi_warps(mode)) * 32; }
 constexpr int TMEM_COLS = 512;
 constexpr int SFB_COL = BN;             // two B-scale buffers of 8 * KPS columns
 constexpr int SFB_BUF_COLS = 8 * KPS;
@@ -192,7 +196,8 @@ __device__ __forceinline__ uint32_t act_quant32(const uint32_t (&x0)[32], const 
 }
 
 template <int MODE, int ACT>
-__global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+  constexpr int NUM_EPI_WARPS = epi_warps(MODE);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sfa_smem = smem + STAGES * STAGE_BYTES;
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
   } else {
     // ------------------------------------------------------------------ epilogue warps
     const int q = warp & 3;                       // TMEM lane quarter this warp may access
-    const int sub = (warp - EPI_WARP0) >> 2;      // which half of the tile's columns
+    const int sub = (warp - EPI_WARP0) >> 2;      // which half (w13) / quarter (w2) of the tile's columns
     const int r = q * 32 + lane;                  // row inside the tile
     uint32_t acc_phase = 0;
     bool ok = true;
@@ -410,17 +415,15 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         acc_phase ^= 1u;
         tc_fence_after();
         const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16);
-        // full tiles: this warp's half = 128 output columns (mode 0) or 64 gate + 64 up columns (mode 1);
-        // the narrow last tile: 64 columns (mode 0) or 32 gate + 32 up (mode 1)
+        // full tiles: this warp's 64 output columns (mode 0) or 64 gate + 64 up columns (mode 1);
+        // the narrow last tile: 32 columns (mode 0) or 32 gate + 32 up (mode 1)
         const int half = un / 2;
         uint32_t x[4][32];
         if constexpr (MODE == 0) {
-          tc_ld_32x32b_x32(t_base + sub * half, x[0]);
-          tc_ld_32x32b_x32(t_base + sub * half + 32, x[1]);
-          if (un == BN) {
-            tc_ld_32x32b_x32(t_base + sub * half + 64, x[2]);
-            tc_ld_32x32b_x32(t_base + sub * half + 96, x[3]);
-          }
+          // 16 warps: this warp's quarter = 64 columns (32 in the narrow last tile)
+          const int cw = un / 4;
+          tc_ld_32x32b_x32(t_base + sub * cw, x[0]);
+          if (un == BN) tc_ld_32x32b_x32(t_base + sub * cw + 32, x[1]);
         } else {
           const int hw = un / 4;                  // h columns per warp half
           tc_ld_32x32b_x32(t_base + sub * hw, x[0]);             // gate
@@ -438,10 +441,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         const float alpha = p.alphas[M.e];
         if constexpr (MODE == 0) {
           // 32 columns per x[j] -> 64 bytes of bf16 -> two full 32-byte sectors per 256-bit store
-          uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + row * p.N + nt * BN + sub * half);
-          const int nq = un == BN ? 4 : 2;
+          uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + row * p.N + nt * BN + sub * (un / 4));
+          const int nq = un == BN ? 2 : 1;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 2; ++j) {
             if (j < nq) {
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
@@ -490,7 +493,7 @@ static int launch_t(const Params& prm, int grid, cudaStream_t s) {
   auto kfn = grouped_gemm_kernel<MODE, ACT>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
     return REAXMOE_ERR_CUDA;
-  kfn<<<grid, THREADS, SMEM_BYTES, s>>>(prm);
+  kfn<<<grid, threads_for(MODE), SMEM_BYTES, s>>>(prm);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
 }
 
