@@ -616,8 +616,8 @@ def run_ours_ep(args, wl: dict) -> None:
     decision = decision_leg(args, dev, world, rank)
 
     # route; dispatch 4 (rank ids, count, plan, pack); expert forward 8 (unpack, count, plan, permute, swizzle, w13,
-    # w2, combine); combine -- per token part; p2p adds the three signals
-    launches_per_step = 1 + 13 * layer.chunks + (3 if transport == "p2p" else 0)
+    # w2, combine); combine -- per token part; p2p adds the three signals and the direct-row table
+    launches_per_step = 1 + 13 * layer.chunks + (4 if transport == "p2p" else 0)
     line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
                 ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
                 data="synthetic",

@@ -306,8 +306,9 @@ int reaxmoe_ep_dispatch_pack(const reaxmoe_problem* p, int32_t ranks, const void
                              size_t workspace_bytes, int32_t* send_map, const uint64_t* records, void* stream);
 /* reaxmoe_ep_expert_forward with the pre-summed row of received record i stored at
  * rows[s] + (i - bounds[s]) * hidden * 2 for the source s with bounds[s] <= i < bounds[s + 1] (host arrays:
- * bounds [ranks + 1] from 0 to local->tokens, non-decreasing; rows [ranks] device addresses, 16-byte aligned:
- * the row in rank s's return buffer of the first record s sent here). */
+ * bounds [ranks + 1] from 0 to local->tokens, non-decreasing; rows [ranks] device addresses, 32-byte aligned:
+ * the row in rank s's return buffer of the first record s sent here). A record with exactly one local pair has its
+ * row stored by the w2 GEMM's epilogue, the others by the pre-sum kernel; the rows are the same either way. */
 int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
                                  const void* w1_sf, const float* w1_alphas, const float* a2_gscale,
                                  const void* w2_fp4, const void* w2_sf, const float* w2_alphas, void* workspace,

@@ -184,13 +184,19 @@ static int check_ep(const reaxmoe_problem* p, int ranks) {
 }
 
 // Expert-parallel receiver workspace: the single-GPU layout of the local problem, then the records' local ids and
-// weights as [tokens, topk] arrays.
+// weights as [tokens, topk] arrays, then (peer transport) the direct-row table per slot: return address and weight.
 static size_t ep_expert_lid(const Layout& L) { return L.total; }
 static size_t ep_expert_lw(const reaxmoe_problem* p, const Layout& L) {
   return up256(L.total + (size_t)p->tokens * p->topk * 4);
 }
-static size_t ep_expert_total(const reaxmoe_problem* p, const Layout& L) {
+static size_t ep_expert_direct(const reaxmoe_problem* p, const Layout& L) {
   return up256(ep_expert_lw(p, L) + (size_t)p->tokens * p->topk * 4);
+}
+static size_t ep_expert_direct_w(const reaxmoe_problem* p, const Layout& L) {
+  return up256(ep_expert_direct(p, L) + (size_t)p->tokens * p->topk * 8);
+}
+static size_t ep_expert_total(const reaxmoe_problem* p, const Layout& L) {
+  return up256(ep_expert_direct_w(p, L) + (size_t)p->tokens * p->topk * 4);
 }
 
 static unsigned long long device_timeout_ns() {
@@ -741,6 +747,15 @@ static int ep_expert_forward(const reaxmoe_problem* local, const void* recv_reco
   GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4, w.int_sf);
   if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "%s: gemm_w13 launch failed", who);
   GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, w2_fp4, w2_sf, w2_alphas, w.c3);
+  if (route != nullptr) {
+    // records with one local pair: the w2 epilogue stores their finished rows straight to the source rank
+    uint64_t* direct_dst = reinterpret_cast<uint64_t*>(b + ep_expert_direct(p, L));
+    float* direct_w = reinterpret_cast<float*>(b + ep_expert_direct_w(p, L));
+    launch_ep_direct(w.c_map, lw, p->tokens, p->topk, p->hidden, *route, direct_dst, direct_w, s);
+    g2.direct_dst = direct_dst;
+    g2.direct_w = direct_w;
+    g2.topk = p->topk;
+  }
   if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "%s: gemm_w2 launch failed", who);
   if (route != nullptr)
     launch_combine_routed(w.c3, w.c_map, lw, p->tokens, p->hidden, p->topk, *route, sms, s);
@@ -770,14 +785,15 @@ int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_
     return fail(REAXMOE_ERR_BAD_SHAPE, "ep_expert_forward_to: bounds must run from 0 to tokens=%d", local->tokens);
   RowRoute route{};
   route.ranks = ranks;
+  route.skip_single = 1;
   for (int q = 0; q <= ranks; ++q) {
     if (q > 0 && bounds[q] < bounds[q - 1])
       return fail(REAXMOE_ERR_BAD_SHAPE, "ep_expert_forward_to: bounds decrease at %d", q);
     route.bound[q] = bounds[q];
   }
   for (int q = 0; q < ranks; ++q) {
-    if (bounds[q + 1] > bounds[q] && (rows[q] == 0 || rows[q] % 16 != 0))
-      return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_forward_to: rows[%d] is NULL or not 16-byte aligned", q);
+    if (bounds[q + 1] > bounds[q] && (rows[q] == 0 || rows[q] % 32 != 0))
+      return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_forward_to: rows[%d] is NULL or not 32-byte aligned", q);
     route.p[q] = rows[q];
   }
   return ep_expert_forward(local, recv_records, w1_fp4, w1_sf, w1_alphas, a2_gscale, w2_fp4, w2_sf, w2_alphas,

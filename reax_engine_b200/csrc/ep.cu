@@ -331,6 +331,39 @@ int launch_ep_pack_peer(const __nv_bfloat16* a, const float* a1_gscale, const in
   return 0;
 }
 
+// One thread per received record: a record with exactly one local pair is finished by the w2 epilogue (its row is
+// bf16(c3 * w) rounded once, which the combine would compute too), so its slot gets the record's return address.
+__global__ void __launch_bounds__(256) ep_direct_kernel(const int* __restrict__ c_map, const float* __restrict__ lw,
+                                                        int n, int k, const __grid_constant__ RowRoute route, int H,
+                                                        uint64_t* __restrict__ direct_dst,
+                                                        float* __restrict__ direct_w) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int cnt = 0, jj = 0;
+  for (int j = 0; j < k; ++j)
+    if (c_map[i * k + j] >= 0) {
+      ++cnt;
+      jj = j;
+    }
+  if (cnt == 1) {
+    const int slot = c_map[i * k + jj];
+    direct_dst[slot] = route.row_addr(i, H);
+    direct_w[slot] = lw[i * k + jj];
+  } else {
+    for (int j = 0; j < k; ++j) {
+      const int slot = c_map[i * k + j];
+      if (slot >= 0) direct_dst[slot] = 0ull;
+    }
+  }
+}
+
+int launch_ep_direct(const int* c_map, const float* lw, int n, int k, int H, const RowRoute& route,
+                     uint64_t* direct_dst, float* direct_w, cudaStream_t s) {
+  if (n > 0)
+    ep_direct_kernel<<<(unsigned)ceil_div64(n, 256), 256, 0, s>>>(c_map, lw, n, k, route, H, direct_dst, direct_w);
+  return 0;
+}
+
 int launch_ep_signal(const PeerPtrs& blocks, int rank, int ranks, uint32_t epoch, const int* counts,
                      unsigned long long timeout_ns, cudaStream_t s) {
   ep_signal_kernel<<<1, kMaxRanks, 0, s>>>(blocks, rank, ranks, epoch, counts, timeout_ns);

@@ -94,6 +94,9 @@ struct Params {
   const float* q_gscale;
   int* status;
   unsigned long long timeout_ns;
+  const uint64_t* direct_dst;  // mode 0: per slot row, its record's return address (0 = write c3)
+  const float* direct_w;
+  int topk;
   int E, N, K, n_tiles, k_chunks;
   int tail_n;           // width of the last n-tile (256, or 128 when N % 256 == 128)
 };
@@ -406,6 +409,15 @@ __global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(cons
     for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
       const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
       const int64_t row = (int64_t)M.row0 + r;
+      // expert-parallel receiver: a slot that is its record's only local pair is written as the finished row
+      uint64_t direct = 0ull;
+      float wdir = 0.0f;
+      if constexpr (MODE == 0) {
+        if (p.direct_dst != nullptr && r < M.rows) {
+          direct = p.direct_dst[row];
+          wdir = bf16r(p.direct_w[row]);
+        }
+      }
       for (int nt = 0; nt < n_tiles; ++nt) {
         const int un = (nt == n_tiles - 1) ? p.tail_n : BN;
         if (!wait_bounded(smem_u32(accf), acc_phase, abort_flag, p.status, p.timeout_ns)) {
@@ -441,7 +453,9 @@ __global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(cons
         const float alpha = p.alphas[M.e];
         if constexpr (MODE == 0) {
           // 32 columns per x[j] -> 64 bytes of bf16 -> two full 32-byte sectors per 256-bit store
-          uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + row * p.N + nt * BN + sub * (un / 4));
+          const int col0 = nt * BN + sub * (un / 4);
+          uint8_t* dst = direct != 0ull ? reinterpret_cast<uint8_t*>(direct) + (size_t)col0 * 2
+                                        : reinterpret_cast<uint8_t*>(p.out + row * p.N + col0);
           const int nq = un == BN ? 2 : 1;
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
@@ -449,10 +463,25 @@ __global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(cons
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 uint32_t o[8];
+                if (direct != 0ull) {
+                  // the combine of a record with one pair: bf16(bf16(c3) * bf16(w)); its fp32 sum with the
+                  // absent pairs' +0 terms turns -0 into +0 when topk > 1
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                  o[i] = pack_bf16x2(alpha * __uint_as_float(x[j][16 * h + 2 * i]),
-                                     alpha * __uint_as_float(x[j][16 * h + 2 * i + 1]));
+                  for (int i = 0; i < 8; ++i) {
+                    float v0 = bf16r(__fmul_rn(bf16r(alpha * __uint_as_float(x[j][16 * h + 2 * i])), wdir));
+                    float v1 = bf16r(__fmul_rn(bf16r(alpha * __uint_as_float(x[j][16 * h + 2 * i + 1])), wdir));
+                    if (p.topk > 1) {
+                      v0 = __fadd_rn(v0, 0.0f);
+                      v1 = __fadd_rn(v1, 0.0f);
+                    }
+                    o[i] = pack_bf16x2(v0, v1);
+                  }
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 8; ++i)
+                    o[i] = pack_bf16x2(alpha * __uint_as_float(x[j][16 * h + 2 * i]),
+                                       alpha * __uint_as_float(x[j][16 * h + 2 * i + 1]));
+                }
                 st_global_v8(dst + 64 * j + 32 * h, o);
               }
             }
@@ -476,6 +505,8 @@ __global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(cons
         }
       }
     }
+    // direct rows went to peers' memory: fence them at system scope for the signal that follows the layer
+    if (MODE == 0 && p.direct_dst != nullptr) __threadfence_system();
   }
 
   tc_fence_before();
@@ -521,6 +552,9 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   prm.q_gscale = g.q_gscale;
   prm.status = g.status;
   prm.timeout_ns = g.timeout_ns;
+  prm.direct_dst = g.mode == 0 ? g.direct_dst : nullptr;
+  prm.direct_w = g.direct_w;
+  prm.topk = g.topk;
   prm.E = g.E;
   prm.N = g.N;
   prm.K = g.K;

@@ -407,15 +407,13 @@ struct PlainRows {
   static constexpr bool kPeer = false;
   __nv_bfloat16* out;
   __device__ __forceinline__ uint4* row(int64_t t, int H) const { return reinterpret_cast<uint4*>(out + t * H); }
+  __device__ __forceinline__ bool skip(int) const { return false; }
 };
 struct RoutedRows {
   static constexpr bool kPeer = true;
   RowRoute r;
-  __device__ __forceinline__ uint4* row(int64_t t, int H) const {
-    int src = 0;
-    for (int q = 1; q < r.ranks; ++q) src += (t >= r.bound[q]) ? 1 : 0;
-    return reinterpret_cast<uint4*>(r.p[src] + (uint64_t)(t - r.bound[src]) * (uint64_t)H * 2u);
-  }
+  __device__ __forceinline__ uint4* row(int64_t t, int H) const { return reinterpret_cast<uint4*>(r.row_addr(t, H)); }
+  __device__ __forceinline__ bool skip(int valid_pairs) const { return r.skip_single && valid_pairs == 1; }
 };
 
 template <int K, class Rows>
@@ -436,13 +434,16 @@ __global__ void __launch_bounds__(256, 3) combine_kernel_k(const __nv_bfloat16* 
     const uint4* rowp[K];
     float wb[K];
     bool valid[K];
+    int nvalid = 0;
 #pragma unroll
     for (int j = 0; j < K; ++j) {
       const int pj = __shfl_sync(0xffffffffu, mypos, j);
       wb[j] = __shfl_sync(0xffffffffu, myw, j);
       valid[j] = pj >= 0;  // -1 marks a pair whose expert id was out of range (flagged by the plan)
+      nvalid += valid[j] ? 1 : 0;
       rowp[j] = reinterpret_cast<const uint4*>(c3 + (int64_t)(valid[j] ? pj : 0) * H);
     }
+    if (out.skip(nvalid)) continue;
     uint4* orow = out.row(t, H);
     for (int ch = lane; ch < nch; ch += 32) {
       uint4 v[K];
@@ -473,11 +474,14 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
     }
     int pos[kMaxTopk];
     float wb[kMaxTopk];
+    int nvalid = 0;
 #pragma unroll
     for (int j = 0; j < kMaxTopk; ++j) {
       pos[j] = __shfl_sync(0xffffffffu, mypos, j);
       wb[j] = __shfl_sync(0xffffffffu, myw, j);
+      nvalid += (j < k && pos[j] >= 0) ? 1 : 0;
     }
+    if (out.skip(nvalid)) continue;
     for (int ch = lane; ch < H / 8; ch += 32) {
       float part[4][8];
 #pragma unroll

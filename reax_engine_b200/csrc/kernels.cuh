@@ -52,6 +52,14 @@ struct RowRoute {
   uint64_t p[kMaxRanks];
   int64_t bound[kMaxRanks + 1];
   int ranks;
+  int skip_single;  // the combine leaves out records with exactly one local pair (the w2 epilogue sent those)
+#ifdef __CUDACC__
+  __device__ __forceinline__ uint64_t row_addr(int64_t t, int H) const {
+    int src = 0;
+    for (int q = 1; q < ranks; ++q) src += (t >= bound[q]) ? 1 : 0;
+    return p[src] + (uint64_t)(t - bound[src]) * (uint64_t)H * 2u;
+  }
+#endif
 };
 // Signal block (one per rank, peer-mapped): status word, one flag per source rank, the [ranks, ranks] send-count
 // matrix (row s written by rank s).
@@ -67,6 +75,10 @@ int launch_combine_routed(const __nv_bfloat16* c3, const int* c_map, const float
                           const RowRoute& route, int num_sms, cudaStream_t s);
 int launch_ep_signal(const PeerPtrs& blocks, int rank, int ranks, uint32_t epoch, const int* counts,
                      unsigned long long timeout_ns, cudaStream_t s);
+// Direct rows: for every received record with exactly one local pair, its slot's entry gets the record's return
+// address (route) and router weight; the other local pairs' slots get 0 (summed by the routed combine).
+int launch_ep_direct(const int* c_map, const float* lw, int n, int k, int H, const RowRoute& route,
+                     uint64_t* direct_dst, float* direct_w, cudaStream_t s);
 
 // Grouped NVFP4 GEMM (gemm_sm100.cu). mode 0: out bf16 [slots, N]; mode 1: fused act(gate)*up + NVFP4 quant
 // into q_out [slots, N/4] (N = 2*inter interleaved) and q_sf atoms.
@@ -87,6 +99,12 @@ struct GemmLaunch {
   const float* q_gscale;
   int* status;
   unsigned long long timeout_ns;
+  // mode 0, expert-parallel receiver: slot rows whose direct_dst is non-zero are written as the record's finished
+  // row, bf16(bf16(alpha * acc) * bf16(direct_w)) (+0 normalised when topk > 1, as the combine's sum does), at
+  // direct_dst (a peer's return buffer over NVLink) instead of c3
+  const uint64_t* direct_dst;
+  const float* direct_w;
+  int topk;
 };
 int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s);
 

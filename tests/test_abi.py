@@ -165,6 +165,8 @@ def test_p2p_entry_points_reject_bad_args():
     assert L.lib().reaxmoe_ep_expert_forward_to(ctypes.byref(p), *args, 2, bounds, rows, None) == L.ERR_BAD_SHAPE
     bounds = (ctypes.c_int64 * 3)(0, 3, 4)
     assert L.lib().reaxmoe_ep_expert_forward_to(ctypes.byref(p), *args, 2, bounds, rows, None) == L.ERR_MISALIGNED
+    rows = (ctypes.c_uint64 * 2)(64, 16)                            # rows[1] only 16-byte aligned
+    assert L.lib().reaxmoe_ep_expert_forward_to(ctypes.byref(p), *args, 2, bounds, rows, None) == L.ERR_MISALIGNED
     recs = (ctypes.c_uint64 * 2)(16, 8)
     assert L.lib().reaxmoe_ep_dispatch_pack(ctypes.byref(p), 2, 16, 16, 16, 16, 16, 1 << 20, 16, recs,
                                             None) == L.ERR_MISALIGNED
