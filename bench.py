@@ -11,8 +11,9 @@ data of that shape (activations N(0,1) bf16, weights N(0,0.02) quantised to NVFP
 `value` times the kernels with the inputs resident in HBM (CUDA events, max over ranks); `e2e` times the public
 API for host-resident batches (reax_engine_b200.HostStreamedMoE: route + run_moe_nvfp4 per token chunk) with the
 pinned host inputs copied in and the output copied back every step, the copies overlapped with the layer.
-`--impl reference` times the reference path's CPU restatement (oracle/moe_oracle.py, numpy) on the host cores on a
-bounded token sample. With torchrun (N > 1) each rank runs the expert-parallel layer
+`--impl reference` times the reference's layer on the host cores (oracle/ref_torch.py: the reference's engine/fp4.py
+quantisation and the stock vLLM arithmetic in torch on the CPU, inputs generated on the CPU), one measured 4096-token
+slice of the workload per step. With torchrun (N > 1) each rank runs the expert-parallel layer
 (reax_engine_b200.ep) on its own 65,536-token batch.
 """
 from __future__ import annotations
@@ -23,6 +24,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -85,7 +87,7 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"reaxmoe_clocks_{os.getpid()}_{index}.csv")
         self.t_in = self.t_out = None
 
     def __enter__(self):
@@ -224,69 +226,99 @@ def decision_leg(args, dev, world: int, rank: int) -> dict | None:
     return out
 
 
-def cpu_sample(wl: dict, inp_cpu: dict, n_tokens: int, reps: int = 1):
-    """Time the oracle (reference CPU restatement) on the first n_tokens of the workload. Returns tokens/s."""
-    from oracle import moe_oracle as O
-    n = min(n_tokens, wl["T"])
-    x = inp_cpu["x"][:n]
-    logits = inp_cpu["logits"][:n]
-    wcache: dict = {}
-    # untimed: dequantise the touched experts' weights once (model-load work for a CPU engine)
-    w, ids = O.route(logits, wl["k"])
-    for e in np.unique(ids):
-        wcache[O.weight_cache_key(inp_cpu["w1q"], e)] = O.expert_weights(inp_cpu["w1q"], inp_cpu["w1s"], int(e))
-        wcache[O.weight_cache_key(inp_cpu["w2q"], e)] = O.expert_weights(inp_cpu["w2q"], inp_cpu["w2s"], int(e))
-    times = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        w, ids = O.route(logits, wl["k"])
-        O.moe_forward(x, w, ids, inp_cpu["w1q"], inp_cpu["w1s"], inp_cpu["w1_alphas"], inp_cpu["w2q"],
-                      inp_cpu["w2s"], inp_cpu["w2_alphas"], inp_cpu["a1_gscale"], inp_cpu["a2_gscale"], wl["act"],
-                      wcache)
-        times.append(time.perf_counter() - t0)
-    return n / statistics.median(times), n, statistics.median(times)
+REFERENCE_SLICE = 4096   # tokens per step of the CPU reference path (the first tokens of the workload's batch)
 
 
-def to_cpu_inputs(inp: dict) -> dict:
-    return dict(x=inp["x"].float().cpu().numpy(), logits=inp["logits"].cpu().numpy(),
-                w1q=inp["w1q"].cpu().numpy(), w1s=inp["w1s"].cpu().numpy(), w2q=inp["w2q"].cpu().numpy(),
-                w2s=inp["w2s"].cpu().numpy(), a1_gscale=inp["a1_gscale"].cpu().numpy(),
-                a2_gscale=inp["a2_gscale"].cpu().numpy(), w1_alphas=inp["w1_alphas"].cpu().numpy(),
-                w2_alphas=inp["w2_alphas"].cpu().numpy())
+def seeded_normal(shape, seed: int, scale: float = 1.0, chunk: int = 1 << 22) -> np.ndarray:
+    """float32 N(0, scale^2) of `shape` from numpy's PCG64, in fixed chunks with spawned child seeds (filled by a
+    thread pool; the values do not depend on the thread count)."""
+    from concurrent.futures import ThreadPoolExecutor
+    out = np.empty(int(np.prod(shape)), dtype=np.float32)
+    n_chunks = -(-out.size // chunk)
+    seqs = np.random.SeedSequence(seed).spawn(n_chunks)
+
+    def fill(i):
+        part = out[i * chunk:(i + 1) * chunk]
+        np.random.default_rng(seqs[i]).standard_normal(out=part, dtype=np.float32)
+        if scale != 1.0:
+            part *= np.float32(scale)
+
+    with ThreadPoolExecutor(max(1, os.cpu_count() or 1)) as ex:
+        list(ex.map(fill, range(n_chunks)))
+    return out.reshape(shape)
+
+
+def reference_cpu_run(wl: dict, steps: int, warmup: int, slice_tokens: int = REFERENCE_SLICE, seed: int = 0) -> dict:
+    """The reference's layer on the host cores (oracle/ref_torch.py: engine/fp4.py quantisation, Gemma-4 routing, the
+    stock run_cutlass_moe_fp4 arithmetic in torch on the CPU). Inputs are generated on the CPU (seeded numpy) with the
+    workload's shapes and distributions; no GPU and none of this repository's CUDA code is involved. Each step runs
+    routing + the layer over the first `slice_tokens` tokens of the workload; returns the timing."""
+    import torch
+
+    from oracle import ref_torch as RT
+    T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
+    n = min(slice_tokens, T)
+    t_setup = time.perf_counter()
+    x = torch.from_numpy(seeded_normal((n, H), seed)).bfloat16()
+    if wl["skew"] is None:
+        gate = torch.from_numpy(seeded_normal((E, H), seed + 1, 0.02))
+        logits = x.float() @ gate.t()
+    else:
+        from moe_cases import zipf_bias
+        logits = torch.from_numpy(seeded_normal((n, E), seed + 1)) + zipf_bias(E, wl["skew"], seed)[None]
+    w1q, w1s, w1g = RT.quantize_weights(torch.from_numpy(seeded_normal((E, 2 * I, H), seed + 2, 0.02)))
+    w2q, w2s, w2g = RT.quantize_weights(torch.from_numpy(seeded_normal((E, H, I), seed + 3, 0.02)))
+    a1_g = float(x.float().abs().max()) / 2688.0
+    a2_g = 8.0 / 2688.0
+    layer = RT.ReferenceMoE(w1q, w1s, w2q, w2s, w1g * a1_g, w2g * a2_g, torch.full((E,), 1.0 / a1_g),
+                            torch.full((E,), 1.0 / a2_g), wl["act"])
+    setup_s = time.perf_counter() - t_setup
+
+    def step():
+        w, ids = RT.route(logits, k)
+        return layer.forward(x, w, ids)
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        out = step()
+    total = time.perf_counter() - t0
+    assert bool(torch.isfinite(out.float()).all())
+    return dict(tokens=n, steps=steps, seconds=total, ms_per_step=1000.0 * total / steps,
+                value=n * steps / total, threads=torch.get_num_threads(), setup_s=setup_s,
+                sample=f"first {n} of the workload's {T} tokens per step (seeded numpy inputs of the workload's "
+                       f"shapes and distributions); oracle/ref_torch.py: the reference's engine/fp4.py "
+                       f"quantisation, Gemma-4 routing and the stock run_cutlass_moe_fp4 arithmetic in torch on the "
+                       f"host cores, dequantised weights built once before timing")
+
+
+def workload_config(wl: dict) -> dict:
+    """The `config` of the bench line, identical in both arms."""
+    T, H, E, I = wl["T"], wl["H"], wl["E"], wl["I"]
+    weights = E * 3 * H * I * (1 / 2 + 1 / 16)
+    return dict(workload=wl["name"], tokens=T, hidden=H, experts=E, topk=wl["k"], inter=I, activation=wl["act"],
+                parallelism="single",
+                l2="inputs larger than L2 (x %.0f MB, weights %.0f MB); no flush" % (T * H * 2 / 1e6, weights / 1e6))
 
 
 def run_reference(args, wl: dict) -> None:
-    """The reference arm: the reference path's CPU restatement (numpy oracle), all host cores, bounded samples."""
+    """The reference arm: the reference's layer on the host cores (reference_cpu_run), all host threads, each step
+    a measured 4096-token slice of the same workload (the reference's MoE ops are GPU-only compiled code; its own
+    CPU-runnable pieces are restated and pinned in oracle/ref_torch.py). Under torchrun only rank 0 runs it."""
     import torch
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    dev = torch.device("cuda:0") if torch.cuda.is_available() else None
-    if dev is not None:
-        inp = build_inputs(wl, dev)
-        cpu = to_cpu_inputs(inp)
-        del inp
-        torch.cuda.empty_cache()
-    else:
-        raise SystemExit("reference arm needs the same seeded inputs (generated on the GPU)")
-    sample = 256
-    for _ in range(args.warmup):
-        cpu_sample(wl, cpu, 32)
-    rates = []
-    for _ in range(args.steps):
-        r, n, t = cpu_sample(wl, cpu, sample)
-        rates.append(r)
-    v = statistics.median(rates)
-    line = dict(metric=METRIC, value=v, unit="tokens/s", n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
-                ms_per_step=1000.0 * wl["T"] / v, higher_is_better=True, scaling="weak", vs_baseline=None,
-                dtype="fp32 (dequantised NVFP4)", data="synthetic",
-                config=dict(workload=wl["name"], tokens=wl["T"], hidden=wl["H"], experts=wl["E"], topk=wl["k"],
-                            inter=wl["I"]),
-                impl="reference",
-                cpu_baseline=dict(value=v, unit="tokens/s", cores=os.cpu_count(), kind="port",
-                                  sample=f"first {sample} tokens of the workload per step, numpy oracle "
-                                         f"(oracle/moe_oracle.py), expert weights pre-dequantised"),
-                e2e=dict(value=v, unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    torch.set_num_threads(os.cpu_count() or 1)
+    r = reference_cpu_run(wl, args.steps, args.warmup)
+    line = dict(metric=METRIC, value=r["value"], unit="tokens/s", n_gpus=args.gpus, steps=args.steps,
+                warmup=args.warmup, ms_per_step=r["ms_per_step"], higher_is_better=True, scaling="weak",
+                vs_baseline=None, dtype="fp32 (dequantised NVFP4), bf16 rounding points", data="synthetic",
+                config=workload_config(wl), impl="reference", sample=r["sample"],
+                cpu_baseline=dict(value=r["value"], unit="tokens/s", cores=r["threads"], kind="port",
+                                  sample=r["sample"]),
+                e2e=dict(value=r["value"], unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+                setup_s=r["setup_s"])
     print(json.dumps(line), flush=True)
 
 
@@ -446,19 +478,14 @@ def run_ours(args, wl: dict) -> None:
                  frac_fp4=layer_flop / (ms_step / 1000.0) / 1e12 / fp4_peak)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu_in = to_cpu_inputs(inp)
-        rate, n, t = cpu_sample(wl, cpu_in, args.cpu_tokens)
-        cpu = dict(value=rate, unit="tokens/s", cores=os.cpu_count(), kind="port",
-                   sample=f"first {n} tokens of the workload, numpy oracle, {t:.2f} s")
+        r = reference_cpu_run(wl, steps=3, warmup=1)
+        cpu = dict(value=r["value"], unit="tokens/s", cores=r["threads"], kind="port",
+                   sample=r["sample"] + f"; 3 steps, {r['seconds']:.2f} s")
     launches_per_step = 8   # route, count, plan, permute_quant, swizzle_scales, gemm_w13, gemm_w2, combine
     line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
                 ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
                 data="synthetic",
-                config=dict(workload=wl["name"], tokens=T, hidden=H, experts=E, topk=k, inter=I,
-                            activation=wl["act"], parallelism="single",
-                            l2="inputs larger than L2 (x %.0f MB, weights %.0f MB); no flush" % (
-                                T * H * 2 / 1e6, (inp["w1q"].numel() + inp["w1s"].numel() + inp["w2q"].numel() +
-                                                  inp["w2s"].numel()) / 1e6)),
+                config=workload_config(wl),
                 e2e=None if e2e_value is None else dict(
                     value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * H * 2 + T * E * 4,
                     d2h_bytes_per_step=T * H * 2,
@@ -648,7 +675,6 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default=None)
-    ap.add_argument("--cpu-tokens", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--no-router", action="store_true", help="skip the fused router measurement (profiling runs)")

@@ -121,3 +121,66 @@ def test_router_mean_square_order_only_moves_rsqrt_by_an_ulp():
     assert d.any(axis=1).mean() < 0.1
     ulp = 2.0 ** (np.floor(np.log2(np.abs(u[d]))) - 7)
     assert (np.abs(uk - u)[d] <= 4 * ulp).all()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# oracle/ref_torch.py: the reference's layer in torch on the CPU (the timed CPU baseline), pinned to the same fixtures
+# ---------------------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("case", ["a", "b", "c", "d"])
+def test_ref_torch_quantize_matches_engine_fp4(case):
+    import torch
+
+    from oracle import ref_torch as RT
+    d = load("quant_golden.npz")
+    x = torch.from_numpy(d[f"{case}_x"])
+    packed, s8 = RT.quantize(x, torch.tensor(float(d[f"{case}_g"])))
+    assert np.array_equal(packed.numpy(), d[f"{case}_packed"])
+    assert np.array_equal(O.to_blocked(s8.numpy()), d[f"{case}_sf"])
+    k16 = x.shape[1] // 16
+    assert np.array_equal(RT.unswizzle(torch.from_numpy(d[f"{case}_sf"]), x.shape[0], k16).numpy(), s8.numpy())
+
+
+def test_ref_torch_weight_quantisation_matches_oracle():
+    import torch
+
+    from oracle import ref_torch as RT
+    w = torch.randn(3, 256, 512, generator=torch.Generator().manual_seed(5)) * 0.02
+    q, s, g = RT.quantize_weights(w, experts_per_chunk=2)
+    q_o, s_o, g_o = O.quantize_weights(w.numpy())
+    assert np.array_equal(q.numpy(), q_o) and np.array_equal(s.numpy(), s_o) and np.array_equal(g.numpy(), g_o)
+
+
+@pytest.mark.parametrize("name", ["e128k8", "e64k4"])
+def test_ref_torch_route_matches_vllm_torch(name):
+    import torch
+
+    from oracle import ref_torch as RT
+    d = load("route_golden.npz")
+    k = d[f"{name}_ids"].shape[1]
+    w, ids = RT.route(torch.from_numpy(d[f"{name}_logits"]), k)
+    assert np.array_equal(ids.numpy(), d[f"{name}_ids"])
+    w_ref = d[f"{name}_w"] / d[f"{name}_scale"][d[f"{name}_ids"]]      # the fixture folds in per_expert_scale
+    np.testing.assert_allclose(w.numpy(), w_ref, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("act", ["gelu_tanh", "silu"])
+def test_ref_torch_layer_matches_reference_composition(act):
+    """The batched torch layer against the per-pair composition make_golden.py ran with the reference's own
+    engine/fp4.py, and against the numpy oracle: within the north-star tolerance (the GEMMs' fp32 sums run in other
+    orders, which moves a few bf16 roundings)."""
+    import torch
+
+    from oracle import ref_torch as RT
+    d = load("layer_golden.npz")
+    p = act + "_"
+    t = {n: torch.from_numpy(d[p + n]) for n in ("w1_fp4", "w1_sf", "w2_fp4", "w2_sf", "w1_alphas", "w2_alphas",
+                                                 "a1_gscale", "a2_gscale", "topk_w", "topk_ids")}
+    layer = RT.ReferenceMoE(t["w1_fp4"], t["w1_sf"], t["w2_fp4"], t["w2_sf"], t["w1_alphas"], t["w2_alphas"],
+                            t["a1_gscale"], t["a2_gscale"], act)
+    out = layer.forward(torch.from_numpy(d[p + "x"]).bfloat16(), t["topk_w"], t["topk_ids"]).float().numpy()
+    r = O.moe_forward(d[p + "x"], d[p + "topk_w"], d[p + "topk_ids"], d[p + "w1_fp4"], d[p + "w1_sf"],
+                      d[p + "w1_alphas"], d[p + "w2_fp4"], d[p + "w2_sf"], d[p + "w2_alphas"], d[p + "a1_gscale"],
+                      d[p + "a2_gscale"], act)
+    for ref in (d[p + "out"], r["out"]):
+        assert np.abs(out - ref).max() <= 2e-2
+        assert np.linalg.norm(out - ref) <= 1e-2 * np.linalg.norm(ref)
