@@ -37,6 +37,8 @@ METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
 E2E_CHUNK = 4096   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
 DECISION_PROMPTS, DECISION_WARMUP, DECISION_STEPS = 64, 2, 3   # config 3 decision forward
 EP_SM_RESERVE = 0   # SMs the persistent kernels leave to the NCCL exchanges in expert-parallel runs
+EP_E2E_CHUNKS = 4   # token parts per rank in the expert-parallel end-to-end pipeline (HostStreamedEP)
+EP_PARITY_TOKENS = 1024   # tokens per rank checked against the single-GPU layer after the timed expert-parallel steps
 EP_TRANSPORT = "p2p"    # expert-parallel exchange: "nccl" (two all-to-alls) or "p2p" (the kernels' own NVLink stores)
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
@@ -538,7 +540,8 @@ def run_ours_ep(args, wl: dict) -> None:
                                 inp["w2q"][sl].contiguous(), R.expand_scales(inp["w2s"][sl].contiguous(), H, I),
                                 inp["w2_alphas"][sl].contiguous())
     weight_bytes = sum(t.numel() for t in (inp["w1q"], inp["w1s"], inp["w2q"], inp["w2s"])) // world
-    for key in ("w1q", "w1s", "w2q", "w2s", "w1p", "w1p_sf", "w2sx"):
+    full_w = dict(w1p=inp.pop("w1p"), w1p_sf=inp.pop("w1p_sf"), w2q=inp.pop("w2q"), w2sx=inp.pop("w2sx"))
+    for key in ("w1q", "w1s", "w2s"):
         inp.pop(key)
     torch.cuda.empty_cache()
     layer = R.ep.ExpertParallelMoE(H, I, E, k, wl["act"], inp["a1_gscale"], local_w,
@@ -616,15 +619,10 @@ def run_ours_ep(args, wl: dict) -> None:
         x_h = x.cpu().pin_memory()
         lg_h = logits.cpu().pin_memory()
         out_h = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-        x_d = torch.empty_like(x)
-        lg_d = torch.empty_like(logits)
+        host_layer = R.HostStreamedEP(layer, dev, chunks=EP_E2E_CHUNKS)
 
         def e2e_step():
-            x_d.copy_(x_h, non_blocking=True)
-            lg_d.copy_(lg_h, non_blocking=True)
-            w, ids = R.route(None, lg_d, k)
-            layer(x_d, w, ids, out)
-            out_h.copy_(out, non_blocking=True)
+            host_layer(x_h, lg_h, out_h)
 
         for _ in range(args.warmup):
             e2e_step()
@@ -639,6 +637,8 @@ def run_ours_ep(args, wl: dict) -> None:
         ems = torch.tensor([e0.elapsed_time(e1)], device=dev)
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
         e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
+
+    parity = ep_parity(R, layer, x, logits, inp, full_w, rank, world, dev)
 
     decision = decision_leg(args, dev, world, rank)
 
@@ -655,8 +655,10 @@ def run_ours_ep(args, wl: dict) -> None:
                                 T * H * 2 / 1e6, weight_bytes / 1e6)),
                 e2e=None if e2e_value is None else dict(
                     value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * H * 2 + T * E * 4,
-                    d2h_bytes_per_step=T * H * 2),
-                gpu_launches=launches_per_step * args.steps, roofline=roof,
+                    d2h_bytes_per_step=T * H * 2,
+                    api=f"reax_engine_b200.HostStreamedEP: pinned host x + logits in, output out, {EP_E2E_CHUNKS} "
+                        "parts per rank, copies overlapped with route + the expert-parallel forward"),
+                gpu_launches=launches_per_step * args.steps, roofline=roof, parity=parity,
                 phases_ms={n: v for n, v in phase_ms.items()},
                 exchange=dict(records_sent=send, records_received=recv, record_bytes=rec,
                               nvlink_bytes_per_direction=float(nvl.item())),
@@ -666,6 +668,95 @@ def run_ours_ep(args, wl: dict) -> None:
     layer.close()
     dist.barrier()
     dist.destroy_process_group()
+
+
+def ep_parity_sample(ids, El: int, ranks: int, rank: int, n: int):
+    """Token indices for the expert-parallel output check: n evenly spaced tokens, plus up to n / 4 tokens whose pairs
+    all live on other ranks and up to n / 4 tokens with a rank that owns exactly one of their pairs (records that take
+    the w2-epilogue direct-row path). Returns (indices, how many have all pairs remote, one-pair records)."""
+    import torch
+    T, k = ids.shape
+    owner = torch.where(ids >= 0, ids // El, -1).long()
+    all_remote = ~(owner == rank).any(1)
+    per_rank = torch.zeros(T, ranks, dtype=torch.int32, device=ids.device)
+    per_rank.scatter_add_(1, owner.clamp(min=0), (owner >= 0).int())
+    single = (per_rank == 1).any(1)
+    pick = [torch.linspace(0, T - 1, min(n, T), device=ids.device).long(),
+            torch.nonzero(all_remote).flatten()[:n // 4], torch.nonzero(single).flatten()[:n // 4]]
+    idx = torch.unique(torch.cat(pick))
+    return idx, int(all_remote[idx].sum()), int((per_rank[idx] == 1).sum())
+
+
+def ep_parity(R, layer, x, logits, inp, full_w, rank: int, world: int, dev) -> dict:
+    """Checks the expert-parallel output against the single-GPU layer after the timed steps ("the
+    output is checked against the 1-GPU result"), on a sample of this rank's tokens (a token's output depends only on
+    its own row and routing):
+
+    * bit-exact (compared as bits, so -0 and +0 differ): the single-GPU layer's own c3 rows (full weights, on this
+      GPU), combined per rank with that rank's pairs only (reaxmoe_combine with the other pairs unmapped), and the
+      per-rank rows summed in first-pair order (reaxmoe_ep_combine) -- the order the expert-parallel layer sums in;
+    * north-star tolerance (max-abs 2e-2, rel-L2 1e-2) against the single-GPU layer's output.
+    Every rank reports; a mismatch on any rank ends the run with a non-zero exit."""
+    import torch
+    import torch.distributed as dist
+    T, H = x.shape
+    k, E, I = layer.k, layer.E, layer.I
+    El = E // world
+    w, ids = R.route(None, logits, k)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    layer(x, w, ids, out)
+    idx, n_remote, n_single = ep_parity_sample(ids, El, world, rank, EP_PARITY_TOKENS)
+    n = int(idx.numel())
+    xs, ws, ids_s = x[idx].contiguous(), w[idx].contiguous(), ids[idx].contiguous()
+    st = R.Stages(n, H, I, E, k, layer.ops.act, dev)
+    st.plan(ids_s)
+    st.permute_quant(xs, inp["a1_gscale"])
+    st.gemm_w13(full_w["w1p"], full_w["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"])
+    st.gemm_w2(full_w["w2q"], full_w["w2sx"], inp["w2_alphas"])
+    single = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+    st.combine(ws, single)
+    owner = torch.where(ids_s >= 0, ids_s // El, -1).long()
+    cmap = st.c_map.view(n, k)
+    parts = []
+    for r in range(world):
+        pr = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        st.combine(ws, pr, c_map=torch.where(owner == r, cmap, -1).reshape(-1).contiguous())
+        parts.append(pr)
+    returned = torch.cat(parts).contiguous()
+    first = torch.full((n, k), -1, dtype=torch.int32, device=dev)
+    seen = torch.zeros(n, world, dtype=torch.bool, device=dev)
+    tok = torch.arange(n, device=dev)
+    for j in range(k):
+        o = owner[:, j]
+        new = (o >= 0) & ~seen[tok, o.clamp(min=0)]
+        first[:, j] = torch.where(new, (o.clamp(min=0) * n + tok).int(), first[:, j])
+        seen[tok[new], o[new]] = True
+    expect = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+    layer.ops.combine(first, returned, expect)
+    got = out[idx]
+    torch.cuda.synchronize(dev)
+    rows_differ = int((got.view(torch.int16) != expect.view(torch.int16)).any(1).sum())
+    d = got.float() - single.float()
+    max_abs = float(d.abs().max()) if n else 0.0
+    rel = float(d.norm() / single.float().norm().clamp(min=1e-30)) if n else 0.0
+    stats = torch.tensor([rows_differ, n, n_remote, n_single, max_abs, rel], dtype=torch.float64, device=dev)
+    every = [torch.empty_like(stats) for _ in range(world)]
+    dist.all_gather(every, stats)
+    every = torch.stack(every).cpu()
+    differ = int(every[:, 0].sum())
+    worst_abs, worst_rel = float(every[:, 4].max()), float(every[:, 5].max())
+    ok = differ == 0 and worst_abs <= 2e-2 and worst_rel <= 1e-2
+    res = dict(ok=ok, tokens_checked=int(every[:, 1].sum()), tokens_all_pairs_remote=int(every[:, 2].sum()),
+               one_pair_records=int(every[:, 3].sum()), rows_not_bit_exact=differ,
+               bit_exact_vs="single-GPU c3 rows combined per rank in the expert-parallel order",
+               max_abs_vs_single_gpu=worst_abs, rel_l2_vs_single_gpu=worst_rel,
+               tolerance="max-abs 2e-2, rel-L2 1e-2 (north star)")
+    if not ok:
+        if rank == 0:
+            print(json.dumps(dict(parity=res)), flush=True)
+        dist.barrier()
+        raise SystemExit(f"rank {rank}: expert-parallel output check failed: {res}")
+    return res
 
 
 def main():

@@ -191,7 +191,8 @@ int reaxmoe_gemm_w2(const reaxmoe_problem* p, const void* int_fp4, const void* i
                     void* stream);
 
 /* out[t] = bf16( sum_j bf16(c3[c_map[t*topk+j]] * bf16(w[t, j])) ), fp32 sums in the canonical order
- * ((s0 + s1) + s2) + s3 of 4 strided partial sums (blink_moe.py:168-198, ORDER 1 for top-8). */
+ * ((s0 + s1) + s2) + s3 of 4 strided partial sums (blink_moe.py:168-198, ORDER 1 for top-8). A pair with
+ * c_map -1 (no slot) adds exactly +0, whatever its weight. */
 int reaxmoe_combine(const reaxmoe_problem* p, const void* c3, const int32_t* c_map, const float* topk_weights,
                     void* output, void* stream);
 
@@ -214,8 +215,10 @@ int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, 
  * but no caller workspace: its scratch is a file-scope static device array of about 1 MiB that every GPU loading
  * this library holds until exit. Limit: tokens <= 65536 (REAXMOE_ERR_BAD_SHAPE beyond). The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress) and should come before any stream capture. All calls
- * share the array, so calls that overlap on the GPU (e.g. on two streams) race; routed ids outside [0, experts)
- * are skipped as in reaxmoe_plan. Allocates nothing (no cudaMalloc / cudaFree). */
+ * share the array, so calls that overlap on the GPU (e.g. on two streams) race. Routed ids outside [0, experts) are
+ * skipped as in reaxmoe_plan, but this entry point reports no device status for them (there is no workspace to
+ * hold the status word reaxmoe_read_status reads). Shapes are checked as in reaxmoe_plan. Allocates nothing (no
+ * cudaMalloc / cudaFree). */
 int reaxmoe_plan_static(const reaxmoe_problem* p, const int32_t* topk_ids, int32_t* expert_offsets,
                         int32_t* blockscale_offsets, int32_t* problem_sizes1, int32_t* problem_sizes2, void* stream);
 
@@ -308,7 +311,9 @@ int reaxmoe_ep_dispatch_pack(const reaxmoe_problem* p, int32_t ranks, const void
  * rows[s] + (i - bounds[s]) * hidden * 2 for the source s with bounds[s] <= i < bounds[s + 1] (host arrays:
  * bounds [ranks + 1] from 0 to local->tokens, non-decreasing; rows [ranks] device addresses, 32-byte aligned:
  * the row in rank s's return buffer of the first record s sent here). A record with exactly one local pair has its
- * row stored by the w2 GEMM's epilogue, the others by the pre-sum kernel; the rows are the same either way. */
+ * row stored by the w2 GEMM's epilogue, the others by the pre-sum kernel; the rows are bit-identical either way,
+ * signed zeros included, for router weights of any sign. Environment REAXMOE_EP_DIRECT_ROWS=0 (read once per
+ * process) sends every record through the pre-sum kernel. */
 int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
                                  const void* w1_sf, const float* w1_alphas, const float* a2_gscale,
                                  const void* w2_fp4, const void* w2_sf, const float* w2_alphas, void* workspace,

@@ -64,6 +64,9 @@ static int check_problem(const reaxmoe_problem* p, bool local_topk = false) {
   return 0;
 }
 
+// The shape checks of every entry point, for the other translation units (reaxmoe_plan_static).
+int check_problem_shape(const reaxmoe_problem* p) { return check_problem(p); }
+
 // Workspace regions, each 256-byte aligned.
 struct Layout {
   size_t status, seg_counts, seg_base, counts, eoff, boff, tile_prefix, c_map, rep_fp4, lin_sf, rep_sf, int_fp4,
@@ -197,6 +200,16 @@ static size_t ep_expert_direct_w(const reaxmoe_problem* p, const Layout& L) {
 }
 static size_t ep_expert_total(const reaxmoe_problem* p, const Layout& L) {
   return up256(ep_expert_direct_w(p, L) + (size_t)p->tokens * p->topk * 4);
+}
+
+// REAXMOE_EP_DIRECT_ROWS=0 turns off the w2-epilogue direct rows of the peer transport (every record's row then comes
+// from the pre-sum kernel); the rows are bit-identical either way. Read once per process.
+static bool ep_direct_rows() {
+  static const bool on = [] {
+    const char* v = getenv("REAXMOE_EP_DIRECT_ROWS");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
 }
 
 static unsigned long long device_timeout_ns() {
@@ -747,7 +760,7 @@ static int ep_expert_forward(const reaxmoe_problem* local, const void* recv_reco
   GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4, w.int_sf);
   if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "%s: gemm_w13 launch failed", who);
   GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, w2_fp4, w2_sf, w2_alphas, w.c3);
-  if (route != nullptr) {
+  if (route != nullptr && route->skip_single) {
     // records with one local pair: the w2 epilogue stores their finished rows straight to the source rank
     uint64_t* direct_dst = reinterpret_cast<uint64_t*>(b + ep_expert_direct(p, L));
     float* direct_w = reinterpret_cast<float*>(b + ep_expert_direct_w(p, L));
@@ -785,7 +798,7 @@ int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_
     return fail(REAXMOE_ERR_BAD_SHAPE, "ep_expert_forward_to: bounds must run from 0 to tokens=%d", local->tokens);
   RowRoute route{};
   route.ranks = ranks;
-  route.skip_single = 1;
+  route.skip_single = ep_direct_rows() ? 1 : 0;
   for (int q = 0; q <= ranks; ++q) {
     if (q > 0 && bounds[q] < bounds[q - 1])
       return fail(REAXMOE_ERR_BAD_SHAPE, "ep_expert_forward_to: bounds decrease at %d", q);

@@ -429,7 +429,8 @@ __global__ void __launch_bounds__(256, 3) combine_kernel_k(const __nv_bfloat16* 
     float myw = 0.0f;
     if (lane < K) {
       mypos = c_map[t * K + lane];
-      myw = bf16r(topk_w[t * K + lane]);
+      // an unmapped pair (no slot) adds exactly +0: its weight is taken as +0, whatever the router gave it
+      myw = mypos >= 0 ? bf16r(topk_w[t * K + lane]) : 0.0f;
     }
     const uint4* rowp[K];
     float wb[K];
@@ -470,7 +471,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
     float myw = 0.0f;
     if (lane < k) {
       mypos = c_map[t * k + lane];
-      myw = bf16r(topk_w[t * k + lane]);
+      myw = mypos >= 0 ? bf16r(topk_w[t * k + lane]) : 0.0f;   // an unmapped pair adds exactly +0
     }
     int pos[kMaxTopk];
     float wb[kMaxTopk];

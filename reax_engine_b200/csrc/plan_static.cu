@@ -1,11 +1,11 @@
 // plan_static.cu -- the routing-data plan (reaxmoe_plan) for callers that cannot allocate device memory.
 //
 // Some callers of this library run where cudaMalloc is off limits: a plugin's enqueue step inside an inference
-// runtime that plans all device memory ahead of time and forbids allocation during execution, or code that runs
-// while a CUDA graph is being captured and must not create new allocations. reaxmoe_plan_static gives them the
-// same routing data as reaxmoe_plan without a caller workspace: its scratch (per-segment expert histograms and
-// their prefix sums, the status word) lives in one file-scope __device__ array of fixed size, which every GPU
-// that loads this library holds until the process exits.
+// runtime that plans all device memory ahead of time and forbids allocation while it executes. reaxmoe_plan_static
+// gives them the same routing data as reaxmoe_plan without a caller workspace: its scratch (per-segment expert
+// histograms and their prefix sums, the status word its count kernel needs) lives in one file-scope __device__
+// array of fixed size, which every GPU that loads this library holds until the process exits. It reports no device
+// status: routed ids outside [0, experts) are skipped, as reaxmoe_plan skips them, but nothing tells the caller.
 #include <mutex>
 
 #include "common.cuh"
@@ -14,6 +14,7 @@
 namespace reaxmoe {
 
 int set_error(int code, const char* msg);  // api.cu: records the text returned by reaxmoe_last_error
+int check_problem_shape(const reaxmoe_problem* p);  // api.cu: the shape checks of every entry point
 
 // Limits of the static scratch: at most kStaticMaxTokens tokens (all experts up to kMaxExperts).
 constexpr int kStaticMaxTokens = 65536;
@@ -59,9 +60,9 @@ int reaxmoe_plan_static(const reaxmoe_problem* p, const int32_t* topk_ids, int32
                         void* stream) {
   if (p == nullptr || topk_ids == nullptr || expert_offsets == nullptr || blockscale_offsets == nullptr)
     return set_error(REAXMOE_ERR_NULL, "plan_static: NULL pointer");
-  if (p->experts < 1 || p->experts > kMaxExperts || p->topk < 1 || p->topk > kMaxTopk || p->topk > p->experts)
-    return set_error(REAXMOE_ERR_TOO_MANY_EXPERTS, "plan_static: experts / topk outside the supported range");
-  if (p->tokens < 0 || p->tokens > kStaticMaxTokens)
+  const int rc = check_problem_shape(p);   // the same shape checks (and error text) as reaxmoe_plan
+  if (rc) return rc;
+  if (p->tokens > kStaticMaxTokens)
     return set_error(REAXMOE_ERR_BAD_SHAPE, "plan_static: tokens outside [0, 65536], the limit of its static scratch");
   void* base = nullptr;
   int dev = 0;

@@ -33,6 +33,8 @@ class MoEActivation(enum.IntEnum):
     def parse(a) -> "MoEActivation":
         if isinstance(a, MoEActivation):
             return a
+        if isinstance(a, int):
+            return MoEActivation(a)
         name = getattr(a, "name", a)
         name = str(name).lower()
         if name in ("silu", "swiglu"):

@@ -83,3 +83,69 @@ class HostStreamedMoE:
                 self.out_done[slot].record(self.s_out)
             self.count += 1
         cur.wait_stream(self.s_out)
+
+
+class HostStreamedEP:
+    """The expert-parallel layer (:class:`reax_engine_b200.ep.ExpertParallelMoE`) over pinned host tensors.
+
+    The rank's tokens are cut into ``chunks`` parts. Every part's input copy is queued at once on an input stream,
+    each part runs routing + the expert-parallel forward on a compute stream as soon as its inputs have landed, and
+    its output is copied back on an output stream while the next part computes. Every rank must call it with the
+    same ``chunks`` (each part is one collective forward of the layer); a token's output is exactly what one forward
+    over the whole batch gives it. Device buffers hold one batch and are reused across calls; a call's input copies
+    wait until the previous call's forward of the same part has consumed its inputs."""
+
+    def __init__(self, layer, device, chunks: int = 4, per_expert_scale=None):
+        self.layer = layer
+        self.dev = torch.device(device)
+        self.chunks = max(1, int(chunks))
+        self.pes = per_expert_scale
+        self.s_in = torch.cuda.Stream(self.dev)
+        self.s_cmp = torch.cuda.Stream(self.dev)
+        self.s_out = torch.cuda.Stream(self.dev)
+        self.cap = 0
+        self.in_done = [torch.cuda.Event() for _ in range(self.chunks)]
+        self.cmp_done = [torch.cuda.Event() for _ in range(self.chunks)]
+        self.out_done = [torch.cuda.Event() for _ in range(self.chunks)]
+        self.calls = 0
+
+    def _buffers(self, T: int, H: int, E: int) -> None:
+        if T > self.cap:
+            torch.cuda.synchronize(self.dev)     # the old buffers may still be in use on the three streams
+            self.x_d = torch.empty(T, H, dtype=torch.bfloat16, device=self.dev)
+            self.lg_d = torch.empty(T, E, dtype=torch.float32, device=self.dev)
+            self.out_d = torch.empty(T, H, dtype=torch.bfloat16, device=self.dev)
+            self.cap = T
+
+    def __call__(self, x_host: torch.Tensor, logits_host: torch.Tensor, out_host: torch.Tensor) -> None:
+        """x_host [T, hidden] bf16, logits_host [T, experts] fp32 (global expert ids), out_host [T, hidden] bf16,
+        all pinned. Asynchronous like :class:`HostStreamedMoE`: synchronise the caller's current stream before
+        reading ``out_host``."""
+        assert not x_host.is_cuda and x_host.is_pinned(), "x_host must be pinned host memory"
+        assert logits_host.is_pinned() and out_host.is_pinned(), "logits_host and out_host must be pinned host memory"
+        T, H = x_host.shape
+        self._buffers(T, H, logits_host.shape[1])
+        step = -(-T // self.chunks) if T else 0
+        parts = [(min(T, c * step), min(T, (c + 1) * step)) for c in range(self.chunks)]
+        cur = torch.cuda.current_stream(self.dev)
+        with torch.cuda.stream(self.s_in):
+            for c, (t0, t1) in enumerate(parts):
+                if self.calls > 0:
+                    self.s_in.wait_event(self.cmp_done[c])   # the previous call's forward has read this part
+                self.x_d[t0:t1].copy_(x_host[t0:t1], non_blocking=True)
+                self.lg_d[t0:t1].copy_(logits_host[t0:t1], non_blocking=True)
+                self.in_done[c].record(self.s_in)
+        for c, (t0, t1) in enumerate(parts):
+            with torch.cuda.stream(self.s_cmp):
+                self.s_cmp.wait_event(self.in_done[c])
+                if self.calls > 0:
+                    self.s_cmp.wait_event(self.out_done[c])  # the previous call's output of this part is out
+                w, ids = route(None, self.lg_d[t0:t1], self.layer.k, True, self.pes)
+                self.layer(self.x_d[t0:t1], w, ids, self.out_d[t0:t1])
+                self.cmp_done[c].record(self.s_cmp)
+            with torch.cuda.stream(self.s_out):
+                self.s_out.wait_event(self.cmp_done[c])
+                out_host[t0:t1].copy_(self.out_d[t0:t1], non_blocking=True)
+                self.out_done[c].record(self.s_out)
+        self.calls += 1
+        cur.wait_stream(self.s_out)

@@ -19,6 +19,7 @@ import torch
 import torch.multiprocessing as mp
 
 from moe_cases import make_case, tol_check
+from oracle import moe_oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -42,7 +43,7 @@ def _single_gpu(R, c, w, ids, T, H, E, k, inter, dev="cuda"):
     return st, single
 
 
-def _emulate_p2p(R, c, w, ids, Ts, ranks):
+def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False):
     """R ranks on one GPU over the peer-memory device halves: plan, pack into the destinations' receive buffers,
     expert forward into the sources' return buffers, combine."""
     from test_gpu_ep import _local
@@ -66,16 +67,17 @@ def _emulate_p2p(R, c, w, ids, Ts, ranks):
     for d in range(ranks):
         _, bounds, rows, n_recv, _ = R.ep.p2p_addresses(C, d, rec, row, recv_ptrs, ret_ptrs)
         ops[d].expert_forward_to(recv_ptrs[d], n_recv, _local(R, c, d, ranks), bounds, rows)
-    outs = []
+    outs, rows_back = [], []
     for s in range(ranks):
         n_send = sum(C[s])
+        rows_back.append(ret[s][:n_send * row].view(torch.bfloat16).view(n_send, H))
         out = torch.empty(Ts[s], H, dtype=torch.bfloat16, device="cuda")
-        ops[s].combine(maps[s], ret[s][:n_send * row].view(torch.bfloat16).view(n_send, H), out)
+        ops[s].combine(maps[s], rows_back[-1], out)
         outs.append(out)
     torch.cuda.synchronize()
     for o in ops:
         assert o.status() == 0
-    return torch.cat(outs)
+    return (torch.cat(outs), rows_back) if return_rows else torch.cat(outs)
 
 
 @pytest.mark.parametrize("ranks,Ts", [(2, [700, 313]), (4, [256, 0, 511, 64]), (8, [100] * 8)])
@@ -91,6 +93,44 @@ def test_p2p_emulated_ranks_bit_exact(R, ranks, Ts):
     assert np.array_equal(got.float().cpu().numpy(), expect)
     assert torch.equal(got, _emulate(R, c, w, ids, Ts, ranks))
     tol_check(got.float().cpu().numpy(), single.float().cpu().numpy())
+
+
+def test_p2p_direct_rows_keep_signed_zeros(R):
+    """Records with one local pair get their returned row from the w2 epilogue (direct rows), the others from the
+    pre-sum kernel. Both must equal the single-GPU combine of the record's local pairs bit for bit, signed zeros
+    included: with zero token rows (c3 rows of zeros) and negative router weights, a record's row is -0 exactly when
+    every term of its combine is -0, i.e. every weight of the token is negative. Compared as bits (-0 != +0)."""
+    ranks, Ts = 8, [96] * 8
+    T, H, E, k, inter = sum(Ts), 2816, 128, 8, 704
+    El = E // ranks
+    c = make_case(T, H, E, k, inter, "gelu_tanh", seed=21)
+    w, ids = R.route(None, c["logits"], k)
+    t = torch.arange(T, device="cuda")
+    c["x"][t % 2 == 0] = 0.0                                       # zero rows: c3 rows of zeros
+    sign = torch.ones(T, k, device="cuda")
+    sign[t % 3 == 0] = -1.0                                        # every weight negative
+    sign[t % 3 == 1, 0] = -1.0                                     # mixed signs
+    w = (w * sign).contiguous()
+    st, _ = _single_gpu(R, c, w, ids, T, H, E, k, inter)
+    _, rows_back = _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=True)
+    c3, cmap = st.c3.float().cpu().numpy(), st.c_map.cpu().numpy().reshape(T, k)
+    idn, wn = ids.cpu().numpy(), w.cpu().numpy()
+    owner = idn // El
+    starts = np.concatenate([[0], np.cumsum(Ts)]).astype(int)
+    singles = neg = 0
+    for s in range(ranks):
+        toks = np.arange(starts[s], starts[s + 1])
+        expect = []
+        for d in range(ranks):
+            mine = toks[(owner[toks] == d).any(1)]
+            cm = np.where(owner[mine] == d, cmap[mine], -1)
+            expect.append(O.combine(c3, cm.reshape(-1), wn[mine]))
+            singles += int(((owner[mine] == d).sum(1) == 1).sum())
+        expect = np.concatenate(expect)
+        got = rows_back[s].view(torch.int16).cpu().numpy().view(np.uint16)
+        assert np.array_equal(got, O.bf16_bits(expect)), f"source {s}: returned rows differ"
+        neg += int((got == 0x8000).all(1).sum())
+    assert singles > 100 and neg > 0            # the direct-row path and -0 rows were both exercised
 
 
 def _ipc_block(R):
