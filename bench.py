@@ -174,7 +174,6 @@ def build_inputs(wl: dict, device, seed: int = 0):
                a2_gscale=torch.full((E,), 1.0 / a2_g, device=device),
                w1_alphas=(w1g * a1_g).float(), w2_alphas=(w2g * a2_g).float(), w1g=w1g, a2_g=a2_g)
     inp["w1p"], inp["w1p_sf"] = R.prepack_w13(w1q, w1s, I)
-    inp["w2sx"] = R.expand_scales(w2s, H, I)
     torch.cuda.synchronize(device)
     return inp
 
@@ -353,7 +352,7 @@ def run_ours(args, wl: dict) -> None:
         if ev is not None: ev[2].record(s)
         st.gemm_w13(inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"])
         if ev is not None: ev[3].record(s)
-        st.gemm_w2(inp["w2q"], inp["w2sx"], inp["w2_alphas"])
+        st.gemm_w2(inp["w2q"], inp["w2s"], inp["w2_alphas"])
         if ev is not None: ev[4].record(s)
         st.combine(w, out)
         if ev is not None: ev[5].record(s)
@@ -399,7 +398,7 @@ def run_ours(args, wl: dict) -> None:
         lg_h = inp["logits"].cpu().pin_memory()
         out_h = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
         host_layer = R.HostStreamedMoE(H, I, E, k, wl["act"], inp["a1_gscale"], inp["w1p"], inp["w1p_sf"],
-                                       inp["w1_alphas"], inp["a2_gscale"], inp["w2q"], inp["w2sx"], inp["w2_alphas"],
+                                       inp["w1_alphas"], inp["a2_gscale"], inp["w2q"], inp["w2s"], inp["w2_alphas"],
                                        dev, chunk_tokens=E2E_CHUNK)
 
         def e2e_step():
@@ -537,11 +536,11 @@ def run_ours_ep(args, wl: dict) -> None:
     sl = slice(rank * El, (rank + 1) * El)
     w1p, w1p_sf = R.prepack_w13(inp["w1q"][sl].contiguous(), inp["w1s"][sl].contiguous(), I)
     local_w = R.ep.LocalExperts(w1p, w1p_sf, inp["w1_alphas"][sl].contiguous(), inp["a2_gscale"][sl].contiguous(),
-                                inp["w2q"][sl].contiguous(), R.expand_scales(inp["w2s"][sl].contiguous(), H, I),
+                                inp["w2q"][sl].contiguous(), inp["w2s"][sl].contiguous(),
                                 inp["w2_alphas"][sl].contiguous())
     weight_bytes = sum(t.numel() for t in (inp["w1q"], inp["w1s"], inp["w2q"], inp["w2s"])) // world
-    full_w = dict(w1p=inp.pop("w1p"), w1p_sf=inp.pop("w1p_sf"), w2q=inp.pop("w2q"), w2sx=inp.pop("w2sx"))
-    for key in ("w1q", "w1s", "w2s"):
+    full_w = dict(w1p=inp.pop("w1p"), w1p_sf=inp.pop("w1p_sf"), w2q=inp.pop("w2q"), w2s=inp.pop("w2s"))
+    for key in ("w1q", "w1s"):
         inp.pop(key)
     torch.cuda.empty_cache()
     layer = R.ep.ExpertParallelMoE(H, I, E, k, wl["act"], inp["a1_gscale"], local_w,
@@ -712,7 +711,7 @@ def ep_parity(R, layer, x, logits, inp, full_w, rank: int, world: int, dev) -> d
     st.plan(ids_s)
     st.permute_quant(xs, inp["a1_gscale"])
     st.gemm_w13(full_w["w1p"], full_w["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"])
-    st.gemm_w2(full_w["w2q"], full_w["w2sx"], inp["w2_alphas"])
+    st.gemm_w2(full_w["w2q"], full_w["w2s"], inp["w2_alphas"])
     single = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
     st.combine(ws, single)
     owner = torch.where(ids_s >= 0, ids_s // El, -1).long()

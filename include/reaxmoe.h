@@ -84,11 +84,11 @@ typedef struct reaxmoe_forward_args {
   const void* a;              /* [tokens, hidden] bf16 */
   const float* a1_gscale;     /* [experts] quant-side input scale of w13 */
   const void* w1_fp4;         /* [experts, 2*inter, hidden/2] u8, gate/up INTERLEAVED (reaxmoe_prepack_w13) */
-  const void* w1_sf;          /* scales of the interleaved w1_fp4, expanded by reaxmoe_expand_scales(n = 2*inter, k = hidden) */
+  const void* w1_sf;          /* scale atoms of the interleaved w1_fp4, as reaxmoe_prepack_w13 writes them */
   const float* w1_alphas;     /* [experts] */
   const float* a2_gscale;     /* [experts] quant-side scale of the intermediate */
   const void* w2_fp4;         /* [experts, hidden, inter/2] u8 */
-  const void* w2_sf;          /* scales of w2_fp4, expanded by reaxmoe_expand_scales(n = hidden, k = inter) */
+  const void* w2_sf;          /* scale atoms of w2_fp4 as engine/fp4.py lays them out: [experts][hidden/128][inter/64][512] */
   const float* w2_alphas;     /* [experts] */
   const float* topk_weights;  /* [tokens, topk] fp32 */
   const int32_t* topk_ids;    /* [tokens, topk] int32; a negative id marks an unused slot (contributes nothing) */
@@ -179,13 +179,13 @@ int reaxmoe_permute_quant(const reaxmoe_problem* p, const void* a, const float* 
 
 /* Grouped NVFP4 GEMM w13 with the fused activation(gate) * up and NVFP4 re-quantisation epilogue
  * (blink_moegemm.cu:472-934 MODE 1). Needs the plan of the same workspace. w1_fp4 is interleaved
- * (reaxmoe_prepack_w13) and w1_sf expanded (reaxmoe_expand_scales). hidden <= 3072. */
+ * (reaxmoe_prepack_w13) with its scale atoms. hidden <= 3072. */
 int reaxmoe_gemm_w13(const reaxmoe_problem* p, const void* rep_fp4, const void* rep_sf, const void* w1_fp4,
                      const void* w1_sf, const float* w1_alphas, const float* a2_gscale, void* workspace,
                      size_t workspace_bytes, void* int_fp4, void* int_sf, void* stream);
 
-/* Grouped NVFP4 GEMM w2: c3[slot] = bf16(alpha_e * int[slot] . w2_e^T) (blink_moegemm.cu:1173-1197). w2_sf expanded
- * (reaxmoe_expand_scales). inter <= 3072. */
+/* Grouped NVFP4 GEMM w2: c3[slot] = bf16(alpha_e * int[slot] . w2_e^T) (blink_moegemm.cu:1173-1197). w2_sf: the
+ * engine/fp4.py scale atoms of w2_fp4 as they are. inter <= 3072. */
 int reaxmoe_gemm_w2(const reaxmoe_problem* p, const void* int_fp4, const void* int_sf, const void* w2_fp4,
                     const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes, void* c3,
                     void* stream);
@@ -221,14 +221,6 @@ int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, 
  * cudaMalloc / cudaFree). */
 int reaxmoe_plan_static(const reaxmoe_problem* p, const int32_t* topk_ids, int32_t* expert_offsets,
                         int32_t* blockscale_offsets, int32_t* problem_sizes1, int32_t* problem_sizes2, void* stream);
-
-/* One-time expansion of weight block scales ([experts][n/128][k/64][512] atoms, engine/fp4.py layout per expert) into
- * the grouped GEMMs' B-scale records: [experts][ceil(n/256)][k/64][4096 B]. Each record holds the scales of one 256-row
- * n-tile and one 64-element k-chunk laid out for a single tcgen05.cp.128x256b (16 groups of 8 rows: block 0's 8 rows
- * of 16 B then block 1's; row i of group g = row (8g+i) % 32 of the 512-byte atom); a 128-row last tile has zeros
- * for block 1. Size: reaxmoe_expanded_scales_size(). */
-size_t reaxmoe_expanded_scales_size(int32_t experts, int32_t n, int32_t k);
-int reaxmoe_expand_scales(const void* sf, int32_t experts, int32_t n, int32_t k, void* out, void* stream);
 
 /* ---- Expert parallelism (no counterpart in the reference, which requires ep_size == 1 at
  * champions/uid240/opt/blink/blink_par.py:99). The three calls below are the device halves of vLLM's

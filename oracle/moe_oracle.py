@@ -470,25 +470,6 @@ def interleave_w13(w1_fp4: np.ndarray, w1_sf: np.ndarray, inter: int, half_tile:
     return fp4, sf
 
 
-def expand_b_scales(w_sf: np.ndarray, N: int, K: int) -> np.ndarray:
-    """The grouped GEMMs' B-scale records (test restatement of reaxmoe_expand_scales): w_sf [E, N/128 atoms-rows *
-    K/64 atoms * 512] -> [E, ceil(N/256), K/64, 4096]: per record 16 groups of 8 rows, block 0's rows then block 1's,
-    row i of group g = row (8g + i) % 32 of the 512-byte atom; zeros for a missing block 1."""
-    E = w_sf.shape[0]
-    kc = K // 64
-    nblk = N // 128
-    nt = -(-N // 256)
-    atoms = np.asarray(w_sf, dtype=np.uint8).reshape(E, nblk, kc, 32, 16)
-    out = np.zeros((E, nt, kc, 16, 2, 8, 16), dtype=np.uint8)
-    rows = (8 * np.arange(16)[:, None] + np.arange(8)[None, :]) % 32
-    for t in range(nt):
-        for h in range(2):
-            b = 2 * t + h
-            if b < nblk:
-                out[:, t, :, :, h] = atoms[:, b][:, :, rows]
-    return out.reshape(E, nt, kc, 4096)
-
-
 # ----------------------------------------------------------------------------------------------------------
 # Expert parallelism (no counterpart in the reference, which requires ep_size == 1 at
 # ``champions/uid240/opt/blink/blink_par.py:99``). Restates the record exchange of the library's EP path: each

@@ -78,8 +78,6 @@ SIGNATURES = {
     "reaxmoe_prepack_w13": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P]),
     "reaxmoe_read_status": (ctypes.c_int, [_P, ctypes.c_size_t, _I32, _P]),
     "reaxmoe_plan_static": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P]),
-    "reaxmoe_expanded_scales_size": (ctypes.c_size_t, [_I32, _I32, _I32]),
-    "reaxmoe_expand_scales": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P]),
     "reaxmoe_ep_record_bytes": (ctypes.c_size_t, [_I32, _I32]),
     "reaxmoe_ep_dispatch_workspace_size": (ctypes.c_size_t, [_PP, _I32]),
     "reaxmoe_ep_dispatch": (ctypes.c_int, [_PP, _I32, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, _P, _P]),

@@ -603,21 +603,6 @@ int reaxmoe_prepack_w13(const void* w1_fp4, const void* w1_sf, int32_t experts, 
   return cuda_check("prepack_w13");
 }
 
-size_t reaxmoe_expanded_scales_size(int32_t experts, int32_t n, int32_t k) {
-  if (experts < 1 || n < 128 || n % 128 != 0 || k < 64 || k % 64 != 0) return 0;
-  return (size_t)experts * ((n + 255) / 256) * (k / 64) * 4096;
-}
-
-int reaxmoe_expand_scales(const void* sf, int32_t experts, int32_t n, int32_t k, void* out, void* stream) {
-  if (reaxmoe_expanded_scales_size(experts, n, k) == 0)
-    return fail(REAXMOE_ERR_BAD_SHAPE, "expand_scales: experts=%d n=%d k=%d (n %% 128, k %% 64)", experts, n, k);
-  if (!sf || !out) return fail(REAXMOE_ERR_NULL, "expand_scales: NULL pointer");
-  if (!aligned16(sf) || !aligned16(out)) return fail(REAXMOE_ERR_MISALIGNED, "expand_scales: misaligned");
-  launch_expand_scales(static_cast<const uint8_t*>(sf), experts, n, k, static_cast<uint8_t*>(out),
-                       static_cast<cudaStream_t>(stream));
-  return cuda_check("expand_scales");
-}
-
 size_t reaxmoe_ep_record_bytes(int32_t hidden, int32_t topk) {
   if (hidden < 128 || hidden % 128 != 0 || topk < 1 || topk > kMaxTopk) return 0;
   const size_t b = (size_t)hidden / 2 + (size_t)hidden / 16 + (size_t)topk * 8;

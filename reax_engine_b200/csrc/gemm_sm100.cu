@@ -10,21 +10,22 @@
 //
 // Design (one CTA per SM, persistent). Work is handed out per m-tile (expert, 128 routed rows); a CTA computes all
 // n-tiles of its m-tile in a row (256 output columns each; a narrower last n-tile of 128 when N % 256 == 128).
-//   warp 0      TMA producer: A (routed FP4 rows, 128 x 256 K) and B (expert weights, 256 x 256 K) tiles by 2D TMA
-//               with 128-byte swizzle plus the stage's B-scale records by one 1D bulk copy, into a 3-deep ring;
-//               once per m-tile, all its A scale atoms by a bulk copy.
-//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.mma.kind::mxf4nvf4.block_scale.block16
-//               (M=128, N=256, K=64: 512 clk of tensor work per stage, enough to hide the per-stage barrier
-//               round trip) into the fp32 accumulator, and tcgen05.commit.
-//   warp 2      one thread issues every tcgen05.cp: once per m-tile the A scales into a resident TMEM region
-//               (32x128b.warpx4 per 64-element chunk), and per k-step the B scales of the whole 256-row tile with a
-//               single 128x256b copy of the pre-expanded record (reaxmoe_expand_scales), into one of two buffers.
-//               Copies cost tensor-pipe time in proportion to the (4x replicated) TMEM bytes they write; issued from
-//               this thread they overlap the MMAs, and the MMA thread's barrier waits do not queue behind them.
-//   warps 3..   epilogue (8 for w13, 16 for w2): tcgen05.ld the whole accumulator into registers (each warp owns its
-//               32-lane TMEM quarter and a half / quarter of the columns) and release it to the MMA warp at once,
+//   warp 0      TMA producer, into a 4-deep ring of 54 KiB stages: A (routed FP4 rows, 128 x 256 K) and B (expert
+//               weights, 256 x 256 K) by 2D TMA with 128-byte swizzle, plus the stage's scale atoms as they lie in
+//               memory (engine/fp4.py 128x4 atoms, 512 B per 128 rows x 64-element k-chunk) by 1D bulk copies: the
+//               A scales of the m-tile's rows and the B scales of the n-tile's two 128-row blocks.
+//   warp 1      allocates 512 TMEM columns (warps 2-3 idle); one thread issues tcgen05.mma.kind::mxf4nvf4.block_scale.block16
+//               (M=128, N=256, K=64; 4 per stage) into the fp32 accumulator and commits each stage to its empty
+//               barrier (which frees the stage's shared memory and its scale columns in TMEM).
+//   warps 4-7   scale writers, one per TMEM lane quarter: each lane reads one 16-byte row of every scale atom of the
+//               stage from shared memory and writes it into its lane with tcgen05.st -- the TMEM image the MMA reads
+//               (A: lane i gets atom row i in 4 columns; B: atom row i of block 0 then of block 1 in 8 columns,
+//               replicated in every quarter). Written from registers, these stores do not queue in the tensor pipe
+//               behind the running MMAs (a tcgen05.cp would, and the next stage's MMAs would wait on its commit).
+//   warps 8-15  epilogue: tcgen05.ld the whole accumulator into registers (each warp owns its 32-lane TMEM quarter and
+//               half of the columns) and release it to the MMA warp at once,
 //               then convert / activate / quantise and store while the next unit's MMAs run.
-// TMEM: accumulator [0, 256), two B-scale buffers of 32 columns, resident A scales (4 columns per k-chunk).
+// TMEM: accumulator [0, 256); per stage, A scales (16 columns) and B scales (32 columns) -- 448 columns in all.
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records REAXMOE_ERR_DEVICE_TIMEOUT in the
 // status word, raises a CTA-wide abort flag, drains its own in-flight copies and MMAs, frees TMEM and returns.
 // Plain per-CTA TMA loads, no thread-block clusters: the same kernel runs on every rank of the expert-parallel path.
@@ -46,28 +47,30 @@ constexpr int KSTAGE = 256;             // K per pipeline stage = one 128-byte s
 constexpr int KPS = KSTAGE / KSTEP;     // MMAs per stage
 constexpr int A_BYTES = BM * KSTAGE / 2;
 constexpr int B_BYTES = BN * KSTAGE / 2;
-constexpr int SFB_REC = 4096;           // expanded B-scale record per k-chunk
-constexpr int SFB_BYTES = KPS * SFB_REC;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFB_BYTES;
-constexpr int STAGES = 3;
-constexpr int MAX_K_CHUNKS = 48;        // K <= 3072: the resident A scales fit in TMEM
-constexpr int SFA_SMEM_BYTES = MAX_K_CHUNKS * 512;
-constexpr int EPI_WARP0 = 3;
-// Epilogue warps: w13 (mode 1) 8, two per TMEM lane quarter, each half of the tile's columns; w2 (mode 0) 16, four
-// per quarter, each a quarter of the columns (its epilogue is bound by the bf16 stores: more warps keep more of them
-// in flight; w13's activation + quantisation measured slower with 16, its extra issue pressure landing on the
-// single-thread producer / MMA / copy warps).
-__host__ __device__ constexpr int epi_warps(int mode) { return mode == 0 ? 16 : 8; }
-__host__ __device__ constexpr int threads_for(int mode) { return (EPI_WARP0 + epi_warps(mode)) * 32; }
+constexpr int SF_ATOM = 512;            // scales of 128 rows x one 64-element k-chunk (a 128x4 atom)
+constexpr int SFA_BYTES = KPS * SF_ATOM;        // the stage's A scale atoms
+constexpr int SFB_BYTES = 2 * KPS * SF_ATOM;    // the stage's B scale atoms: block 0 (rows 0-127), then block 1
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int STAGES = 4;
+// Four warpgroups: 0 = producer (warp 0), MMA issuer (warp 1), two idle warps; 1 = the scale writers (warps 4-7, one
+// per TMEM lane quarter); 2 and 3 = the epilogue (warps 8-15, two per lane quarter, each half of the tile's columns).
+// Launched with 128 registers a thread; warpgroups 0 and 1 hand registers to the epilogue with setmaxnreg
+// (2 x 128 x 56 + 2 x 128 x 200 = 65536, the launch's total).
+constexpr int SCALE_WARP0 = 4;
+constexpr int EPI_WARP0 = 8;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
+constexpr int REGS_CONTROL = 56;
+constexpr int REGS_EPILOGUE = 200;
+static_assert(2 * 128 * REGS_CONTROL + 2 * 128 * REGS_EPILOGUE <= 65536, "register split above the launch total");
 constexpr int TMEM_COLS = 512;
-constexpr int SFB_COL = BN;             // two B-scale buffers of 8 * KPS columns
-constexpr int SFB_BUF_COLS = 8 * KPS;
-constexpr int SFA_COL = SFB_COL + 2 * SFB_BUF_COLS;
-constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 2 + 2;
+constexpr int SFA_COL = BN;                           // A scales of stage s: columns SFA_COL + 16 s + 4 kk
+constexpr int SFB_COL = SFA_COL + STAGES * 4 * KPS;   // B scales of stage s: columns SFB_COL + 32 s + 8 kk
+constexpr int NUM_BARS = 3 * STAGES + 3;
 constexpr int SMEM_TABLE_INTS = 4 * (kMaxExperts + 1);
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + SFA_SMEM_BYTES + 256 + SMEM_TABLE_INTS * 4;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + SMEM_TABLE_INTS * 4;
 static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned for the 128B swizzle");
-static_assert(SFA_COL + 4 * MAX_K_CHUNKS <= TMEM_COLS, "TMEM budget");
+static_assert(SFB_COL + STAGES * 8 * KPS <= TMEM_COLS, "TMEM budget");
 static_assert(NUM_BARS * 8 + 8 <= 256, "barrier area");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
@@ -81,8 +84,8 @@ __host__ __device__ constexpr uint32_t idesc_for(int n) {
 struct Params {
   CUtensorMap tmA;  // [slots, K/2] u8, box 128 x 128 rows, 128B swizzle
   CUtensorMap tmB;  // [E*N, K/2] u8, same box
-  const uint8_t* sfA;
-  const uint8_t* sfB;
+  const uint8_t* sfA;   // A scale atoms [row blocks][k_chunks][512] (blockscale_offsets rows)
+  const uint8_t* sfB;   // B scale atoms as engine/fp4.py lays them out: [E][N/128][k_chunks][512]
   const float* alphas;
   const int* counts;
   const int* eoff;
@@ -97,13 +100,10 @@ struct Params {
   const uint64_t* direct_dst;  // mode 0: per slot row, its record's return address (0 = write c3)
   const float* direct_w;
   int topk;
-  int E, N, K, n_tiles, k_chunks;
+  int E, N, K, n_tiles, k_chunks, n_blocks;
   int tail_n;           // width of the last n-tile (256, or 128 when N % 256 == 128)
 };
 
-__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
 __device__ __forceinline__ void tc_mma_fp4(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
                                            uint32_t sfb, uint32_t accumulate) {
   asm volatile(
@@ -113,21 +113,6 @@ __device__ __forceinline__ void tc_mma_fp4(uint32_t d, uint64_t adesc, uint64_t 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
       : "memory");
 }
-
-// Scale atoms for tcgen05.cp 32x128b: no swizzle, 32 rows x 16 bytes, 8-row core matrices 128 bytes apart.
-__device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | (8ull << 32) | (1ull << 46);
-}
-
-// Expanded B-scale record for tcgen05.cp 128x256b: no swizzle, 8-row groups 256 bytes apart (SBO), the two 16-byte
-// halves of each row 128 bytes apart (LBO).
-__device__ __forceinline__ uint64_t desc_sfb_x(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) | (1ull << 46);
-}
-__device__ __forceinline__ void tc_cp_sfb_x(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
 
 struct MTile {
   int e, mt, row0, rows, sfblk;
@@ -199,22 +184,17 @@ __device__ __forceinline__ uint32_t act_quant32(const uint32_t (&x0)[32], const 
 }
 
 template <int MODE, int ACT>
-__global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
-  constexpr int NUM_EPI_WARPS = epi_warps(MODE);
+__global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sfa_smem = smem + STAGES * STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sfa_smem + SFA_SMEM_BYTES);
-  uint64_t* full = bars;                 // [STAGES] A, B and the B-scale records landed (TMA tx)
-  uint64_t* empty = bars + STAGES;       // [STAGES] MMAs of the stage done: smem stage free
-  uint64_t* sff = empty + STAGES;        // [2] B-scale TMEM buffer b filled (commit of the copy thread)
-  uint64_t* accf = sff + 2;              // accumulator ready for the epilogue
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                 // [STAGES] A, B and the scale atoms landed (TMA tx)
+  uint64_t* empty = bars + STAGES;       // [STAGES] MMAs of the stage done: smem stage and its TMEM scales free
+  uint64_t* sff = empty + STAGES;        // [STAGES] the stage's scales written to TMEM (4 scale-writer warps)
+  uint64_t* accf = sff + STAGES;         // accumulator ready for the epilogue
   uint64_t* acce = accf + 1;             // accumulator drained by the epilogue
-  uint64_t* sfa_full = acce + 1;         // A scales of the next m-tile landed in smem
-  uint64_t* sfa_ready = sfa_full + 1;    // A scales copied to TMEM (and the smem copy free again)
-  uint64_t* drain_mma = sfa_ready + 1;
-  uint64_t* drain_cp = drain_mma + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_cp + 1);
+  uint64_t* drain_mma = acce + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_mma + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   int* s_tp = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + 256);
   int* s_cnt = s_tp + (kMaxExperts + 1);
@@ -236,15 +216,11 @@ __global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(cons
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
+      mbar_init(smem_u32(&sff[s]), 4);
     }
-    mbar_init(smem_u32(&sff[0]), 1);
-    mbar_init(smem_u32(&sff[1]), 1);
     mbar_init(smem_u32(accf), 1);
     mbar_init(smem_u32(acce), NUM_EPI_WARPS);
-    mbar_init(smem_u32(sfa_full), 1);
-    mbar_init(smem_u32(sfa_ready), 1);
     mbar_init(smem_u32(drain_mma), 1);
-    mbar_init(smem_u32(drain_cp), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmA)) : "memory");
@@ -264,145 +240,139 @@ __global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(cons
   const int total_mtiles = s_tp[E];
   const int k_chunks = p.k_chunks;
   const int k_stages = (k_chunks + KPS - 1) / KPS;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      long fills = 0;
-      int groups = 0;
-      bool ok = true;
-      for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x, ++groups) {
-        const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
-        // the A scales of the whole K of this m-tile, once; the smem copy is free once the copy thread's
-        // tcgen05.cp of the previous m-tile's scales completed
-        if (groups > 0 &&
-            !wait_bounded(smem_u32(sfa_ready), (uint32_t)((groups - 1) & 1), abort_flag, p.status, p.timeout_ns))
-          break;
-        mbar_expect_tx(smem_u32(sfa_full), (uint32_t)(k_chunks * 512));
-        bulk_load(smem_u32(sfa_smem), p.sfA + (size_t)M.sfblk * k_chunks * 512, (uint32_t)(k_chunks * 512),
-                  smem_u32(sfa_full));
-        for (int nt = 0; nt < n_tiles && ok; ++nt) {
-          const int brow = M.e * p.N + nt * BN;
-          const uint8_t* sfb = p.sfB + ((size_t)M.e * n_tiles + nt) * k_chunks * SFB_REC;
-          for (int ks = 0; ks < k_stages; ++ks) {
-            const int kc0 = ks * KPS;
-            const int nk = min(KPS, k_chunks - kc0);
-            if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
-              ok = false;
-              break;
+  // the n-tile's second 128-row block of B exists unless it is the narrow last tile
+  auto has_block1 = [&](int nt) { return nt < n_tiles - 1 || p.tail_n == BN; };
+  if (warp < EPI_WARP0) {
+    // warpgroups 0 and 1: producer, MMA issuer, scale writers (two idle warps); their registers go to the epilogue
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CONTROL));
+    if (warp == 0) {
+      // ------------------------------------------------------------------ TMA producer
+      if (lane == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        long fills = 0;
+        bool ok = true;
+        for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
+          const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
+          const uint8_t* sfa = p.sfA + (size_t)M.sfblk * k_chunks * SF_ATOM;
+          for (int nt = 0; nt < n_tiles && ok; ++nt) {
+            const int brow = M.e * p.N + nt * BN;
+            const bool b1 = has_block1(nt);
+            const uint8_t* sfb0 = p.sfB + ((size_t)M.e * p.n_blocks + 2 * nt) * k_chunks * SF_ATOM;
+            const uint8_t* sfb1 = sfb0 + (size_t)k_chunks * SF_ATOM;
+            for (int ks = 0; ks < k_stages; ++ks) {
+              const int kc0 = ks * KPS;
+              const int nk = min(KPS, k_chunks - kc0);
+              if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
+                ok = false;
+                break;
+              }
+              uint8_t* st = smem + stage * STAGE_BYTES;
+              const uint32_t bar = smem_u32(&full[stage]);
+              const uint32_t sf_bytes = (uint32_t)(nk * SF_ATOM);
+              mbar_expect_tx(bar, (uint32_t)(A_BYTES + B_BYTES) + sf_bytes * (b1 ? 3u : 2u));
+              tma_load_2d(smem_u32(st), &p.tmA, bar, kc0 * (KSTEP / 2), M.row0);
+              tma_load_2d(smem_u32(st + A_BYTES), &p.tmB, bar, kc0 * (KSTEP / 2), brow);
+              uint8_t* sf_st = st + A_BYTES + B_BYTES;
+              bulk_load(smem_u32(sf_st), sfa + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
+              bulk_load(smem_u32(sf_st + SFA_BYTES), sfb0 + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
+              if (b1) bulk_load(smem_u32(sf_st + SFA_BYTES + KPS * SF_ATOM), sfb1 + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
+              ++fills;
+              if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
-            uint8_t* st = smem + stage * STAGE_BYTES;
-            const uint32_t bar = smem_u32(&full[stage]);
-            mbar_expect_tx(bar, (uint32_t)(A_BYTES + B_BYTES + nk * SFB_REC));
-            tma_load_2d(smem_u32(st), &p.tmA, bar, kc0 * (KSTEP / 2), M.row0);
-            tma_load_2d(smem_u32(st + A_BYTES), &p.tmB, bar, kc0 * (KSTEP / 2), brow);
-            bulk_load(smem_u32(st + A_BYTES + B_BYTES), sfb + (size_t)kc0 * SFB_REC, (uint32_t)(nk * SFB_REC), bar);
-            ++fills;
-            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
           }
         }
+        // let the last fills land before the CTA may exit (only matters after an abort)
+        for (long f = fills - 1; f >= 0 && f >= fills - STAGES; --f)
+          wait_drain(smem_u32(&full[f % STAGES]), (uint32_t)((f / STAGES) & 1));
       }
-      // let the last fills land before the CTA may exit (only matters after an abort)
-      for (long f = fills - 1; f >= 0 && f >= fills - STAGES; --f)
-        wait_drain(smem_u32(&full[f % STAGES]), (uint32_t)((f / STAGES) & 1));
-      if (groups > 0) wait_drain(smem_u32(sfa_full), (uint32_t)((groups - 1) & 1));
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer (one thread)
-    if (lane == 0) {
-      long n = 0;  // global stage counter of this CTA
-      uint32_t acc_phase = 0;
-      int groups = 0;
-      bool ok = true;
-      for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x, ++groups) {
-        if (!wait_bounded(smem_u32(sfa_ready), (uint32_t)(groups & 1), abort_flag, p.status, p.timeout_ns)) break;
-        tc_fence_after();
-        for (int nt = 0; nt < n_tiles && ok; ++nt) {
-          const uint32_t idesc = idesc_for(nt == n_tiles - 1 ? p.tail_n : BN);
-          if (!wait_bounded(smem_u32(acce), acc_phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          for (int ks = 0; ks < k_stages; ++ks, ++n) {
-            const int stage = (int)(n % STAGES);
-            const int b = (int)(n & 1);
-            const int nk = min(KPS, k_chunks - ks * KPS);
-            // the B scales of this stage are in TMEM buffer b (the copy thread waited for the stage's TMA data
-            // before copying them, so the A/B tiles of the stage have landed as well)
-            if (!wait_bounded(smem_u32(&sff[b]), (uint32_t)((n >> 1) & 1), abort_flag, p.status, p.timeout_ns)) {
+    } else if (warp == 1) {
+      // ------------------------------------------------------------------ MMA issuer (one thread)
+      if (lane == 0) {
+        long n = 0;  // global stage counter of this CTA
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
+          for (int nt = 0; nt < n_tiles && ok; ++nt) {
+            const uint32_t idesc = idesc_for(nt == n_tiles - 1 ? p.tail_n : BN);
+            if (!wait_bounded(smem_u32(acce), acc_phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t a_s = smem_u32(smem + stage * STAGE_BYTES);
-            const uint32_t b_s = a_s + A_BYTES;
-            for (int kk = 0; kk < nk; ++kk) {
-              const int kc = ks * KPS + kk;
-              tc_mma_fp4(tmem, desc_sw128(a_s + kk * (KSTEP / 2)), desc_sw128(b_s + kk * (KSTEP / 2)), idesc,
-                         tmem + SFA_COL + 4 * kc, tmem + SFB_COL + SFB_BUF_COLS * b + 8 * kk,
-                         (ks | kk) != 0 ? 1u : 0u);
+            for (int ks = 0; ks < k_stages; ++ks, ++n) {
+              const int stage = (int)(n % STAGES);
+              const int nk = min(KPS, k_chunks - ks * KPS);
+              // the stage's scales are in TMEM (the writers waited for the stage's TMA data first, so the A/B tiles
+              // have landed as well)
+              if (!wait_bounded(smem_u32(&sff[stage]), (uint32_t)((n / STAGES) & 1), abort_flag, p.status,
+                                p.timeout_ns)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t a_s = smem_u32(smem + stage * STAGE_BYTES);
+              const uint32_t b_s = a_s + A_BYTES;
+              for (int kk = 0; kk < nk; ++kk)
+                tc_mma_fp4(tmem, desc_sw128(a_s + kk * (KSTEP / 2)), desc_sw128(b_s + kk * (KSTEP / 2)), idesc,
+                           tmem + SFA_COL + 4 * (KPS * stage + kk), tmem + SFB_COL + 8 * (KPS * stage + kk),
+                           (ks | kk) != 0 ? 1u : 0u);
+              tc_commit(smem_u32(&empty[stage]));
             }
-            tc_commit(smem_u32(&empty[stage]));
+            if (!ok) break;
+            tc_commit(smem_u32(accf));
+            acc_phase ^= 1u;
           }
-          if (!ok) break;
-          tc_commit(smem_u32(accf));
-          acc_phase ^= 1u;
         }
+        // all tcgen05 work of this thread has completed once this commit arrives
+        tc_commit(smem_u32(drain_mma));
+        wait_drain(smem_u32(drain_mma), 0);
       }
-      // all tcgen05 work of this thread has completed once this commit arrives
-      tc_commit(smem_u32(drain_mma));
-      wait_drain(smem_u32(drain_mma), 0);
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------------ scale-factor copies (one thread)
-    if (lane == 0) {
+    } else if (warp >= SCALE_WARP0 && warp < EPI_WARP0) {
+      // ------------------------------------------------------------------ scale writers (one warp per lane quarter)
+      // A stage's TMEM scale columns are free once its previous MMAs completed; the producer waited for that (the
+      // stage's empty barrier) before refilling the stage, so the stage's full barrier implies it.
+      const uint32_t tq = tmem + ((uint32_t)((warp & 3) * 32) << 16);
       long n = 0;
-      int groups = 0;
       bool ok = true;
-      for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x, ++groups) {
-        if (!wait_bounded(smem_u32(sfa_full), (uint32_t)(groups & 1), abort_flag, p.status, p.timeout_ns)) break;
-        // the previous m-tile's MMAs must be done reading the resident A scales before they are replaced
-        if (n > 0 && !wait_bounded(smem_u32(&empty[(n - 1) % STAGES]), (uint32_t)(((n - 1) / STAGES) & 1), abort_flag,
-                                   p.status, p.timeout_ns))
-          break;
-        tc_fence_after();
-        const uint32_t sfa_s = smem_u32(sfa_smem);
-        for (int kc = 0; kc < k_chunks; ++kc) tc_cp_sf(tmem + SFA_COL + 4 * kc, desc_sf(sfa_s + kc * 512));
-        tc_commit(smem_u32(sfa_ready));
+      const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+      for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
         for (int nt = 0; nt < n_tiles && ok; ++nt) {
+          const bool b1 = has_block1(nt);
           for (int ks = 0; ks < k_stages; ++ks, ++n) {
             const int stage = (int)(n % STAGES);
-            const int b = (int)(n & 1);
             const int nk = min(KPS, k_chunks - ks * KPS);
-            if (!wait_bounded(smem_u32(&full[stage]), (uint32_t)((n / STAGES) & 1), abort_flag, p.status,
-                              p.timeout_ns)) {
-              ok = false;
-              break;
-            }
-            // B-scale buffer b was last read by the MMAs of stage n - 2
-            if (n >= 2 && !wait_bounded(smem_u32(&empty[(n - 2) % STAGES]), (uint32_t)(((n - 2) / STAGES) & 1),
-                                        abort_flag, p.status, p.timeout_ns)) {
+            // one lane waits, the warp follows its verdict (the stores below are warp-collective)
+            bool landed = lane == 0 ? wait_bounded(smem_u32(&full[stage]), (uint32_t)((n / STAGES) & 1), abort_flag,
+                                                   p.status, p.timeout_ns)
+                                    : false;
+            landed = __shfl_sync(0xffffffffu, landed ? 1 : 0, 0) != 0;
+            if (!landed) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t sfb_s = smem_u32(smem + stage * STAGE_BYTES + A_BYTES + B_BYTES);
-            for (int kk = 0; kk < nk; ++kk)
-              tc_cp_sfb_x(tmem + SFB_COL + SFB_BUF_COLS * b + 8 * kk, desc_sfb_x(sfb_s + kk * SFB_REC));
-            tc_commit(smem_u32(&sff[b]));
+            const uint8_t* sf_st = smem + stage * STAGE_BYTES + A_BYTES + B_BYTES + lane * 16;
+            for (int kk = 0; kk < nk; ++kk) {
+              const uint4 a = *reinterpret_cast<const uint4*>(sf_st + kk * SF_ATOM);
+              const uint4 b0 = *reinterpret_cast<const uint4*>(sf_st + SFA_BYTES + kk * SF_ATOM);
+              const uint4 bb = b1 ? *reinterpret_cast<const uint4*>(sf_st + SFA_BYTES + (KPS + kk) * SF_ATOM) : zero;
+              tc_st_32x32b_x4(tq + SFA_COL + 4 * (KPS * stage + kk), a);
+              tc_st_32x32b_x8(tq + SFB_COL + 8 * (KPS * stage + kk), b0, bb);
+            }
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&sff[stage]));
           }
         }
       }
-      tc_commit(smem_u32(drain_cp));
-      wait_drain(smem_u32(drain_cp), 0);
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPILOGUE));
     // ------------------------------------------------------------------ epilogue warps
     const int q = warp & 3;                       // TMEM lane quarter this warp may access
-    const int sub = (warp - EPI_WARP0) >> 2;      // which half (w13) / quarter (w2) of the tile's columns
+    const int sub = (warp - EPI_WARP0) >> 2;      // which half of the tile's columns
     const int r = q * 32 + lane;                  // row inside the tile
     uint32_t acc_phase = 0;
     bool ok = true;
@@ -427,15 +397,19 @@ __global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(cons
         acc_phase ^= 1u;
         tc_fence_after();
         const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16);
-        // full tiles: this warp's 64 output columns (mode 0) or 64 gate + 64 up columns (mode 1);
-        // the narrow last tile: 32 columns (mode 0) or 32 gate + 32 up (mode 1)
+        // full tiles: this warp's 128 output columns (mode 0) or 64 gate + 64 up columns (mode 1);
+        // the narrow last tile: 64 columns (mode 0) or 32 gate + 32 up (mode 1)
         const int half = un / 2;
         uint32_t x[4][32];
         if constexpr (MODE == 0) {
-          // 16 warps: this warp's quarter = 64 columns (32 in the narrow last tile)
-          const int cw = un / 4;
+          // this warp's half = 128 columns (64 in the narrow last tile)
+          const int cw = un / 2;
           tc_ld_32x32b_x32(t_base + sub * cw, x[0]);
-          if (un == BN) tc_ld_32x32b_x32(t_base + sub * cw + 32, x[1]);
+          tc_ld_32x32b_x32(t_base + sub * cw + 32, x[1]);
+          if (un == BN) {
+            tc_ld_32x32b_x32(t_base + sub * cw + 64, x[2]);
+            tc_ld_32x32b_x32(t_base + sub * cw + 96, x[3]);
+          }
         } else {
           const int hw = un / 4;                  // h columns per warp half
           tc_ld_32x32b_x32(t_base + sub * hw, x[0]);             // gate
@@ -453,12 +427,12 @@ __global__ void __launch_bounds__(threads_for(MODE), 1) grouped_gemm_kernel(cons
         const float alpha = p.alphas[M.e];
         if constexpr (MODE == 0) {
           // 32 columns per x[j] -> 64 bytes of bf16 -> two full 32-byte sectors per 256-bit store
-          const int col0 = nt * BN + sub * (un / 4);
+          const int col0 = nt * BN + sub * (un / 2);
           uint8_t* dst = direct != 0ull ? reinterpret_cast<uint8_t*>(direct) + (size_t)col0 * 2
                                         : reinterpret_cast<uint8_t*>(p.out + row * p.N + col0);
-          const int nq = un == BN ? 2 : 1;
+          const int nq = un == BN ? 4 : 2;
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
+          for (int j = 0; j < 4; ++j) {
             if (j < nq) {
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
@@ -524,7 +498,7 @@ static int launch_t(const Params& prm, int grid, cudaStream_t s) {
   auto kfn = grouped_gemm_kernel<MODE, ACT>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
     return REAXMOE_ERR_CUDA;
-  kfn<<<grid, threads_for(MODE), SMEM_BYTES, s>>>(prm);
+  kfn<<<grid, THREADS, SMEM_BYTES, s>>>(prm);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
 }
 
@@ -562,7 +536,7 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   prm.n_tiles = (g.N + BN - 1) / BN;
   prm.tail_n = g.N - (prm.n_tiles - 1) * BN;   // 256 or 128
   prm.k_chunks = g.K / KSTEP;
-  if (prm.k_chunks > MAX_K_CHUNKS) return REAXMOE_ERR_BAD_SHAPE;  // resident A scales would not fit in TMEM
+  prm.n_blocks = g.N / 128;
   const int64_t max_mtiles = g.slots / BM + g.E + 1;
   const int grid = (int)(max_mtiles < num_sms ? max_mtiles : num_sms);
   if (g.mode == 0) return launch_t<0, 0>(prm, grid, s);

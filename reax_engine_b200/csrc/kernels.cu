@@ -584,35 +584,6 @@ int launch_prepack_w13(const uint8_t* w, const uint8_t* sf, int E, int inter, in
   return 0;
 }
 
-// ------------------------------------------------------------------------------------------------------
-// Weight-scale expansion for the grouped GEMMs (one-time, at weight load). For every expert e, 256-row n-tile nt
-// and 64-element k-chunk kc, a 4 KiB record holds the scales of both 128-row blocks of the tile in the layout one
-// tcgen05.cp.128x256b copies into TMEM as the B scales of one N=256 MMA: 16 groups of 8 rows; per group the
-// 8 x 16 B rows of block 0 then the 8 x 16 B rows of block 1, row i of group g being row (8g + i) % 32 of the
-// block's 512-byte 128x4 atom. A 128-row last tile has zeros for block 1.
-// ------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) expand_scales_kernel(const uint8_t* __restrict__ sf, int N, int k_chunks,
-                                                            int n_tiles, uint8_t* __restrict__ out) {
-  const int e = blockIdx.z, nt = blockIdx.y, kc = blockIdx.x;
-  const int64_t rec = ((int64_t)e * n_tiles + nt) * k_chunks + kc;
-  uint4* dst = reinterpret_cast<uint4*>(out + rec * 4096);
-  const int nblk = N / 128;
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {   // 256 rows of 16 bytes
-    const int g = i >> 4, h = (i >> 3) & 1, r = i & 7;
-    const int row = (8 * g + r) & 31;
-    const int blk = 2 * nt + h;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (blk < nblk) v = *reinterpret_cast<const uint4*>(sf + (((int64_t)e * nblk + blk) * k_chunks + kc) * 512 + row * 16);
-    dst[i] = v;
-  }
-}
-
-int launch_expand_scales(const uint8_t* sf, int E, int N, int K, uint8_t* out, cudaStream_t s) {
-  const int k_chunks = K / 64, n_tiles = (N + 255) / 256;
-  expand_scales_kernel<<<dim3(k_chunks, n_tiles, E), 256, 0, s>>>(sf, N, k_chunks, n_tiles, out);
-  return 0;
-}
-
 int launch_count(const int* ids, int m, int k, int E, int* seg_counts, int* status, cudaStream_t s) {
   const int nseg = (int)ceil_div64(m, kSegTokens);
   if (nseg > 0) count_kernel<<<nseg, 256, 0, s>>>(ids, m, k, E, seg_counts, status);

@@ -24,7 +24,6 @@ int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, in
                    __nv_bfloat16* out, int num_sms, cudaStream_t s);
 int launch_quantize(const void* x, bool f32, int64_t rows, int cols, int group_rows, const float* gscale,
                     uint8_t* packed, uint8_t* scales, cudaStream_t s);
-int launch_expand_scales(const uint8_t* sf, int E, int N, int K, uint8_t* out, cudaStream_t s);
 int launch_prepack_w13(const uint8_t* w, const uint8_t* sf, int E, int inter, int H, uint8_t* wp, uint8_t* sfp,
                        cudaStream_t s);
 
@@ -89,7 +88,7 @@ struct GemmLaunch {
   int64_t slots;
   const void* a_sf;  // atoms over blockscale rows
   const void* b;     // [E, N, K/2]
-  const void* b_sf;  // expanded: [E][ceil(N/256)][K/64][4096] (reaxmoe_expand_scales)
+  const void* b_sf;  // weight scale atoms as engine/fp4.py lays them out: [E][N/128][K/64][512]
   const float* alphas;
   int E, N, K;
   const int* counts; const int* eoff; const int* boff; const int* tile_prefix;

@@ -99,6 +99,20 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[3
 
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 4 / 8 columns of 32-bit from registers: thread i of the warp writes lane (quarter*32 + i), register j to
+// column col + j.
+__device__ __forceinline__ void tc_st_32x32b_x4(uint32_t taddr, const uint4& v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void tc_st_32x32b_x8(uint32_t taddr, const uint4& a, const uint4& b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Shared-memory matrix descriptor (sm_100 format, version 1 at bits [46,48)): start >> 4 at [0,14),
 // leading byte offset >> 4 at [16,30), stride byte offset >> 4 at [32,46), layout at [61,64).
 // A/B tiles: K-major, 128-byte swizzle, 8-row core-matrix groups 1024 bytes apart (SBO), LBO unused (1).

@@ -73,7 +73,7 @@ class LayerWeights:
     router_scale: torch.Tensor   # [hidden] bf16
     router_w: torch.Tensor       # [experts, hidden] bf16
     per_expert_scale: torch.Tensor   # [experts] fp32
-    w1p: torch.Tensor            # NVFP4 experts, prepacked (prepack_w13 / expand_scales)
+    w1p: torch.Tensor            # NVFP4 experts, w13 prepacked (prepack_w13)
     w1p_sf: torch.Tensor
     w1_fp4: torch.Tensor         # engine/fp4 layout as quantised (kept for the oracle)
     w1_sf: torch.Tensor
@@ -181,7 +181,7 @@ class DecisionModel:
                           * (c.router_std if c.router_std is not None else c.init_std)).to(bf),
                 per_expert_scale=torch.ones(c.experts, dtype=torch.float32, device=self.dev),
                 w1p=w1p, w1p_sf=w1p_sf, w1_fp4=w1q, w1_sf=w1s, w1_g=w1g, w2_fp4=w2q, w2_sf=w2s,
-                w2_sfx=M.expand_scales(w2s, c.hidden, c.moe_inter), w2_g=w2g))
+                w2_sfx=w2s, w2_g=w2g))
         self.max_positions = 0
         self._rope_cache = {}
         self.moe_stream = torch.cuda.Stream(self.dev)

@@ -52,8 +52,8 @@ def record_bytes(hidden: int, topk: int) -> int:
 @dataclass
 class LocalExperts:
     """This rank's expert weights in the grouped GEMMs' formats, all [El, ...] slices of the global tensors:
-    w1 interleaved by :func:`reax_engine_b200.prepack_w13` with its expanded scales, w2 with scales expanded by
-    :func:`reax_engine_b200.expand_scales`, and the per-expert alphas and intermediate scales."""
+    w1 interleaved by :func:`reax_engine_b200.prepack_w13` with its scale atoms, w2 and its scale atoms as they
+    are (engine/fp4.py layout), and the per-expert alphas and intermediate scales."""
     w1_fp4: torch.Tensor
     w1_sf: torch.Tensor
     w1_alphas: torch.Tensor

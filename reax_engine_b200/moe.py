@@ -145,26 +145,11 @@ _prepack_cache: dict = {}
 _prepack_lock = threading.Lock()
 
 
-def expand_scales(w_blockscale: torch.Tensor, n: int, k: int) -> torch.Tensor:
-    """Weight block scales ([E, n, k/16] e4m3 in 128x4 atoms per expert) -> the grouped GEMMs' B-scale records
-    [E, ceil(n/256), k/64, 4096] uint8 (reaxmoe_expand_scales). One-time, at weight load."""
-    _require_cuda(w_blockscale)
-    E = w_blockscale.shape[0]
-    src = w_blockscale.view(torch.uint8).reshape(E, -1).contiguous()
-    assert src.shape[1] == n * k // 16, "scale tensor does not match n x k/16 per expert"
-    nbytes = L.lib().reaxmoe_expanded_scales_size(E, n, k)
-    if nbytes == 0:
-        raise L.ReaxMoEError(L.ERR_BAD_SHAPE, f"expand_scales: n={n} k={k}")
-    out = torch.empty(nbytes, dtype=torch.uint8, device=w_blockscale.device)
-    L.check(L.lib().reaxmoe_expand_scales(src.data_ptr(), E, n, k, out.data_ptr(), _stream(w_blockscale.device)))
-    return out.view(E, -1)
-
-
 def prepack_w13(w1_fp4: torch.Tensor, w1_blockscale: torch.Tensor, inter: int) -> tuple[torch.Tensor, torch.Tensor]:
     """Re-lay w13 for the fused gate/up epilogue (row block b of 256 = gate rows [128b, 128b+128) then the matching
-    up rows; a narrower last block when inter % 128 != 0) and expand its scales for the GEMM
-    (:func:`expand_scales`). One-time, at weight load (the analogue of ``process_weights_after_loading``).
-    Returns (interleaved fp4 [E, 2*inter, hidden/2], expanded scales)."""
+    up rows; a narrower last block when inter % 128 != 0), its scale atoms moving with their rows. One-time, at
+    weight load (the analogue of ``process_weights_after_loading``). Returns (interleaved fp4 [E, 2*inter,
+    hidden/2], interleaved scale atoms [E, 2*inter*hidden/16])."""
     _require_cuda(w1_fp4, w1_blockscale)
     E, N, K2 = w1_fp4.shape
     assert N == 2 * inter
@@ -173,7 +158,7 @@ def prepack_w13(w1_fp4: torch.Tensor, w1_blockscale: torch.Tensor, inter: int) -
     sfp = torch.empty_like(src_sf)
     L.check(L.lib().reaxmoe_prepack_w13(w1_fp4.view(torch.uint8).contiguous().data_ptr(), src_sf.data_ptr(), E, inter,
                                         K2 * 2, w1p.data_ptr(), sfp.data_ptr(), _stream(w1_fp4.device)))
-    return w1p, expand_scales(sfp, N, K2 * 2)
+    return w1p, sfp
 
 
 def _cached(kind, tensors, fn):
@@ -246,9 +231,9 @@ def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor
     rows, or the interleaved layout when ``w1_prepacked``); w1_blockscale [e, 2n, k/16] e4m3 in 128x4 atoms per
     expert; w2_fp4 [e, k, n/2]; w2_blockscale [e, k, n/16]; w*_alphas [e]; topk_weights / topk_ids [m, topk].
     ``workspace13`` / ``workspace2`` are accepted for signature compatibility; the library's workspace comes from
-    ``workspace`` (uint8, >= :func:`workspace_size` bytes) or a cached per-device buffer. Weights are re-laid for the
-    GEMMs once per weight tensor and cached (:func:`prepack_w13`, :func:`expand_scales`); pass already prepacked
-    tensors with ``w1_prepacked`` / ``w2_prepacked``.
+    ``workspace`` (uint8, >= :func:`workspace_size` bytes) or a cached per-device buffer. w13 is re-laid for the
+    fused epilogue once per weight tensor and cached (:func:`prepack_w13`); pass an already prepacked w13 with
+    ``w1_prepacked``. w2 is read as it is (``w2_prepacked`` is accepted and has no effect).
     """
     act = MoEActivation.parse(activation)
     pre = a if isinstance(a, NVFP4Rows) else None
@@ -289,10 +274,7 @@ def run_moe_nvfp4(output: torch.Tensor, a: torch.Tensor, a1_gscale: torch.Tensor
         w1p, w1p_sf = w1_fp4.contiguous(), w1_blockscale.view(torch.uint8).reshape(e, -1).contiguous()
     else:
         w1p, w1p_sf = _cached("w13", (w1_fp4, w1_blockscale), lambda: prepack_w13(w1_fp4, w1_blockscale, n))
-    if w2_prepacked:
-        w2_sf = w2_blockscale.view(torch.uint8).reshape(e, -1).contiguous()
-    else:
-        w2_sf = _cached("w2", (w2_blockscale,), lambda: expand_scales(w2_blockscale, k, n))
+    w2_sf = w2_blockscale.view(torch.uint8).reshape(e, -1).contiguous()
     ids = topk_ids.to(torch.int32).contiguous()
     tw = topk_weights.float().contiguous()
     a1 = a1_gscale.float().reshape(-1).contiguous()

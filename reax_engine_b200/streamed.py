@@ -22,8 +22,7 @@ class HostStreamedMoE:
     """NVFP4 MoE layer (Gemma-4 routing + experts + combine) over pinned host tensors.
 
     Weights and scales are device tensors in the formats of :func:`reax_engine_b200.run_moe_nvfp4` with
-    ``w1_prepacked=True`` (w1 interleaved by :func:`reax_engine_b200.prepack_w13`; w2 scales expanded by
-    :func:`reax_engine_b200.expand_scales`). ``chunk_tokens`` trades pipeline fill / drain against GEMM size; 4096
+    ``w1_prepacked=True`` (w1 interleaved by :func:`reax_engine_b200.prepack_w13`; w2 as it is). ``chunk_tokens`` trades pipeline fill / drain against GEMM size; 4096
     tokens measured best on a B200 at config 2 (2048: 4.7M, 4096: 6.5M, 8192: 6.0M tokens/s).
     """
 

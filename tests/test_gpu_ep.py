@@ -94,7 +94,7 @@ def _local(R, c, r, ranks):
     sl = slice(r * El, (r + 1) * El)
     w1p, w1p_sf = R.prepack_w13(c["w1q"][sl].contiguous(), c["w1s"][sl].contiguous(), c["inter"])
     return R.ep.LocalExperts(w1p, w1p_sf, c["w1_alphas"][sl].contiguous(), c["a2_gscale"][sl].contiguous(),
-                             c["w2q"][sl].contiguous(), R.expand_scales(c["w2s"][sl].contiguous(), c["H"], c["inter"]),
+                             c["w2q"][sl].contiguous(), c["w2s"][sl].contiguous(),
                              c["w2_alphas"][sl].contiguous())
 
 
@@ -179,7 +179,7 @@ def test_ep_emulated_ranks_bit_exact_vs_single_gpu(R, ranks, Ts):
     st.plan(ids)
     st.permute_quant(c["x"], c["a1_gscale"])
     st.gemm_w13(w1p, w1p_sf, c["w1_alphas"], c["a2_gscale"])
-    st.gemm_w2(c["w2q"], R.expand_scales(c["w2s"], H, inter), c["w2_alphas"])
+    st.gemm_w2(c["w2q"], c["w2s"], c["w2_alphas"])
     single = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     st.combine(w, single)
     torch.cuda.synchronize()

@@ -40,7 +40,7 @@ def _worker(rank, world, port, Ts, errq):
         st.plan(ids)
         st.permute_quant(c["x"], c["a1_gscale"])
         st.gemm_w13(w1p, w1p_sf, c["w1_alphas"], c["a2_gscale"])
-        st.gemm_w2(c["w2q"], R.expand_scales(c["w2s"], H, inter), c["w2_alphas"])
+        st.gemm_w2(c["w2q"], c["w2s"], c["w2_alphas"])
         single = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         st.combine(w, single)
         torch.cuda.synchronize(dev)

@@ -36,7 +36,7 @@ def _single_gpu(R, c, w, ids, T, H, E, k, inter, dev="cuda"):
     st.plan(ids)
     st.permute_quant(c["x"], c["a1_gscale"])
     st.gemm_w13(w1p, w1p_sf, c["w1_alphas"], c["a2_gscale"])
-    st.gemm_w2(c["w2q"], R.expand_scales(c["w2s"], H, inter), c["w2_alphas"])
+    st.gemm_w2(c["w2q"], c["w2s"], c["w2_alphas"])
     single = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     st.combine(w, single)
     torch.cuda.synchronize(dev)
@@ -98,8 +98,9 @@ def test_p2p_emulated_ranks_bit_exact(R, ranks, Ts):
 def test_p2p_direct_rows_keep_signed_zeros(R):
     """Records with one local pair get their returned row from the w2 epilogue (direct rows), the others from the
     pre-sum kernel. Both must equal the single-GPU combine of the record's local pairs bit for bit, signed zeros
-    included: with zero token rows (c3 rows of zeros) and negative router weights, a record's row is -0 exactly when
-    every term of its combine is -0, i.e. every weight of the token is negative. Compared as bits (-0 != +0)."""
+    included. With zero token rows (c3 rows of zeros) and negative router weights every product is -0; the combine
+    adds exactly +0 for the pairs on other ranks, so such a record's row is +0 (and -0 only for a record that holds
+    all of its token's pairs). Compared as bits (-0 != +0)."""
     ranks, Ts = 8, [96] * 8
     T, H, E, k, inter = sum(Ts), 2816, 128, 8, 704
     El = E // ranks
@@ -117,7 +118,7 @@ def test_p2p_direct_rows_keep_signed_zeros(R):
     idn, wn = ids.cpu().numpy(), w.cpu().numpy()
     owner = idn // El
     starts = np.concatenate([[0], np.cumsum(Ts)]).astype(int)
-    singles = neg = 0
+    singles = zero_neg = 0
     for s in range(ranks):
         toks = np.arange(starts[s], starts[s + 1])
         expect = []
@@ -125,12 +126,14 @@ def test_p2p_direct_rows_keep_signed_zeros(R):
             mine = toks[(owner[toks] == d).any(1)]
             cm = np.where(owner[mine] == d, cmap[mine], -1)
             expect.append(O.combine(c3, cm.reshape(-1), wn[mine]))
-            singles += int(((owner[mine] == d).sum(1) == 1).sum())
+            one = (owner[mine] == d).sum(1) == 1
+            singles += int(one.sum())
+            neg_w = ((owner[mine] == d) & (wn[mine] < 0)).any(1)
+            zero_neg += int((one & neg_w & (mine % 2 == 0)).sum())     # zero row, negative weight: -0 product
         expect = np.concatenate(expect)
         got = rows_back[s].view(torch.int16).cpu().numpy().view(np.uint16)
         assert np.array_equal(got, O.bf16_bits(expect)), f"source {s}: returned rows differ"
-        neg += int((got == 0x8000).all(1).sum())
-    assert singles > 100 and neg > 0            # the direct-row path and -0 rows were both exercised
+    assert singles > 100 and zero_neg > 50      # the direct-row path saw -0 products
 
 
 def _ipc_block(R):

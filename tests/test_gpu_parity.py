@@ -111,15 +111,7 @@ def test_prepack_w13_matches_oracle(R):
     qp, sp = R.prepack_w13(q, s, inter)
     rq, rs = O.interleave_w13(q.cpu().numpy(), s.cpu().numpy(), inter)
     assert np.array_equal(qp.cpu().numpy(), rq)
-    assert np.array_equal(sp.cpu().numpy().reshape(-1), O.expand_b_scales(rs, 2 * inter, H).reshape(-1))
-
-
-@pytest.mark.parametrize("E,N,K", [(2, 384, 256), (3, 2816, 704), (1, 1408, 2816)])
-def test_expand_scales_matches_oracle(R, E, N, K):
-    g = torch.Generator().manual_seed(N + K)
-    sf = torch.randint(0, 255, (E, N * K // 16), generator=g, dtype=torch.uint8)
-    out = R.expand_scales(sf.cuda(), N, K)
-    assert np.array_equal(out.cpu().numpy().reshape(-1), O.expand_b_scales(sf.numpy(), N, K).reshape(-1))
+    assert np.array_equal(sp.cpu().numpy().reshape(-1), rs.reshape(-1))
 
 
 # ------------------------------------------------------------------------------------------------ plan / permute
@@ -196,7 +188,7 @@ def test_gemm_w2_matches_oracle(R, shape):
     c3_ref = O.grouped_gemm(packed, sf, n["w2q"], n["w2s"], n["w2_alphas"], pl)
     st = R.Stages(T, H, inter, E, k, "gelu_tanh", "cuda")
     st.plan(torch.from_numpy(idr).cuda())
-    st.gemm_w2(c["w2q"], R.expand_scales(c["w2s"], H, inter), c["w2_alphas"], int_fp4=torch.from_numpy(packed).cuda(),
+    st.gemm_w2(c["w2q"], c["w2s"], c["w2_alphas"], int_fp4=torch.from_numpy(packed).cuda(),
                int_sf=torch.from_numpy(sf).cuda())
     _sync()
     assert st.status() == 0

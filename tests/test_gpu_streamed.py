@@ -16,7 +16,7 @@ def test_host_streamed_equals_single_call(T, chunk):
     H, E, k, inter = 2816, 128, 8, 704
     c = make_case(T, H, E, k, inter, "gelu_tanh", seed=T)
     w1p, w1p_sf = R.prepack_w13(c["w1q"], c["w1s"], inter)
-    w2x = R.expand_scales(c["w2s"], H, inter)
+    w2x = c["w2s"]
     w, ids = R.route(None, c["logits"], k)
     ref = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     R.run_moe_nvfp4(ref, c["x"], c["a1_gscale"], w1p, w1p_sf, c["w1_alphas"], c["a2_gscale"], c["w2q"], w2x,
@@ -40,6 +40,6 @@ def test_host_streamed_refuses_pageable_memory():
     c = make_case(16, H, E, k, inter, "silu", seed=1)
     w1p, w1p_sf = R.prepack_w13(c["w1q"], c["w1s"], inter)
     layer = R.HostStreamedMoE(H, inter, E, k, "silu", c["a1_gscale"], w1p, w1p_sf, c["w1_alphas"], c["a2_gscale"],
-                              c["w2q"], R.expand_scales(c["w2s"], H, inter), c["w2_alphas"], "cuda")
+                              c["w2q"], c["w2s"], c["w2_alphas"], "cuda")
     with pytest.raises(AssertionError):
         layer(c["x"].cpu(), c["logits"].cpu(), torch.empty(16, H, dtype=torch.bfloat16))
