@@ -425,8 +425,8 @@ int reaxmoe_plan(const reaxmoe_problem* p, const int32_t* topk_ids, void* worksp
   if (rc) return rc;
   Layout L;
   if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
-  if (p->tokens == 0) return 0;
-  if (topk_ids == nullptr) return fail(REAXMOE_ERR_NULL, "plan: topk_ids is NULL");
+  // zero tokens still write the outputs: offsets of 0 and problem sizes (0, n, k)
+  if (p->tokens > 0 && topk_ids == nullptr) return fail(REAXMOE_ERR_NULL, "plan: topk_ids is NULL");
   const WS w = carve(workspace, L);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = do_plan(p, topk_ids, w, problem_sizes1, problem_sizes2, s))) return rc;
