@@ -302,10 +302,10 @@ int reaxmoe_ep_dispatch_pack(const reaxmoe_problem* p, int32_t ranks, const void
 /* reaxmoe_ep_expert_forward with the pre-summed row of received record i stored at
  * rows[s] + (i - bounds[s]) * hidden * 2 for the source s with bounds[s] <= i < bounds[s + 1] (host arrays:
  * bounds [ranks + 1] from 0 to local->tokens, non-decreasing; rows [ranks] device addresses, 32-byte aligned:
- * the row in rank s's return buffer of the first record s sent here). A record with exactly one local pair has its
- * row stored by the w2 GEMM's epilogue, the others by the pre-sum kernel; the rows are bit-identical either way,
- * signed zeros included, for router weights of any sign. Environment REAXMOE_EP_DIRECT_ROWS=0 (read once per
- * process) sends every record through the pre-sum kernel. */
+ * the row in rank s's return buffer of the first record s sent here). Every record's row is stored by the pre-sum
+ * kernel. With environment REAXMOE_EP_DIRECT_ROWS=1 (read once per process) a record with
+ * exactly one local pair gets its row from the w2 GEMM's epilogue instead; the rows are bit-identical either way,
+ * signed zeros included, for router weights of any sign. */
 int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
                                  const void* w1_sf, const float* w1_alphas, const float* a2_gscale,
                                  const void* w2_fp4, const void* w2_sf, const float* w2_alphas, void* workspace,

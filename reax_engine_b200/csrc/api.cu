@@ -202,12 +202,14 @@ static size_t ep_expert_total(const reaxmoe_problem* p, const Layout& L) {
   return up256(ep_expert_direct_w(p, L) + (size_t)p->tokens * p->topk * 4);
 }
 
-// REAXMOE_EP_DIRECT_ROWS=0 turns off the w2-epilogue direct rows of the peer transport (every record's row then comes
-// from the pre-sum kernel); the rows are bit-identical either way. Read once per process.
+// REAXMOE_EP_DIRECT_ROWS=1 turns on the w2-epilogue direct rows of the peer transport: a record with one local pair
+// gets its row stored to its source rank by the w2 epilogue instead of the pre-sum kernel (bit-identical rows). Off
+// by default: on 2 B200s the epilogue's peer stores slowed the w2 GEMM more than the pre-sum pass they save (26.7M
+// against 30.1M tokens/s at 65,536 tokens per rank). Read once per process.
 static bool ep_direct_rows() {
   static const bool on = [] {
     const char* v = getenv("REAXMOE_EP_DIRECT_ROWS");
-    return !(v != nullptr && v[0] == '0');
+    return v != nullptr && v[0] == '1';
   }();
   return on;
 }
