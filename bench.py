@@ -69,8 +69,9 @@ def workload(name: str):
                     act="silu", skew=None, lens=lens)
     if name.startswith("cfg5_"):
         T = int(name.split("_")[1])
+        from moe_cases import zipf_c
         return dict(name=f"cfg5: skewed Zipf routing T={T}", T=T, H=2816, E=128, k=8, I=704, act="gelu_tanh",
-                    skew=2.0, lens=[T])
+                    skew=zipf_c(), lens=[T])
     if name == "cfg4":
         return dict(name="cfg4: expert-parallel layer, 65536 tokens/rank", T=65536, H=2816, E=128, k=8, I=704,
                     act="gelu_tanh", skew=None, lens=[65536])
@@ -323,6 +324,84 @@ def run_reference(args, wl: dict) -> None:
     print(json.dumps(line), flush=True)
 
 
+EXTRA_WORKLOADS = ("cfg1", "cfg5_16", "cfg5_1024", "cfg5_131072")
+
+
+def measure_workload(name: str, dev, steps: int, warmup: int) -> dict:
+    """One of BASELINE's other single-GPU configs (cfg1, cfg5 at T = 16 / 1024 / 131072) through the same layer
+    steps as the headline: tokens/s with CUDA events over `steps` steps after `warmup`, per-kernel times, and the
+    roofline of the whole layer: the larger of its FP4 tensor time (6 k H I FLOP per token at the FP4 basis) and its
+    HBM time (the weights of the experts the routing touches, x and logits read once, the output written once)."""
+    import torch
+
+    import reax_engine_b200 as R
+    wl = workload(name)
+    inp = build_inputs(wl, dev)
+    T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
+    st = R.Stages(T, H, I, E, k, wl["act"], dev)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    s = torch.cuda.current_stream(dev)
+    names = ["route", "plan", "permute_quant", "gemm_w13", "gemm_w2", "combine"]
+
+    def step(ev=None):
+        w, ids = R.route(None, inp["logits"], k)
+        if ev is not None: ev[0].record(s)
+        st.plan(ids)
+        if ev is not None: ev[1].record(s)
+        st.permute_quant(inp["x"], inp["a1_gscale"])
+        if ev is not None: ev[2].record(s)
+        st.gemm_w13(inp["w1p"], inp["w1p_sf"], inp["w1_alphas"], inp["a2_gscale"])
+        if ev is not None: ev[3].record(s)
+        st.gemm_w2(inp["w2q"], inp["w2s"], inp["w2_alphas"])
+        if ev is not None: ev[4].record(s)
+        st.combine(w, out)
+        if ev is not None: ev[5].record(s)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if st.status() != 0:
+        raise SystemExit(f"{name}: device status {st.status()}")
+    _, ids = R.route(None, inp["logits"], k)
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    touched = int((counts > 0).sum())
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for i in range(steps):
+        step(evs[i])
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / steps
+    per = {n: statistics.mean((a if i == 0 else evs[i - 1][5]).elapsed_time(evs[i][0]) if j == 0 else
+                              evs[i][j - 1].elapsed_time(evs[i][j]) for i in range(steps)) for j, n in enumerate(names)}
+    peaks = load_peaks()
+    fp4_peak = 4.0 * peaks["bf16"]
+    flop = 6.0 * k * H * I * T
+    w_bytes = touched * 3 * H * I * (1 / 2 + 1 / 16)
+    hbm_bytes = w_bytes + T * H * 2 * 2 + T * E * 4
+    t_tensor = flop / (fp4_peak * 1e12)
+    t_hbm = hbm_bytes / (peaks["hbm_gbs"] * 1e9)
+    tensor_bound = t_tensor >= t_hbm
+    res = dict(workload=wl["name"], tokens=T, hidden=H, experts=E, topk=k, inter=I, activation=wl["act"],
+               value=T / (ms / 1000.0), unit="tokens/s", ms_per_step=ms, steps=steps, warmup=warmup,
+               kernels_ms=per, experts_touched=touched, hottest_over_mean=float(counts.max() / counts.float().mean()),
+               roofline=dict(bound="tensor" if tensor_bound else "hbm",
+                             achieved=(flop / (ms / 1000.0) / 1e12) if tensor_bound else
+                             (hbm_bytes / (ms / 1000.0) / 1e9),
+                             peak=fp4_peak if tensor_bound else peaks["hbm_gbs"],
+                             unit="TFLOP/s" if tensor_bound else "GB/s",
+                             frac=(t_tensor if tensor_bound else t_hbm) / (ms / 1000.0),
+                             algorithmic=dict(flop=flop, hbm_bytes=hbm_bytes),
+                             note="whole layer against the slower of FP4 tensor time and HBM time of the touched "
+                                  "experts' weights + x + logits + output"))
+    if wl["skew"] is not None:
+        res["zipf_c"] = wl["skew"]
+    del inp, st
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args, wl: dict) -> None:
     import torch
     import torch.distributed as dist
@@ -447,6 +526,10 @@ def run_ours(args, wl: dict) -> None:
 
     decision = decision_leg(args, dev, world, rank)
 
+    extra = None
+    if world == 1 and not args.no_extra:
+        extra = {n: measure_workload(n, dev, steps=args.steps, warmup=args.warmup) for n in EXTRA_WORKLOADS}
+
     # ---- roofline of the dominant kernel and per-kernel figures
     peaks = load_peaks()
     slots = T * k
@@ -493,7 +576,7 @@ def run_ours(args, wl: dict) -> None:
                     api=f"reax_engine_b200.HostStreamedMoE: pinned host x + logits in, output out, {E2E_CHUNK}-token "
                         "chunks with the copies overlapped with route + run_moe_nvfp4"),
                 gpu_launches=launches_per_step * args.steps, roofline=roof, layer=layer, kernels=kernels,
-                router_topk=router, decision=decision,
+                router_topk=router, decision=decision, other_configs=extra,
                 cpu_baseline=cpu, clocks=clk.summary())
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -769,6 +852,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--no-router", action="store_true", help="skip the fused router measurement (profiling runs)")
     ap.add_argument("--no-decision", action="store_true", help="skip the config-3 decision forward (profiling runs)")
+    ap.add_argument("--no-extra", action="store_true", help="skip the cfg1 / cfg5 measurements (profiling runs)")
     ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count (profiling)")
     ap.add_argument("--ep-chunks", type=int, default=None, help="expert-parallel token parts in flight (N > 1)")
     ap.add_argument("--ep-transport", choices=["nccl", "p2p"], default=None,

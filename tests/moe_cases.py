@@ -4,6 +4,9 @@ drawn N(0, 0.02) on the device and quantised there by the library (whose quantis
 against the oracle in test_gpu_parity.py::test_quantize_*), and the oracle receives the same bytes."""
 from __future__ import annotations
 
+import json
+import os
+
 import numpy as np
 import torch
 
@@ -20,6 +23,37 @@ def zipf_bias(E: int, c: float, seed: int, s: float = 1.2) -> torch.Tensor:
     g = torch.Generator().manual_seed(seed)
     r = (torch.randperm(E, generator=g) + 1).float()
     return -c * s * torch.log(r)
+
+
+ZIPF_FIXTURE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "zipf_skew.json")
+
+
+def route_load_ratio(c: float, T: int = 131072, E: int = 128, k: int = 8, seed: int = 5) -> tuple[float, int]:
+    """Top-k load of the skewed router (logits N(0,1) + zipf_bias(c)): (hottest expert's count / mean count, number of
+    experts with no pair)."""
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn(T, E, generator=g) + zipf_bias(E, c, 0)[None]
+    cnt = torch.bincount(torch.topk(logits, k, dim=1).indices.flatten(), minlength=E).float()
+    return float(cnt.max() / cnt.mean()), int((cnt == 0).sum())
+
+
+def calibrate_zipf_c(target: float = 10.0, T: int = 131072, E: int = 128, k: int = 8) -> float:
+    """The skewed-routing config's bias constant c, found by bisection so that the hottest expert gets `target` x the
+    mean load at T tokens (the ratio grows with c and saturates at E / k when every token picks that expert)."""
+    lo, hi = 0.0, 2.0
+    for _ in range(30):
+        mid = 0.5 * (lo + hi)
+        if route_load_ratio(mid, T, E, k)[0] < target:
+            lo = mid
+        else:
+            hi = mid
+    return 0.5 * (lo + hi)
+
+
+def zipf_c() -> float:
+    """The calibrated constant (tests/golden/zipf_skew.json, written by calibrate_zipf_c)."""
+    with open(ZIPF_FIXTURE) as f:
+        return float(json.load(f)["c"])
 
 
 def make_case(T: int, H: int, E: int, k: int, inter: int, act: str, seed: int = 0, skew: float | None = None,
