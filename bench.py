@@ -39,6 +39,8 @@ DECISION_PROMPTS, DECISION_WARMUP, DECISION_STEPS = 64, 2, 3   # config 3 decisi
 EP_SM_RESERVE = 0   # SMs the persistent kernels leave to the NCCL exchanges in expert-parallel runs
 EP_E2E_CHUNKS = 4   # token parts per rank in the expert-parallel end-to-end pipeline (HostStreamedEP)
 EP_PARITY_TOKENS = 1024   # tokens per rank checked against the single-GPU layer after the timed expert-parallel steps
+EP_OVERLAP_PARTS = 1   # p2p: received records in this many parts, part c's row stores beside part c+1's GEMMs
+EP_PRESUM_SMS = 16     # p2p: SMs the overlapped row stores are pinned to
 EP_TRANSPORT = "p2p"    # expert-parallel exchange: "nccl" (two all-to-alls) or "p2p" (the kernels' own NVLink stores)
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
@@ -626,8 +628,10 @@ def run_ours_ep(args, wl: dict) -> None:
     for key in ("w1q", "w1s"):
         inp.pop(key)
     torch.cuda.empty_cache()
+    overlap = args.ep_overlap_parts if args.ep_overlap_parts is not None else EP_OVERLAP_PARTS
+    presum_sms = args.ep_presum_sms if args.ep_presum_sms is not None else EP_PRESUM_SMS
     layer = R.ep.ExpertParallelMoE(H, I, E, k, wl["act"], inp["a1_gscale"], local_w,
-                                   transport=transport,
+                                   transport=transport, overlap_parts=overlap, presum_sms=presum_sms,
                                    **({} if args.ep_chunks is None else {"chunks": args.ep_chunks}))
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     s = torch.cuda.current_stream(dev)
@@ -732,7 +736,8 @@ def run_ours_ep(args, wl: dict) -> None:
                 data="synthetic",
                 config=dict(workload=wl["name"], tokens_per_rank=T, hidden=H, experts=E, topk=k, inter=I,
                             activation=wl["act"], parallelism=f"ep{world}", experts_per_rank=El, ep_chunks=layer.chunks,
-                            ep_sm_reserve=sm_reserve, ep_transport=transport,
+                            ep_sm_reserve=sm_reserve, ep_transport=transport, ep_overlap_parts=overlap,
+                            ep_presum_sms=presum_sms, ep_direct_rows=os.environ.get("REAXMOE_EP_DIRECT_ROWS", "0") == "1",
                             l2="inputs larger than L2 (x %.0f MB per rank, local weights %.0f MB); no flush" % (
                                 T * H * 2 / 1e6, weight_bytes / 1e6)),
                 e2e=None if e2e_value is None else dict(
@@ -857,6 +862,9 @@ def main():
     ap.add_argument("--ep-chunks", type=int, default=None, help="expert-parallel token parts in flight (N > 1)")
     ap.add_argument("--ep-transport", choices=["nccl", "p2p"], default=None,
                     help="expert-parallel exchange (N > 1): NCCL all-to-alls or the kernels' NVLink peer stores")
+    ap.add_argument("--ep-overlap-parts", type=int, default=None,
+                    help="p2p (N > 1): received records in this many parts, row stores overlapped with GEMMs")
+    ap.add_argument("--ep-presum-sms", type=int, default=None, help="p2p (N > 1): SMs the overlapped row stores use")
     ap.add_argument("--ep-sm-reserve", type=int, default=None,
                     help="SMs the library's persistent kernels leave free for the exchanges (N > 1)")
     args = ap.parse_args()

@@ -312,6 +312,20 @@ int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_
                                  size_t workspace_bytes, int32_t ranks, const int64_t* bounds, const uint64_t* rows,
                                  void* stream);
 
+/* reaxmoe_ep_expert_forward_to in two calls, so that the row stores of one part of the received records can run
+ * beside the GEMMs of the next part (no counterpart in the reference). ep_expert_gemms: unpack, plan, permute and
+ * the two grouped GEMMs of `local` (the part's records), with c3 left in `workspace`
+ * (reaxmoe_ep_expert_workspace_size(local) bytes, one workspace per part in flight); its persistent GEMMs use at
+ * most sm_limit SMs (0 = all). ep_presum_to: then, on any stream ordered after it, the pre-summed row of each of the
+ * part's records stored as reaxmoe_ep_expert_forward_to stores it (bounds / rows relative to the part), by one
+ * 1024-thread block per SM on `sms` SMs (0 = the plain launch on every SM). */
+int reaxmoe_ep_expert_gemms(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
+                            const void* w1_sf, const float* w1_alphas, const float* a2_gscale, const void* w2_fp4,
+                            const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes,
+                            int32_t sm_limit, void* stream);
+int reaxmoe_ep_presum_to(const reaxmoe_problem* local, const void* workspace, size_t workspace_bytes, int32_t ranks,
+                         const int64_t* bounds, const uint64_t* rows, int32_t sms, void* stream);
+
 /* Synchronises `stream`, returns the device status word of the workspace (0 = ok, else REAXMOE_ERR_*) and
  * clears it when `clear` != 0. Not for the hot path. */
 int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream);

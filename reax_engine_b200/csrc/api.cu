@@ -801,6 +801,87 @@ int reaxmoe_ep_expert_forward_to(const reaxmoe_problem* local, const void* recv_
                            "ep_expert_forward_to");
 }
 
+// ---- the receiver in two calls, so that the row stores of one part of the received records run beside the GEMMs of
+// the next part (on another stream, pinned to a few SMs)
+int reaxmoe_ep_expert_gemms(const reaxmoe_problem* local, const void* recv_records, const void* w1_fp4,
+                            const void* w1_sf, const float* w1_alphas, const float* a2_gscale, const void* w2_fp4,
+                            const void* w2_sf, const float* w2_alphas, void* workspace, size_t workspace_bytes,
+                            int32_t sm_limit, void* stream) {
+  const reaxmoe_problem* p = local;
+  int rc = check_problem(p, true);
+  if (rc) return rc;
+  const Layout L = layout(p);
+  const size_t need = ep_expert_total(p, L);
+  if (workspace == nullptr) return fail(REAXMOE_ERR_WORKSPACE, "ep_expert_gemms: workspace is NULL");
+  if (!aligned16(workspace)) return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_gemms: workspace not 16-byte aligned");
+  if (workspace_bytes < need)
+    return fail(REAXMOE_ERR_WORKSPACE, "ep_expert_gemms: workspace %zu bytes < required %zu", workspace_bytes, need);
+  if (sm_limit < 0) return fail(REAXMOE_ERR_BAD_SHAPE, "ep_expert_gemms: sm_limit=%d", sm_limit);
+  if (p->tokens == 0) return 0;
+  if (!recv_records || !w1_fp4 || !w1_sf || !w1_alphas || !a2_gscale || !w2_fp4 || !w2_sf || !w2_alphas)
+    return fail(REAXMOE_ERR_NULL, "ep_expert_gemms: NULL pointer");
+  if (!aligned16(recv_records) || !aligned16(w1_fp4) || !aligned16(w1_sf) || !aligned16(w2_fp4) || !aligned16(w2_sf))
+    return fail(REAXMOE_ERR_MISALIGNED, "ep_expert_gemms: records and weights must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const WS w = carve(workspace, L);
+  uint8_t* b = static_cast<uint8_t*>(workspace);
+  int* lid = reinterpret_cast<int*>(b + ep_expert_lid(L));
+  float* lw = reinterpret_cast<float*>(b + ep_expert_lw(p, L));
+  const uint8_t* rec = static_cast<const uint8_t*>(recv_records);
+  const int rec_bytes = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
+  launch_ep_unpack_meta(rec, p->tokens, p->topk, p->hidden, rec_bytes, lid, lw, s);
+  if ((rc = do_plan(p, lid, w, nullptr, nullptr, s))) return rc;
+  launch_ep_permute(rec, lid, w.seg_base, w.eoff, p->tokens, p->hidden, p->experts, p->topk, rec_bytes, w.rep_fp4,
+                    w.lin_sf, w.c_map, s);
+  launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
+                        (int64_t)p->tokens * p->topk, w.rep_sf, s);
+  if ((rc = cuda_check("ep_expert_gemms permute"))) return rc;
+  const int sms = sm_limit > 0 && sm_limit < num_sms() ? sm_limit : num_sms();
+  GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4, w.int_sf);
+  if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "ep_expert_gemms: gemm_w13 launch failed");
+  GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, w2_fp4, w2_sf, w2_alphas, w.c3);
+  if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "ep_expert_gemms: gemm_w2 launch failed");
+  return cuda_check("ep_expert_gemms");
+}
+
+int reaxmoe_ep_presum_to(const reaxmoe_problem* local, const void* workspace, size_t workspace_bytes, int32_t ranks,
+                         const int64_t* bounds, const uint64_t* rows, int32_t sms, void* stream) {
+  int rc = check_problem(local, true);
+  if (rc) return rc;
+  const Layout L = layout(local);
+  if (workspace == nullptr || workspace_bytes < ep_expert_total(local, L))
+    return fail(REAXMOE_ERR_WORKSPACE, "ep_presum_to: workspace missing or smaller than the gemms call's");
+  if (ranks < 1 || ranks > kMaxRanks) return fail(REAXMOE_ERR_BAD_SHAPE, "ep_presum_to: ranks=%d", ranks);
+  if (bounds == nullptr || rows == nullptr) return fail(REAXMOE_ERR_NULL, "ep_presum_to: NULL pointer");
+  if (bounds[0] != 0 || bounds[ranks] != local->tokens)
+    return fail(REAXMOE_ERR_BAD_SHAPE, "ep_presum_to: bounds must run from 0 to tokens=%d", local->tokens);
+  if (sms < 0) return fail(REAXMOE_ERR_BAD_SHAPE, "ep_presum_to: sms=%d", sms);
+  RowRoute route{};
+  route.ranks = ranks;
+  route.skip_single = 0;
+  for (int q = 0; q <= ranks; ++q) {
+    if (q > 0 && bounds[q] < bounds[q - 1])
+      return fail(REAXMOE_ERR_BAD_SHAPE, "ep_presum_to: bounds decrease at %d", q);
+    route.bound[q] = bounds[q];
+  }
+  for (int q = 0; q < ranks; ++q) {
+    if (bounds[q + 1] > bounds[q] && (rows[q] == 0 || rows[q] % 32 != 0))
+      return fail(REAXMOE_ERR_MISALIGNED, "ep_presum_to: rows[%d] is NULL or not 32-byte aligned", q);
+    route.p[q] = rows[q];
+  }
+  if (local->tokens == 0) return 0;
+  const WS w = carve(const_cast<void*>(workspace), L);
+  const float* lw = reinterpret_cast<const float*>(static_cast<const uint8_t*>(workspace) + ep_expert_lw(local, L));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (sms > 0)
+    rc = launch_combine_routed_pinned(w.c3, w.c_map, lw, local->tokens, local->hidden, local->topk, route,
+                                      sms < num_sms() ? sms : num_sms(), s);
+  else
+    rc = launch_combine_routed(w.c3, w.c_map, lw, local->tokens, local->hidden, local->topk, route, num_sms(), s);
+  if (rc) return fail(REAXMOE_ERR_CUDA, "ep_presum_to: launch failed");
+  return cuda_check("ep_presum_to");
+}
+
 int reaxmoe_ep_combine(int32_t tokens, int32_t hidden, int32_t topk, const int32_t* send_map, const void* returned,
                        void* output, void* stream) {
   if (tokens < 0 || hidden < 128 || hidden % 128 != 0 || topk < 1 || topk > kMaxTopk)

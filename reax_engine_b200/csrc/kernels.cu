@@ -416,11 +416,11 @@ struct RoutedRows {
   __device__ __forceinline__ bool skip(int valid_pairs) const { return r.skip_single && valid_pairs == 1; }
 };
 
-template <int K, class Rows>
-__global__ void __launch_bounds__(256, 3) combine_kernel_k(const __nv_bfloat16* __restrict__ c3,
-                                                           const int* __restrict__ c_map,
-                                                           const float* __restrict__ topk_w, int m, int H,
-                                                           const __grid_constant__ Rows out) {
+template <int K, class Rows, int THREADS = 256, int MIN_BLOCKS = 3>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) combine_kernel_k(const __nv_bfloat16* __restrict__ c3,
+                                                                        const int* __restrict__ c_map,
+                                                                        const float* __restrict__ topk_w, int m,
+                                                                        int H, const __grid_constant__ Rows out) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int nch = H / 8;
@@ -634,6 +634,31 @@ int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, in
   const int64_t blocks = want < cap ? want : cap;
   launch_combine_rows(c3, c_map, w, m, H, k, PlainRows{out}, (unsigned)blocks, s);
   return 0;
+}
+
+// The routed pre-sum on exactly `sms` SMs, beside a persistent kernel that holds the others: one 1024-thread block per
+// SM, made to own its SM by a 64 KiB shared-memory reservation (with it no grouped-GEMM CTA fits on the same SM, and
+// no second block of this kernel). K = 8 / 4 / 2 / 1 only.
+int launch_combine_routed_pinned(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
+                                 const RowRoute& route, int sms, cudaStream_t s) {
+  if (m == 0) return 0;
+  constexpr int kReserve = 64 * 1024;
+  const RoutedRows out{route};
+  const int64_t want = ceil_div64(m, 32);
+  const unsigned blocks = (unsigned)(want < sms ? want : sms);
+#define REAXMOE_PINNED(KK)                                                                                          \
+  {                                                                                                                 \
+    auto fn = combine_kernel_k<KK, RoutedRows, 1024, 1>;                                                            \
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kReserve) != cudaSuccess) return 1;   \
+    fn<<<blocks, 1024, kReserve, s>>>(c3, c_map, w, m, H, out);                                                     \
+    return 0;                                                                                                       \
+  }
+  if (k == 8) REAXMOE_PINNED(8)
+  if (k == 4) REAXMOE_PINNED(4)
+  if (k == 2) REAXMOE_PINNED(2)
+  if (k == 1) REAXMOE_PINNED(1)
+#undef REAXMOE_PINNED
+  return launch_combine_routed(c3, c_map, w, m, H, k, route, sms, s);
 }
 
 int launch_combine_routed(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,

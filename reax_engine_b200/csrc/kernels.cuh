@@ -72,6 +72,8 @@ int launch_ep_pack_peer(const __nv_bfloat16* a, const float* a1_gscale, const in
                         const PeerPtrs& records, int* send_map, cudaStream_t s);
 int launch_combine_routed(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
                           const RowRoute& route, int num_sms, cudaStream_t s);
+int launch_combine_routed_pinned(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
+                                 const RowRoute& route, int sms, cudaStream_t s);
 int launch_ep_signal(const PeerPtrs& blocks, int rank, int ranks, uint32_t epoch, const int* counts,
                      unsigned long long timeout_ns, cudaStream_t s);
 // Direct rows: for every received record with exactly one local pair, its slot's entry gets the record's return

@@ -178,6 +178,33 @@ class DeviceOps:
                                                      w.w2_alphas.data_ptr(), ws.data_ptr(), ws.numel(), self.R, b, r,
                                                      _stream(self.device)))
 
+    def expert_gemms(self, records_ptr: int, n: int, w: LocalExperts, slot: int, sm_limit: int = 0) -> None:
+        """The receiver's GEMMs over the n records at records_ptr (c3 kept in the workspace of `slot`)."""
+        p = L.problem(n, self.H, self.I, self.El, self.k, self.act)
+        need = L.lib().reaxmoe_ep_expert_workspace_size(ctypes.byref(p))
+        if need == 0:
+            raise L.ReaxMoEError(L.ERR_BAD_SHAPE, L.last_error())
+        ws = self.buf.get(f"expert_ws{slot}", need)
+        self._part = getattr(self, "_part", {})
+        self._part[slot] = (p, ws)
+        if n == 0:
+            return
+        L.check(L.lib().reaxmoe_ep_expert_gemms(ctypes.byref(p), records_ptr, w.w1_fp4.data_ptr(), w.w1_sf.data_ptr(),
+                                                w.w1_alphas.data_ptr(), w.a2_gscale.data_ptr(), w.w2_fp4.data_ptr(),
+                                                w.w2_sf.data_ptr(), w.w2_alphas.data_ptr(), ws.data_ptr(), ws.numel(),
+                                                sm_limit, _stream(self.device)))
+
+    def presum_to(self, slot: int, bounds: list[int], rows: list[int], sms: int = 0) -> None:
+        """The pre-summed rows of the records of `slot`'s last expert_gemms, stored along bounds / rows (relative to
+        that part), on the current stream."""
+        p, ws = self._part[slot]
+        if p.tokens == 0:
+            return
+        b = (ctypes.c_int64 * (self.R + 1))(*bounds)
+        r = (ctypes.c_uint64 * self.R)(*rows)
+        L.check(L.lib().reaxmoe_ep_presum_to(ctypes.byref(p), ws.data_ptr(), ws.numel(), self.R, b, r, sms,
+                                             _stream(self.device)))
+
     def signal(self, rank: int, blocks: list[int], epoch: int, counts: torch.Tensor | None,
                timeout_s: float) -> None:
         """``reaxmoe_ep_signal`` on the current stream (a barrier with the optional send-count payload)."""
@@ -331,6 +358,15 @@ class PeerExchange:
         self.recv = self.ret = None
 
 
+def part_routes(bounds: list[int], rows: list[int], r0: int, r1: int, row_bytes: int) -> tuple[list[int], list[int]]:
+    """The (bounds, rows) of the received records [r0, r1) (see :func:`p2p_addresses`) relative to that part: record i
+    of the part is record r0 + i of the whole, and its row goes where that record's row goes."""
+    R = len(rows)
+    pb = [min(max(bounds[s] - r0, 0), r1 - r0) for s in range(R + 1)]
+    pr = [rows[s] + row_bytes * max(r0 - bounds[s], 0) if pb[s + 1] > pb[s] else rows[s] for s in range(R)]
+    return pb, pr
+
+
 def _a2a_rows(out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int], group,
               async_op: bool = False):
     """all_to_all_single over rows of two 2-D tensors, moved as bytes (returns the work handle when async)."""
@@ -352,7 +388,7 @@ class ExpertParallelMoE:
 
     def __init__(self, hidden: int, inter: int, experts: int, topk: int, activation, a1_gscale: torch.Tensor,
                  local: LocalExperts, group=None, ops=None, chunks: int = 1, transport: str = "auto",
-                 timeout_s: float = 10.0):
+                 timeout_s: float = 10.0, overlap_parts: int = 1, presum_sms: int = 16):
         self.group = group
         self.R = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -374,6 +410,11 @@ class ExpertParallelMoE:
             raise ValueError(f"transport must be 'auto', 'nccl' or 'p2p', got {transport!r}")
         self.transport = transport
         self.peer = PeerExchange(self.ops, group, self.device, timeout_s) if transport == "p2p" else None
+        # p2p: the received records in this many parts; part c's row stores run on a side stream, pinned to
+        # presum_sms SMs, beside the GEMMs of part c + 1 on the other SMs
+        self.overlap_parts = max(1, int(overlap_parts))
+        self.presum_sms = int(presum_sms)
+        self._side = None
 
     def status(self) -> int:
         """Synchronise; the first non-zero device status of the last forward (kernels, and the peer signals' waits
@@ -472,7 +513,10 @@ class ExpertParallelMoE:
         send_map = self.ops.pack_to(a, self.a1_gscale, ids, tw, records)
         px.signal()
         self._mark("dispatch")
-        self.ops.expert_forward_to(px.recv.own, n_recv, self.local, bounds, rows)
+        if self.overlap_parts <= 1 or n_recv < 2 * self.overlap_parts:
+            self.ops.expert_forward_to(px.recv.own, n_recv, self.local, bounds, rows)
+        else:
+            self._experts_overlapped(px.recv.own, n_recv, bounds, rows, rec_bytes, row_bytes)
         px.signal()
         self._mark("experts")
         out = output if output is not None else torch.empty(T, self.H, dtype=torch.bfloat16, device=a.device)
@@ -480,5 +524,31 @@ class ExpertParallelMoE:
         self.ops.combine(send_map, ret, out)
         self._mark("combine")
         return out
+
+    def _experts_overlapped(self, recv_ptr: int, n_recv: int, bounds: list[int], rows: list[int], rec_bytes: int,
+                            row_bytes: int) -> None:
+        """The receiver in parts: part c's GEMMs on the current stream (at most all SMs but presum_sms), then its row
+        stores on a side stream pinned to presum_sms SMs, running while part c + 1's GEMMs run. The same rows as one
+        expert_forward_to over all records: each record's row depends only on the record."""
+        cur = torch.cuda.current_stream(self.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+            self._events = []
+        P = self.overlap_parts
+        while len(self._events) < P:
+            self._events.append(torch.cuda.Event())
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        gemm_sms = max(1, sms - self.presum_sms)
+        step = -(-n_recv // P)
+        self._side.wait_stream(cur)
+        for c in range(P):
+            r0, r1 = min(n_recv, c * step), min(n_recv, (c + 1) * step)
+            self.ops.expert_gemms(recv_ptr + r0 * rec_bytes, r1 - r0, self.local, slot=c, sm_limit=gemm_sms)
+            self._events[c].record(cur)
+            pb, pr = part_routes(bounds, rows, r0, r1, row_bytes)
+            with torch.cuda.stream(self._side):
+                self._side.wait_event(self._events[c])
+                self.ops.presum_to(c, pb, pr, sms=self.presum_sms)
+        cur.wait_stream(self._side)
 
     __call__ = forward

@@ -43,7 +43,7 @@ def _single_gpu(R, c, w, ids, T, H, E, k, inter, dev="cuda"):
     return st, single
 
 
-def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False):
+def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False, parts=1):
     """R ranks on one GPU over the peer-memory device halves: plan, pack into the destinations' receive buffers,
     expert forward into the sources' return buffers, combine."""
     from test_gpu_ep import _local
@@ -66,7 +66,16 @@ def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False):
                                    w[sl[s]].contiguous(), records))
     for d in range(ranks):
         _, bounds, rows, n_recv, _ = R.ep.p2p_addresses(C, d, rec, row, recv_ptrs, ret_ptrs)
-        ops[d].expert_forward_to(recv_ptrs[d], n_recv, _local(R, c, d, ranks), bounds, rows)
+        if parts == 1:
+            ops[d].expert_forward_to(recv_ptrs[d], n_recv, _local(R, c, d, ranks), bounds, rows)
+            continue
+        # the receiver in parts (reaxmoe_ep_expert_gemms + reaxmoe_ep_presum_to), the stores pinned to 8 SMs
+        step = -(-n_recv // parts)
+        for q in range(parts):
+            r0, r1 = min(n_recv, q * step), min(n_recv, (q + 1) * step)
+            ops[d].expert_gemms(recv_ptrs[d] + r0 * rec, r1 - r0, _local(R, c, d, ranks), slot=q, sm_limit=140)
+            pb, pr = R.ep.part_routes(bounds, rows, r0, r1, row)
+            ops[d].presum_to(q, pb, pr, sms=8)
     outs, rows_back = [], []
     for s in range(ranks):
         n_send = sum(C[s])
@@ -80,14 +89,15 @@ def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False):
     return (torch.cat(outs), rows_back) if return_rows else torch.cat(outs)
 
 
-@pytest.mark.parametrize("ranks,Ts", [(2, [700, 313]), (4, [256, 0, 511, 64]), (8, [100] * 8)])
-def test_p2p_emulated_ranks_bit_exact(R, ranks, Ts):
+@pytest.mark.parametrize("ranks,Ts,parts", [(2, [700, 313], 1), (4, [256, 0, 511, 64], 1), (8, [100] * 8, 1),
+                                           (2, [700, 313], 3), (8, [100] * 8, 2)])
+def test_p2p_emulated_ranks_bit_exact(R, ranks, Ts, parts):
     from test_gpu_ep import _emulate, _expected_from_single_gpu_c3
     T, H, E, k, inter = sum(Ts), 2816, 128, 8, 704
     c = make_case(T, H, E, k, inter, "gelu_tanh", seed=ranks)
     w, ids = R.route(None, c["logits"], k)
     st, single = _single_gpu(R, c, w, ids, T, H, E, k, inter)
-    got = _emulate_p2p(R, c, w, ids, Ts, ranks)
+    got = _emulate_p2p(R, c, w, ids, Ts, ranks, parts=parts)
     expect = _expected_from_single_gpu_c3(st.c3.float().cpu().numpy(), st.c_map.cpu().numpy(), w.cpu().numpy(),
                                           ids.cpu().numpy(), E // ranks, ranks)
     assert np.array_equal(got.float().cpu().numpy(), expect)
@@ -205,14 +215,18 @@ def _worker(rank, world, port, Ts, errq):
         nccl = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], loc, transport="nccl")
         p2p = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], loc, transport="p2p",
                                      timeout_s=20.0)
+        p2p3 = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], loc, transport="p2p",
+                                      timeout_s=20.0, overlap_parts=3, presum_sms=8)
         ref = nccl(c["x"][t0:t1], w[t0:t1], ids[t0:t1])
         t4 = t0 + max(1, Ts[rank] // 4)
         first = p2p(c["x"][t0:t4], w[t0:t4], ids[t0:t4])         # small buffers first, grown by the next call
         out = p2p(c["x"][t0:t1], w[t0:t1], ids[t0:t1])
         out2 = p2p(c["x"][t0:t1], w[t0:t1], ids[t0:t1])          # buffers reused
         big = p2p(c["x"], w, ids)                                  # every rank all T tokens: the buffers grow
+        parted = p2p3(c["x"][t0:t1], w[t0:t1], ids[t0:t1])        # the receiver in 3 parts, stores overlapped
         torch.cuda.synchronize(dev)
-        assert p2p.status() == 0 and nccl.status() == 0
+        assert p2p.status() == 0 and nccl.status() == 0 and p2p3.status() == 0
+        assert torch.equal(parted, out), f"rank {rank}: the overlapped receiver differs"
         got = out.float().cpu().numpy()
         assert np.array_equal(got, expect[t0:t1]), f"rank {rank}: p2p output differs from the recombined c3"
         assert torch.equal(out, ref) and torch.equal(out, out2)
@@ -220,6 +234,7 @@ def _worker(rank, world, port, Ts, errq):
         assert np.array_equal(big.float().cpu().numpy(), expect), f"rank {rank}: grown p2p output differs"
         tol_check(got, single[t0:t1].float().cpu().numpy())
         p2p.close()
+        p2p3.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # noqa: BLE001 - reported to the parent
