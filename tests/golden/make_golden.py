@@ -2,7 +2,7 @@
 
 Run in the build container only (it imports the read-only reference checkout and vLLM):
 
-    python tests/golden/make_golden.py [--reference /path/to/reax-engine]
+    python tests/golden/make_golden.py --reference /path/to/reax-engine    (or REAX_REFERENCE=...)
 
 What it runs, and what each fixture pins:
 
@@ -236,7 +236,8 @@ def router_cases(route_fn):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("REAX_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("REAX_REFERENCE"),
+                    help="the reference checkout (or set REAX_REFERENCE)")
     ap.add_argument("--only", choices=["router"], default=None, help="regenerate one fixture file")
     args = ap.parse_args()
     from vllm.model_executor.models.gemma4 import gemma4_routing_function_torch as route_fn
@@ -244,6 +245,8 @@ def main():
     np.savez_compressed(os.path.join(HERE, "router_golden.npz"), **router_cases(route_fn))
     if args.only == "router":
         return
+    if not args.reference:
+        ap.error("pass --reference /path/to/reax-engine or set REAX_REFERENCE")
     fp4 = load_fp4(args.reference)
     np.savez_compressed(os.path.join(HERE, "quant_golden.npz"), **quant_cases(fp4))
     np.savez_compressed(os.path.join(HERE, "e4m3_golden.npz"), **e4m3_cases())
