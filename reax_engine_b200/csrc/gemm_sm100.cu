@@ -8,8 +8,10 @@
 //   mode 1 (w13): gate/up = bf16(alpha_e * acc); h = bf16(bf16(act(gate)) * up); NVFP4 quant of h with the
 //                 expert's intermediate scale (engine/fp4.py numerics) -> FP4 rows + 128x4 scale atoms.
 //
-// Design (one CTA per SM, persistent). Work is handed out per m-tile (expert, 128 routed rows); a CTA computes all
-// n-tiles of its m-tile in a row (256 output columns each; a narrower last n-tile of 128 when N % 256 == 128).
+// Design (one CTA per SM, persistent). Work is handed out round-robin over the CTAs: one m-tile (expert, 128 routed
+// rows) with all its n-tiles (256 output columns each; a narrower last n-tile of 128 when N % 256 == 128) per item;
+// for a small batch (fewer than two m-tiles per CTA) one (m-tile, n-tile) unit per item instead, so that every SM
+// takes part in reading the weights (measured at 1024 skewed tokens: 0.378 -> 0.215 ms per layer).
 //   warp 0      TMA producer, into a 4-deep ring of 54 KiB stages: A (routed FP4 rows, 128 x 256 K) and B (expert
 //               weights, 256 x 256 K) by 2D TMA with 128-byte swizzle, plus the stage's scale atoms as they lie in
 //               memory (engine/fp4.py 128x4 atoms, 512 B per 128 rows x 64-element k-chunk) by 1D bulk copies: the
@@ -238,6 +240,11 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
   const uint32_t tmem = *tmem_holder;
   const int n_tiles = p.n_tiles;
   const int total_mtiles = s_tp[E];
+  // Work items: with at least two m-tiles per CTA, one m-tile with all its n-tiles (the CTA's B reads stay on one
+  // expert); with fewer (a small batch), one (m-tile, n-tile) unit, so that every SM takes part in the weight reads.
+  const bool by_unit = total_mtiles < 2 * (int)gridDim.x;
+  const int items = by_unit ? total_mtiles * n_tiles : total_mtiles;
+  const int per_item = by_unit ? 1 : n_tiles;
   const int k_chunks = p.k_chunks;
   const int k_stages = (k_chunks + KPS - 1) / KPS;
   // the n-tile's second 128-row block of B exists unless it is the narrow last tile
@@ -252,10 +259,11 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         uint32_t phase = 0;
         long fills = 0;
         bool ok = true;
-        for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
+        for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
+          const int gm = by_unit ? u / n_tiles : u;
           const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
           const uint8_t* sfa = p.sfA + (size_t)M.sfblk * k_chunks * SF_ATOM;
-          for (int nt = 0; nt < n_tiles && ok; ++nt) {
+          for (int nt = by_unit ? u % n_tiles : 0, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
             const int brow = M.e * p.N + nt * BN;
             const bool b1 = has_block1(nt);
             const uint8_t* sfb0 = p.sfB + ((size_t)M.e * p.n_blocks + 2 * nt) * k_chunks * SF_ATOM;
@@ -292,8 +300,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         long n = 0;  // global stage counter of this CTA
         uint32_t acc_phase = 0;
         bool ok = true;
-        for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
-          for (int nt = 0; nt < n_tiles && ok; ++nt) {
+        for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
+          for (int nt = by_unit ? u % n_tiles : 0, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
             const uint32_t idesc = idesc_for(nt == n_tiles - 1 ? p.tail_n : BN);
             if (!wait_bounded(smem_u32(acce), acc_phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
               ok = false;
@@ -336,8 +344,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
       long n = 0;
       bool ok = true;
       const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-      for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
-        for (int nt = 0; nt < n_tiles && ok; ++nt) {
+      for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
+        for (int nt = by_unit ? u % n_tiles : 0, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
           const bool b1 = has_block1(nt);
           for (int ks = 0; ks < k_stages; ++ks, ++n) {
             const int stage = (int)(n % STAGES);
@@ -376,7 +384,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     const int r = q * 32 + lane;                  // row inside the tile
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int gm = blockIdx.x; gm < total_mtiles && ok; gm += gridDim.x) {
+    for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
+      const int gm = by_unit ? u / n_tiles : u;
       const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
       const int64_t row = (int64_t)M.row0 + r;
       // expert-parallel receiver: a slot that is its record's only local pair is written as the finished row
@@ -388,7 +397,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
           wdir = bf16r(p.direct_w[row]);
         }
       }
-      for (int nt = 0; nt < n_tiles; ++nt) {
+      for (int nt = by_unit ? u % n_tiles : 0, nt_end = nt + per_item; nt < nt_end; ++nt) {
         const int un = (nt == n_tiles - 1) ? p.tail_n : BN;
         if (!wait_bounded(smem_u32(accf), acc_phase, abort_flag, p.status, p.timeout_ns)) {
           ok = false;
@@ -537,8 +546,8 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   prm.tail_n = g.N - (prm.n_tiles - 1) * BN;   // 256 or 128
   prm.k_chunks = g.K / KSTEP;
   prm.n_blocks = g.N / 128;
-  const int64_t max_mtiles = g.slots / BM + g.E + 1;
-  const int grid = (int)(max_mtiles < num_sms ? max_mtiles : num_sms);
+  const int64_t max_units = (g.slots / BM + g.E + 1) * prm.n_tiles;
+  const int grid = (int)(max_units < num_sms ? max_units : num_sms);
   if (g.mode == 0) return launch_t<0, 0>(prm, grid, s);
   if (g.act == REAXMOE_ACT_GELU_TANH) return launch_t<1, REAXMOE_ACT_GELU_TANH>(prm, grid, s);
   return launch_t<1, REAXMOE_ACT_SILU>(prm, grid, s);

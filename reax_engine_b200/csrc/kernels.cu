@@ -181,9 +181,10 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
 }
 
 // ------------------------------------------------------------------------------------------------------
-// K3 permute_quant: one CTA per segment.
+// K3 permute_quant: `parts` CTAs per segment (parts > 1 only when segments are fewer than two per SM).
 //  Phase A (warp 0, segment_slots): canonical slot of every (token, j) pair of the segment, token-major inside
-//  an expert, starting from run[e] = expert_offsets[e] + seg_base[seg][e].
+//  an expert, starting from run[e] = expert_offsets[e] + seg_base[seg][e]. Every CTA of the segment computes it
+//  (a scan of the segment's ids); part 0 writes c_map.
 //  Phase B (all warps): each token row is NVFP4-quantised once per distinct expert input scale and written
 //  to its k slots (FP4 bytes + the two scale bytes of each 32-element unit), the same bytes as vLLM's per-slot
 //  quant of the shuffled rows (blink_moe.py:301-323, cutlass_moe.py:585-593).
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
 __global__ void __launch_bounds__(256, 3) permute_quant_kernel(
     const __nv_bfloat16* __restrict__ a, const float* __restrict__ a1_gscale, const int* __restrict__ ids,
     const int* __restrict__ seg_base, const int* __restrict__ eoff, const int* __restrict__ boff, int m, int H,
-    int E, int k, uint8_t* __restrict__ rep_fp4, uint8_t* __restrict__ lin_sf, int* __restrict__ c_map) {
+    int E, int k, uint8_t* __restrict__ rep_fp4, uint8_t* __restrict__ lin_sf, int* __restrict__ c_map, int parts) {
   __shared__ int run[kMaxExperts];
   __shared__ uint32_t mask[kMaxExperts];
   __shared__ float gq[kMaxExperts];
@@ -199,7 +200,8 @@ __global__ void __launch_bounds__(256, 3) permute_quant_kernel(
   __shared__ short exp_s[kSegTokens * kMaxTopk];
   __shared__ int sl_pos[8][kMaxTopk];           // per warp: the current token's slots
   __shared__ float sl_g[8][kMaxTopk];
-  const int seg = blockIdx.x;
+  const int seg = blockIdx.x / parts;
+  const int part = blockIdx.x - seg * parts;
   const int64_t t0 = (int64_t)seg * kSegTokens;
   const int nt = (int)(kSegTokens < m - t0 ? (int64_t)kSegTokens : m - t0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -209,9 +211,9 @@ __global__ void __launch_bounds__(256, 3) permute_quant_kernel(
     gq[e] = __fdiv_rn(1.0f, a1_gscale[e]);
   }
   __syncthreads();
-  if (warp == 0) segment_slots(ids, t0, nt, k, E, run, mask, pos_s, exp_s, c_map);
+  if (warp == 0) segment_slots(ids, t0, nt, k, E, run, mask, pos_s, exp_s, part == 0 ? c_map : nullptr);
   __syncthreads();
-  // phase B: one warp per token. Lanes j < k put slot j and its input scale into the warp's shared slot table; lanes
+  // phase B: one warp per token (the segment's tokens strided over its parts' warps). Lanes j < k put slot j and its input scale into the warp's shared slot table; lanes
   // own 32-element units (16 FP4 bytes + 2 scale bytes per slot). A unit is quantised once per distinct input scale
   // among the slots (once for a uniform scale) with the bf16x2 quantiser, then stored to every slot: FP4 bytes into
   // the slot's row, scale bytes into the slot's row of the linear scale buffer (full-sector stores; the atoms are
@@ -219,7 +221,7 @@ __global__ void __launch_bounds__(256, 3) permute_quant_kernel(
   const int units = H / 32;
   const int k16 = H / 16;
   const int nwarps = blockDim.x >> 5;
-  for (int tl = warp; tl < nt; tl += nwarps) {
+  for (int tl = warp + part * nwarps; tl < nt; tl += nwarps * parts) {
     const int64_t t = t0 + tl;
     const uint4* src = reinterpret_cast<const uint4*>(a + t * H);
     uint4 raw[kPermUnits][4];
@@ -601,9 +603,15 @@ int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const i
                          const int* eoff, const int* boff, int m, int H, int E, int k, uint8_t* rep_fp4,
                          uint8_t* lin_sf, int* c_map, cudaStream_t s) {
   const int nseg = (int)ceil_div64(m, kSegTokens);
+  // segments fewer than two per SM (small batches): split each segment's tokens over more CTAs
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int parts = nseg >= 2 * sms ? 1 : (int)ceil_div64(2 * sms, nseg);
+  parts = parts < 1 ? 1 : parts > 16 ? 16 : parts;
   if (nseg > 0)
-    permute_quant_kernel<<<nseg, 256, 0, s>>>(a, a1_gscale, ids, seg_base, eoff, boff, m, H, E, k, rep_fp4, lin_sf,
-                                              c_map);
+    permute_quant_kernel<<<nseg * parts, 256, 0, s>>>(a, a1_gscale, ids, seg_base, eoff, boff, m, H, E, k, rep_fp4,
+                                                      lin_sf, c_map, parts);
   return 0;
 }
 
