@@ -44,8 +44,10 @@ def rope(x: torch.Tensor, pos: torch.Tensor, theta: float) -> torch.Tensor:
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
 
 
-def attention(q, k, v, cu, window: int | None) -> torch.Tensor:
-    """q [n, Hq, D], k / v [n, Hk, D] bf16 -> [n, Hq, D] bf16; causal per sequence, optional window."""
+def attention(q, k, v, cu, window: int | None, pv_bf16: bool = False) -> torch.Tensor:
+    """q [n, Hq, D], k / v [n, Hk, D] bf16 -> [n, Hq, D] bf16; causal per sequence, optional window. pv_bf16: round the
+    softmax probabilities to bf16 before P.V (what a flash-attention kernel feeding bf16 P to its tensor cores does),
+    instead of the fp32 P of this restatement -- a second, equally valid reference for measuring bf16-level drift."""
     out = torch.empty_like(q)
     rep = q.shape[1] // k.shape[1]
     for s, e in zip(cu[:-1].tolist(), cu[1:].tolist()):
@@ -58,11 +60,14 @@ def attention(q, k, v, cu, window: int | None) -> torch.Tensor:
         if window is not None:
             m &= i[None, :] > i[:, None] - window
         sc = sc.masked_fill(~m, float("-inf"))
-        out[s:e] = (sc.softmax(-1) @ vv).transpose(0, 1).to(q.dtype)
+        pm = sc.softmax(-1)
+        if pv_bf16:
+            pm = pm.to(BF).float()
+        out[s:e] = (pm @ vv).transpose(0, 1).to(q.dtype)
     return out
 
 
-def moe_block(lw: dict, r: torch.Tensor, cfg, forced=None) -> torch.Tensor:
+def moe_block(lw: dict, r: torch.Tensor, cfg, forced=None, wcache: dict | None = None) -> torch.Tensor:
     """Router (on the residual) + pre_ff_norm_2 + experts + post_ff_norm_2. ``forced`` = (rows, ids): use these
     expert ids for these rows (teacher forcing), their weights recomputed from this oracle's own logits."""
     u, logits = O.gemma4_router(r.float().numpy(), lw["router_scale"].float().numpy(),
@@ -76,7 +81,7 @@ def moe_block(lw: dict, r: torch.Tensor, cfg, forced=None) -> torch.Tensor:
         w[rows] = O.route_weights(logits[rows], fids, lw["per_expert_scale"].numpy())
     x2 = rms_norm(r, lw["pre_ff_2"], cfg.eps)
     res = O.moe_forward(x2.float().numpy(), w, ids, lw["w1_fp4"], lw["w1_sf"], lw["w1_alphas"], lw["w2_fp4"],
-                        lw["w2_sf"], lw["w2_alphas"], lw["a1_gscale"], lw["a2_gscale"], "gelu_tanh")
+                        lw["w2_sf"], lw["w2_alphas"], lw["a1_gscale"], lw["a2_gscale"], "gelu_tanh", wcache)
     out = torch.from_numpy(np.ascontiguousarray(res["out"])).to(BF)
     return rms_norm(out, lw["post_ff_2"], cfg.eps)
 
@@ -92,7 +97,7 @@ def embed(weights: dict, cfg, token_ids: torch.Tensor) -> torch.Tensor:
     return weights["embed"][token_ids.long()] * torch.tensor(cfg.hidden ** 0.5).to(BF)
 
 
-def attention_block(weights: dict, cfg, i: int, x: torch.Tensor, cu: torch.Tensor) -> torch.Tensor:
+def attention_block(weights: dict, cfg, i: int, x: torch.Tensor, cu: torch.Tensor, pv_bf16: bool = False) -> torch.Tensor:
     """r = post_attention_norm(attn(input_norm(x))) + x for every row of x [n, hidden] bf16."""
     lw = weights["layers"][i]
     cu = cu.to(torch.int64)
@@ -107,7 +112,7 @@ def attention_block(weights: dict, cfg, i: int, x: torch.Tensor, cu: torch.Tenso
     q = rope(rms_norm(q.reshape(n, cfg.heads, cfg.head_dim), lw["q_norm"], cfg.eps), pos, theta)
     k = rope(rms_norm(k.reshape(n, cfg.kv_heads, cfg.head_dim), lw["k_norm"], cfg.eps), pos, theta)
     v = rms_norm(v.reshape(n, cfg.kv_heads, cfg.head_dim), None, cfg.eps)
-    a = attention(q, k, v, cu, cfg.window if sliding else None).reshape(n, hq) @ lw["wo"].t()
+    a = attention(q, k, v, cu, cfg.window if sliding else None, pv_bf16).reshape(n, hq) @ lw["wo"].t()
     return rms_norm(a, lw["post_attention"], cfg.eps) + x
 
 
@@ -122,11 +127,12 @@ def layer_output(lw: dict, r: torch.Tensor, d: torch.Tensor, m: torch.Tensor, cf
     return rms_norm(d + m, lw["post_ff"], cfg.eps) + r
 
 
-def decoder_layer(weights: dict, cfg, i: int, x: torch.Tensor, cu: torch.Tensor, forced=None) -> torch.Tensor:
+def decoder_layer(weights: dict, cfg, i: int, x: torch.Tensor, cu: torch.Tensor, forced=None,
+                  wcache: dict | None = None, pv_bf16: bool = False) -> torch.Tensor:
     """Layer i on every row of x [n, hidden] bf16; ``forced`` = (rows, ids) as in ``moe_block``."""
     lw = weights["layers"][i]
-    r = attention_block(weights, cfg, i, x, cu)
-    return layer_output(lw, r, dense_block(lw, r, cfg), moe_block(lw, r, cfg, forced), cfg)
+    r = attention_block(weights, cfg, i, x, cu, pv_bf16)
+    return layer_output(lw, r, dense_block(lw, r, cfg), moe_block(lw, r, cfg, forced, wcache), cfg)
 
 
 def readout(weights: dict, cfg, x_last: torch.Tensor, option_ids: torch.Tensor,
@@ -141,11 +147,11 @@ def readout(weights: dict, cfg, x_last: torch.Tensor, option_ids: torch.Tensor,
 
 
 def decision_forward(weights: dict, cfg, token_ids: torch.Tensor, cu: torch.Tensor, option_ids: torch.Tensor,
-                     temperature: float = 1.0) -> torch.Tensor:
+                     temperature: float = 1.0, wcache: dict | None = None, pv_bf16: bool = False) -> torch.Tensor:
     """weights: CPU tensors / numpy arrays exported from the GPU model (same names as its fields). Every row of
     every layer. Returns probabilities [B, n_opt] float64."""
     x = embed(weights, cfg, token_ids)
     for i in range(len(weights["layers"])):
-        x = decoder_layer(weights, cfg, i, x, cu)
+        x = decoder_layer(weights, cfg, i, x, cu, wcache=wcache, pv_bf16=pv_bf16)
     last = cu.to(torch.int64)[1:] - 1
     return readout(weights, cfg, x[last], option_ids, temperature)

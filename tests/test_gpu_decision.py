@@ -26,6 +26,16 @@ def small_cfg(**kw):
     return DecisionConfig(**base)
 
 
+def cfg3_shapes(**kw):
+    """BASELINE config 3's shapes (hidden 2816, 16 query / 8 KV heads of 256, the 128-expert top-8 MoE of 704 beside a
+    dense MLP of 2112, vocabulary 262144), at reduced depth; a window of 128 so that prompts of a few hundred tokens
+    exercise the sliding layers."""
+    from reax_engine_b200.decision import DecisionConfig
+    base = dict(layers=2, window=128)
+    base.update(kw)
+    return DecisionConfig(**base)
+
+
 def export(model) -> dict:
     cpu = lambda t: t.detach().cpu()
     layers = []
@@ -46,8 +56,9 @@ def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
     return ((a - b).norm() / b.norm()).item()
 
 
-@pytest.mark.parametrize("layers,n_prompts,seed", [(2, 6, 1), (3, 4, 2)])
-def test_decision_forward_matches_oracle_block_by_block(layers, n_prompts, seed):
+@pytest.mark.parametrize("shapes,layers,n_prompts,seed,lens", [("small", 2, 6, 1, (10, 40)), ("small", 3, 4, 2, (10, 40)),
+                                                              ("cfg3", 2, 3, 3, (64, 300))])
+def test_decision_forward_matches_oracle_block_by_block(shapes, layers, n_prompts, seed, lens):
     """Every block of every layer against the oracle's restatement, each from the GPU's own input to that block:
     attention + residual (flash-attention's bf16 P.V against an fp32 softmax: rel-L2 <= 5e-3), the dense MLP and the
     MoE block given the GPU's routing (the north-star MoE tolerance, rel-L2 <= 1e-2), their combination into the
@@ -57,9 +68,10 @@ def test_decision_forward_matches_oracle_block_by_block(layers, n_prompts, seed)
     boundary and top-k routing swaps experts on near ties, so bf16-level differences grow through the layers; the
     end-to-end comparison is reported by the next test."""
     from reax_engine_b200.decision import DecisionModel, synthetic_prompts
-    cfg = small_cfg(layers=layers)
+    cfg = small_cfg(layers=layers) if shapes == "small" else cfg3_shapes(layers=layers)
     model = DecisionModel(cfg, "cuda", seed=seed)
-    ids, cu = synthetic_prompts(n_prompts, 10, 40, cfg.vocab, seed=seed)
+    ids, cu = synthetic_prompts(n_prompts, lens[0], lens[1], cfg.vocab, seed=seed)
+    wcache: dict = {}
     amax = model.calibrate(ids.cuda(), cu.cuda())
     assert all(a > 0 for a in amax) and len(amax) == layers
     opts = torch.tensor([5, 17, 100, 400])
@@ -81,7 +93,7 @@ def test_decision_forward_matches_oracle_block_by_block(layers, n_prompts, seed)
             r_o = r_o[last]
         assert rel_l2(g["r"], r_o) <= 5e-3, f"layer {i} attention block"
         assert rel_l2(g["d"], D.dense_block(lw, g["r"], cfg)) <= 1e-2, f"layer {i} dense block"
-        m_o = D.moe_block(lw, g["r"], cfg, forced=(np.arange(g["r"].shape[0]), routed[i]))
+        m_o = D.moe_block(lw, g["r"], cfg, forced=(np.arange(g["r"].shape[0]), routed[i]), wcache=wcache)
         assert rel_l2(g["m"], m_o) <= 1e-2, f"layer {i} MoE block"
         x_next = logs[i + 1]["x"] if i + 1 < layers else logs[-1]
         assert rel_l2(x_next, D.layer_output(lw, g["r"], g["d"], g["m"], cfg)) <= 1e-3, f"layer {i} output"
@@ -90,7 +102,8 @@ def test_decision_forward_matches_oracle_block_by_block(layers, n_prompts, seed)
     g = logs[-1 - 1]
     lw = W["layers"][-1]
     x_last = D.layer_output(lw, g["r"], D.dense_block(lw, g["r"], cfg),
-                            D.moe_block(lw, g["r"], cfg, forced=(np.arange(n_prompts), routed[-1])), cfg)
+                            D.moe_block(lw, g["r"], cfg, forced=(np.arange(n_prompts), routed[-1]), wcache=wcache),
+                            cfg)
     ref = D.readout(W, cfg, x_last, opts)
     assert (p - ref).abs().max().item() <= 1e-3
     assert torch.equal(p.argmax(-1), ref.argmax(-1))
@@ -112,6 +125,33 @@ def test_decision_forward_independent_chain_report(capsys):
         print(f"\n[decision] independent chain: max |dp| = {err:.4f}, argmax agree "
               f"{(p.argmax(-1) == ref.argmax(-1)).float().mean().item():.2f}")
     assert err < 0.2
+
+
+def test_decision_forward_cfg3_shapes_independent_chain(capsys):
+    """Config-3 shapes, 2 layers, the oracle routing on its own logits (router std 0.5: top-k margins well above the
+    bf16-level differences upstream). Two equally valid references -- the oracle with fp32 softmax probabilities in
+    attention, and with bf16 ones as flash-attention feeds its tensor cores -- differ from each other at the bf16 level;
+    the GPU readout must be as close to the fp32 reference as that (or within the north-star 1e-3), with the same
+    argmax wherever the two references agree on it."""
+    from reax_engine_b200.decision import DecisionModel, synthetic_prompts
+    cfg = cfg3_shapes(router_std=0.5)
+    model = DecisionModel(cfg, "cuda", seed=4)
+    ids, cu = synthetic_prompts(3, 64, 300, cfg.vocab, seed=4)
+    model.calibrate(ids.cuda(), cu.cuda())
+    opts = torch.tensor([1000, 2000, 3000, 4000])
+    p = model.forward(ids.cuda(), cu.cuda(), opts.cuda()).cpu()
+    W = export(model)
+    wcache: dict = {}
+    ref = D.decision_forward(W, cfg, ids, cu, opts, wcache=wcache)
+    ref16 = D.decision_forward(W, cfg, ids, cu, opts, wcache=wcache, pv_bf16=True)
+    err = (p - ref).abs().max().item()
+    drift = (ref16 - ref).abs().max().item()
+    with capsys.disabled():
+        print(f"\n[decision cfg3 shapes] GPU vs oracle: max |dp| = {err:.2e}; oracle bf16-P vs fp32-P: {drift:.2e}; "
+              f"argmax agree {(p.argmax(-1) == ref.argmax(-1)).float().mean().item():.2f}")
+    assert err <= max(1e-3, 2.0 * drift)
+    same = ref16.argmax(-1) == ref.argmax(-1)
+    assert torch.equal(p.argmax(-1)[same], ref.argmax(-1)[same])
 
 
 def test_decision_forward_is_batch_independent():
