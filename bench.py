@@ -41,6 +41,7 @@ EP_E2E_CHUNKS = 4   # token parts per rank in the expert-parallel end-to-end pip
 EP_PARITY_TOKENS = 1024   # tokens per rank checked against the single-GPU layer after the timed expert-parallel steps
 EP_OVERLAP_PARTS = 1   # p2p: received records in this many parts, part c's row stores beside part c+1's GEMMs
 EP_PRESUM_SMS = 16     # p2p: SMs the overlapped row stores are pinned to
+EP_ROW_COPIES = 1      # p2p: received records in this many parts, each part's rows returned by the copy engines
 EP_TRANSPORT = "p2p"    # expert-parallel exchange: "nccl" (two all-to-alls) or "p2p" (the kernels' own NVLink stores)
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
@@ -632,6 +633,7 @@ def run_ours_ep(args, wl: dict) -> None:
     presum_sms = args.ep_presum_sms if args.ep_presum_sms is not None else EP_PRESUM_SMS
     layer = R.ep.ExpertParallelMoE(H, I, E, k, wl["act"], inp["a1_gscale"], local_w,
                                    transport=transport, overlap_parts=overlap, presum_sms=presum_sms,
+                                   row_copies=args.ep_row_copies if args.ep_row_copies is not None else EP_ROW_COPIES,
                                    **({} if args.ep_chunks is None else {"chunks": args.ep_chunks}))
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     s = torch.cuda.current_stream(dev)
@@ -737,7 +739,7 @@ def run_ours_ep(args, wl: dict) -> None:
                 config=dict(workload=wl["name"], tokens_per_rank=T, hidden=H, experts=E, topk=k, inter=I,
                             activation=wl["act"], parallelism=f"ep{world}", experts_per_rank=El, ep_chunks=layer.chunks,
                             ep_sm_reserve=sm_reserve, ep_transport=transport, ep_overlap_parts=overlap,
-                            ep_presum_sms=presum_sms, ep_direct_rows=os.environ.get("REAXMOE_EP_DIRECT_ROWS", "0") == "1",
+                            ep_presum_sms=presum_sms, ep_row_copies=layer.row_copies, ep_direct_rows=os.environ.get("REAXMOE_EP_DIRECT_ROWS", "0") == "1",
                             l2="inputs larger than L2 (x %.0f MB per rank, local weights %.0f MB); no flush" % (
                                 T * H * 2 / 1e6, weight_bytes / 1e6)),
                 e2e=None if e2e_value is None else dict(
@@ -865,6 +867,8 @@ def main():
     ap.add_argument("--ep-overlap-parts", type=int, default=None,
                     help="p2p (N > 1): received records in this many parts, row stores overlapped with GEMMs")
     ap.add_argument("--ep-presum-sms", type=int, default=None, help="p2p (N > 1): SMs the overlapped row stores use")
+    ap.add_argument("--ep-row-copies", type=int, default=None,
+                    help="p2p (N > 1): received records in this many parts, rows returned by the copy engines")
     ap.add_argument("--ep-sm-reserve", type=int, default=None,
                     help="SMs the library's persistent kernels leave free for the exchanges (N > 1)")
     args = ap.parse_args()

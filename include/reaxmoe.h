@@ -326,6 +326,12 @@ int reaxmoe_ep_expert_gemms(const reaxmoe_problem* local, const void* recv_recor
 int reaxmoe_ep_presum_to(const reaxmoe_problem* local, const void* workspace, size_t workspace_bytes, int32_t ranks,
                          const int64_t* bounds, const uint64_t* rows, int32_t sms, void* stream);
 
+/* n device-to-device copies on `stream`, dst[i] <- src[i] (bytes[i] each; host arrays of device addresses), one
+ * cudaMemcpyAsync each: the copy engines move them, over NVLink when a destination is a peer's CUDA-IPC-mapped
+ * buffer, without taking SMs from the kernels running beside them. Used to return one part's pre-summed rows from a
+ * local staging buffer to their source ranks while the next part's GEMMs run (no counterpart in the reference). */
+int reaxmoe_ep_copy_rows(int32_t n, const uint64_t* dst, const uint64_t* src, const uint64_t* bytes, void* stream);
+
 /* Synchronises `stream`, returns the device status word of the workspace (0 = ok, else REAXMOE_ERR_*) and
  * clears it when `clear` != 0. Not for the hot path. */
 int reaxmoe_read_status(void* workspace, size_t workspace_bytes, int32_t clear, void* stream);

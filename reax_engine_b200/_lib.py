@@ -97,6 +97,7 @@ SIGNATURES = {
                                                     _P, _P, _P]),
     "reaxmoe_ep_expert_gemms": (ctypes.c_int, [_PP, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _I32, _P]),
     "reaxmoe_ep_presum_to": (ctypes.c_int, [_PP, _P, ctypes.c_size_t, _I32, _P, _P, _I32, _P]),
+    "reaxmoe_ep_copy_rows": (ctypes.c_int, [_I32, _P, _P, _P, _P]),
 }
 
 _lock = threading.Lock()

@@ -882,6 +882,22 @@ int reaxmoe_ep_presum_to(const reaxmoe_problem* local, const void* workspace, si
   return cuda_check("ep_presum_to");
 }
 
+int reaxmoe_ep_copy_rows(int32_t n, const uint64_t* dst, const uint64_t* src, const uint64_t* bytes, void* stream) {
+  if (n < 0) return fail(REAXMOE_ERR_BAD_SHAPE, "ep_copy_rows: n=%d", n);
+  if (n > 0 && (dst == nullptr || src == nullptr || bytes == nullptr))
+    return fail(REAXMOE_ERR_NULL, "ep_copy_rows: NULL pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] == 0) continue;
+    if (dst[i] == 0 || src[i] == 0) return fail(REAXMOE_ERR_NULL, "ep_copy_rows: copy %d has a NULL address", i);
+    // one plain copy per range: the copy engines move it (over NVLink when dst is a peer's mapped buffer)
+    if (cudaMemcpyAsync(reinterpret_cast<void*>(dst[i]), reinterpret_cast<const void*>(src[i]), (size_t)bytes[i],
+                        cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return fail(REAXMOE_ERR_CUDA, "ep_copy_rows: copy %d failed", i);
+  }
+  return 0;
+}
+
 int reaxmoe_ep_combine(int32_t tokens, int32_t hidden, int32_t topk, const int32_t* send_map, const void* returned,
                        void* output, void* stream) {
   if (tokens < 0 || hidden < 128 || hidden % 128 != 0 || topk < 1 || topk > kMaxTopk)

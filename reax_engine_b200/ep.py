@@ -205,6 +205,16 @@ class DeviceOps:
         L.check(L.lib().reaxmoe_ep_presum_to(ctypes.byref(p), ws.data_ptr(), ws.numel(), self.R, b, r, sms,
                                              _stream(self.device)))
 
+    def copy_rows(self, dst: list[int], src: list[int], nbytes: list[int]) -> None:
+        """Device-to-device copies on the current stream by the copy engines (``reaxmoe_ep_copy_rows``)."""
+        n = len(dst)
+        if n == 0:
+            return
+        D = (ctypes.c_uint64 * n)(*dst)
+        S = (ctypes.c_uint64 * n)(*src)
+        B = (ctypes.c_uint64 * n)(*nbytes)
+        L.check(L.lib().reaxmoe_ep_copy_rows(n, D, S, B, _stream(self.device)))
+
     def signal(self, rank: int, blocks: list[int], epoch: int, counts: torch.Tensor | None,
                timeout_s: float) -> None:
         """``reaxmoe_ep_signal`` on the current stream (a barrier with the optional send-count payload)."""
@@ -388,7 +398,7 @@ class ExpertParallelMoE:
 
     def __init__(self, hidden: int, inter: int, experts: int, topk: int, activation, a1_gscale: torch.Tensor,
                  local: LocalExperts, group=None, ops=None, chunks: int = 1, transport: str = "auto",
-                 timeout_s: float = 10.0, overlap_parts: int = 1, presum_sms: int = 16):
+                 timeout_s: float = 10.0, overlap_parts: int = 1, presum_sms: int = 16, row_copies: int = 0):
         self.group = group
         self.R = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -415,6 +425,9 @@ class ExpertParallelMoE:
         self.overlap_parts = max(1, int(overlap_parts))
         self.presum_sms = int(presum_sms)
         self._side = None
+        # p2p: with row_copies = P > 1 the received records go in P parts; each part's rows are pre-summed into a
+        # local staging buffer, then copied to their source ranks by the copy engines while the next part computes
+        self.row_copies = int(row_copies)
 
     def status(self) -> int:
         """Synchronise; the first non-zero device status of the last forward (kernels, and the peer signals' waits
@@ -513,7 +526,9 @@ class ExpertParallelMoE:
         send_map = self.ops.pack_to(a, self.a1_gscale, ids, tw, records)
         px.signal()
         self._mark("dispatch")
-        if self.overlap_parts <= 1 or n_recv < 2 * self.overlap_parts:
+        if self.row_copies > 1 and n_recv >= 2 * self.row_copies:
+            self._experts_copied(px.recv.own, n_recv, bounds, rows, rec_bytes, row_bytes)
+        elif self.overlap_parts <= 1 or n_recv < 2 * self.overlap_parts:
             self.ops.expert_forward_to(px.recv.own, n_recv, self.local, bounds, rows)
         else:
             self._experts_overlapped(px.recv.own, n_recv, bounds, rows, rec_bytes, row_bytes)
@@ -549,6 +564,42 @@ class ExpertParallelMoE:
             with torch.cuda.stream(self._side):
                 self._side.wait_event(self._events[c])
                 self.ops.presum_to(c, pb, pr, sms=self.presum_sms)
+        cur.wait_stream(self._side)
+
+    def _experts_copied(self, recv_ptr: int, n_recv: int, bounds: list[int], rows: list[int], rec_bytes: int,
+                        row_bytes: int) -> None:
+        """The receiver in parts with copy-engine returns: part c's GEMMs and pre-sum run on the layer's stream (every
+        SM), the pre-summed rows landing in a local staging buffer at the records' own positions; then, on a copy
+        stream, one cudaMemcpyAsync per source rank moves the part's rows to that source's return buffer (over
+        NVLink), while part c + 1 computes. The same rows as expert_forward_to: each depends only on its record."""
+        cur = torch.cuda.current_stream(self.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+            self._events = []
+        P = self.row_copies
+        while len(self._events) < P:
+            self._events.append(torch.cuda.Event())
+        staging = self.ops.buf.get("row_staging", max(n_recv, 1) * row_bytes)
+        base = staging.data_ptr()
+        local_rows = [base + row_bytes * bounds[s] for s in range(self.R)]
+        step = -(-n_recv // P)
+        self._side.wait_stream(cur)
+        for c in range(P):
+            r0, r1 = min(n_recv, c * step), min(n_recv, (c + 1) * step)
+            self.ops.expert_gemms(recv_ptr + r0 * rec_bytes, r1 - r0, self.local, slot=c)
+            pb, pr = part_routes(bounds, local_rows, r0, r1, row_bytes)
+            self.ops.presum_to(c, pb, pr, sms=0)
+            self._events[c].record(cur)
+            dst, src, nb = [], [], []
+            for s in range(self.R):
+                a, b = max(r0, bounds[s]), min(r1, bounds[s + 1])
+                if b > a:
+                    dst.append(rows[s] + row_bytes * (a - bounds[s]))
+                    src.append(base + row_bytes * a)
+                    nb.append(row_bytes * (b - a))
+            with torch.cuda.stream(self._side):
+                self._side.wait_event(self._events[c])
+                self.ops.copy_rows(dst, src, nb)
         cur.wait_stream(self._side)
 
     __call__ = forward

@@ -43,7 +43,7 @@ def _single_gpu(R, c, w, ids, T, H, E, k, inter, dev="cuda"):
     return st, single
 
 
-def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False, parts=1):
+def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False, parts=1, copies=False):
     """R ranks on one GPU over the peer-memory device halves: plan, pack into the destinations' receive buffers,
     expert forward into the sources' return buffers, combine."""
     from test_gpu_ep import _local
@@ -69,13 +69,29 @@ def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False, parts=1):
         if parts == 1:
             ops[d].expert_forward_to(recv_ptrs[d], n_recv, _local(R, c, d, ranks), bounds, rows)
             continue
-        # the receiver in parts (reaxmoe_ep_expert_gemms + reaxmoe_ep_presum_to), the stores pinned to 8 SMs
+        # the receiver in parts (reaxmoe_ep_expert_gemms + reaxmoe_ep_presum_to): stores pinned to 8 SMs, or
+        # (copies) rows pre-summed into a local staging buffer and moved by reaxmoe_ep_copy_rows
         step = -(-n_recv // parts)
+        staging = torch.empty(max(n_recv, 1) * row, dtype=torch.uint8, device="cuda")
+        local_rows = [staging.data_ptr() + row * bounds[s] for s in range(ranks)]
         for q in range(parts):
             r0, r1 = min(n_recv, q * step), min(n_recv, (q + 1) * step)
-            ops[d].expert_gemms(recv_ptrs[d] + r0 * rec, r1 - r0, _local(R, c, d, ranks), slot=q, sm_limit=140)
-            pb, pr = R.ep.part_routes(bounds, rows, r0, r1, row)
-            ops[d].presum_to(q, pb, pr, sms=8)
+            ops[d].expert_gemms(recv_ptrs[d] + r0 * rec, r1 - r0, _local(R, c, d, ranks), slot=q,
+                                sm_limit=0 if copies else 140)
+            if not copies:
+                pb, pr = R.ep.part_routes(bounds, rows, r0, r1, row)
+                ops[d].presum_to(q, pb, pr, sms=8)
+                continue
+            pb, pr = R.ep.part_routes(bounds, local_rows, r0, r1, row)
+            ops[d].presum_to(q, pb, pr, sms=0)
+            dst, src, nb = [], [], []
+            for s in range(ranks):
+                a, b = max(r0, bounds[s]), min(r1, bounds[s + 1])
+                if b > a:
+                    dst.append(rows[s] + row * (a - bounds[s]))
+                    src.append(staging.data_ptr() + row * a)
+                    nb.append(row * (b - a))
+            ops[d].copy_rows(dst, src, nb)
     outs, rows_back = [], []
     for s in range(ranks):
         n_send = sum(C[s])
@@ -89,15 +105,17 @@ def _emulate_p2p(R, c, w, ids, Ts, ranks, return_rows=False, parts=1):
     return (torch.cat(outs), rows_back) if return_rows else torch.cat(outs)
 
 
-@pytest.mark.parametrize("ranks,Ts,parts", [(2, [700, 313], 1), (4, [256, 0, 511, 64], 1), (8, [100] * 8, 1),
-                                           (2, [700, 313], 3), (8, [100] * 8, 2)])
-def test_p2p_emulated_ranks_bit_exact(R, ranks, Ts, parts):
+@pytest.mark.parametrize("ranks,Ts,parts,copies", [(2, [700, 313], 1, False), (4, [256, 0, 511, 64], 1, False),
+                                                  (8, [100] * 8, 1, False), (2, [700, 313], 3, False),
+                                                  (8, [100] * 8, 2, False), (8, [100] * 8, 3, True),
+                                                  (4, [256, 0, 511, 64], 2, True)])
+def test_p2p_emulated_ranks_bit_exact(R, ranks, Ts, parts, copies):
     from test_gpu_ep import _emulate, _expected_from_single_gpu_c3
     T, H, E, k, inter = sum(Ts), 2816, 128, 8, 704
     c = make_case(T, H, E, k, inter, "gelu_tanh", seed=ranks)
     w, ids = R.route(None, c["logits"], k)
     st, single = _single_gpu(R, c, w, ids, T, H, E, k, inter)
-    got = _emulate_p2p(R, c, w, ids, Ts, ranks, parts=parts)
+    got = _emulate_p2p(R, c, w, ids, Ts, ranks, parts=parts, copies=copies)
     expect = _expected_from_single_gpu_c3(st.c3.float().cpu().numpy(), st.c_map.cpu().numpy(), w.cpu().numpy(),
                                           ids.cpu().numpy(), E // ranks, ranks)
     assert np.array_equal(got.float().cpu().numpy(), expect)
@@ -217,6 +235,8 @@ def _worker(rank, world, port, Ts, errq):
                                      timeout_s=20.0)
         p2p3 = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], loc, transport="p2p",
                                       timeout_s=20.0, overlap_parts=3, presum_sms=8)
+        p2pc = R.ep.ExpertParallelMoE(H, inter, E, k, "gelu_tanh", c["a1_gscale"], loc, transport="p2p",
+                                      timeout_s=20.0, row_copies=3)
         ref = nccl(c["x"][t0:t1], w[t0:t1], ids[t0:t1])
         t4 = t0 + max(1, Ts[rank] // 4)
         first = p2p(c["x"][t0:t4], w[t0:t4], ids[t0:t4])         # small buffers first, grown by the next call
@@ -224,9 +244,11 @@ def _worker(rank, world, port, Ts, errq):
         out2 = p2p(c["x"][t0:t1], w[t0:t1], ids[t0:t1])          # buffers reused
         big = p2p(c["x"], w, ids)                                  # every rank all T tokens: the buffers grow
         parted = p2p3(c["x"][t0:t1], w[t0:t1], ids[t0:t1])        # the receiver in 3 parts, stores overlapped
+        copied = p2pc(c["x"][t0:t1], w[t0:t1], ids[t0:t1])        # rows returned by the copy engines
         torch.cuda.synchronize(dev)
-        assert p2p.status() == 0 and nccl.status() == 0 and p2p3.status() == 0
+        assert p2p.status() == 0 and nccl.status() == 0 and p2p3.status() == 0 and p2pc.status() == 0
         assert torch.equal(parted, out), f"rank {rank}: the overlapped receiver differs"
+        assert torch.equal(copied, out), f"rank {rank}: the copy-engine returns differ"
         got = out.float().cpu().numpy()
         assert np.array_equal(got, expect[t0:t1]), f"rank {rank}: p2p output differs from the recombined c3"
         assert torch.equal(out, ref) and torch.equal(out, out2)
@@ -235,6 +257,7 @@ def _worker(rank, world, port, Ts, errq):
         tol_check(got, single[t0:t1].float().cpu().numpy())
         p2p.close()
         p2p3.close()
+        p2pc.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # noqa: BLE001 - reported to the parent
