@@ -71,9 +71,103 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   }
 }
 
+// The same routing with four lanes per token, for batches large enough to fill the GPU that way. A CTA of 128 threads
+// (32 tokens) stages its tokens' logits in shared memory, rows padded to a stride of 4 mod 32 words so that the
+// quad's reads are free of bank conflicts. Lane q of a token's quad scans the logits q, q + 4, ... keeping its top KMAX
+// keys (the 64-bit (logit, -index) order of route_kernel) sorted by a branch-free insertion; the quad then merges its
+// four lists in K rounds of a 2-step shuffle maximum. Lane 0 computes the weights with route_kernel's arithmetic and
+// summation order: the same ids and weights bit for bit.
+constexpr int kRouteTokens = 32;
+
+template <int KMAX>
+__global__ void __launch_bounds__(128) route_quad_kernel(const float* __restrict__ logits,
+                                                         const float* __restrict__ scale, int T, int E, int K,
+                                                         int* __restrict__ ids, float* __restrict__ weights) {
+  extern __shared__ float tile[];   // [kRouteTokens][stride]
+  const int stride = E + ((4 - E) % 32 + 32) % 32;
+  const int64_t t0 = (int64_t)blockIdx.x * kRouteTokens;
+  const int nt = (int)((T - t0) < kRouteTokens ? (T - t0) : kRouteTokens);
+  for (int tl = 0; tl < nt; ++tl)
+    for (int e = threadIdx.x; e < E; e += blockDim.x) tile[tl * stride + e] = logits[(t0 + tl) * E + e];
+  __syncthreads();
+  const int tl = threadIdx.x >> 2, q = threadIdx.x & 3;
+  const bool active = tl < nt;
+  const float* row = tile + tl * stride;
+  uint64_t top[KMAX];
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) top[j] = 0ull;
+  if (active) {
+    for (int e = q; e < E; e += 4) {
+      const uint64_t key = ((uint64_t)sortable_key(row[e]) << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)e);
+      if (key <= top[KMAX - 1]) continue;
+      // insert into the descending list: new[i] = max(old[i], min(old[i-1], key)), new[0] = max(old[0], key)
+#pragma unroll
+      for (int j = KMAX - 1; j > 0; --j) {
+        const uint64_t m = top[j - 1] < key ? top[j - 1] : key;
+        top[j] = top[j] > m ? top[j] : m;
+      }
+      top[0] = top[0] > key ? top[0] : key;
+    }
+  }
+  // merge the quad's lists: K rounds, each takes the largest head and the lane that owned it drops it
+  uint64_t win[KMAX];
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    if (j < K) {
+      uint64_t best = top[0];
+      uint64_t o = __shfl_xor_sync(0xffffffffu, best, 1);
+      best = o > best ? o : best;
+      o = __shfl_xor_sync(0xffffffffu, best, 2);
+      best = o > best ? o : best;
+      win[j] = best;
+      if (top[0] == best) {
+#pragma unroll
+        for (int i = 0; i < KMAX - 1; ++i) top[i] = top[i + 1];
+        top[KMAX - 1] = 0ull;
+      }
+    }
+  }
+  if (!active || q != 0) return;
+  // weights exactly as route_kernel: e_j = exp(l_j - l_0), denominator summed in increasing j, IEEE division
+  const int64_t t = t0 + tl;
+  const float top_val = row[(int)(0xFFFFFFFFu - (uint32_t)win[0])];
+  float ex[KMAX];
+  float denom = 0.0f;
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    if (j < K) {
+      ex[j] = expf(row[(int)(0xFFFFFFFFu - (uint32_t)win[j])] - top_val);
+      denom = __fadd_rn(denom, ex[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    if (j < K) {
+      const int id = (int)(0xFFFFFFFFu - (uint32_t)win[j]);
+      float w = __fdiv_rn(ex[j], denom);
+      if (scale != nullptr) w = __fmul_rn(w, scale[id]);
+      ids[t * K + j] = id;
+      weights[t * K + j] = w;
+    }
+  }
+}
+
 int launch_route(const float* logits, const float* scale, int T, int E, int K, int* ids, float* w,
                  cudaStream_t s) {
   if (T == 0) return 0;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t blocks = ceil_div64(T, kRouteTokens);
+  const size_t smem = (size_t)kRouteTokens * (E + 32) * sizeof(float);
+  // four lanes per token once there are enough tokens for several CTAs per SM
+  if (blocks >= 4 * sms && K <= 16) {
+    if (K <= 8)
+      route_quad_kernel<8><<<(unsigned)blocks, 128, smem, s>>>(logits, scale, T, E, K, ids, w);
+    else
+      route_quad_kernel<16><<<(unsigned)blocks, 128, smem, s>>>(logits, scale, T, E, K, ids, w);
+    return 0;
+  }
   const int warps_per_block = 8;
   const dim3 grid((unsigned)ceil_div64(T, warps_per_block));
   if (E <= 32) route_kernel<1><<<grid, 256, 0, s>>>(logits, scale, T, E, K, ids, w);

@@ -54,6 +54,26 @@ def test_route_ties_go_to_lower_expert(R):
     np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("T,E,k,ties", [(40000, 128, 8, False), (40000, 128, 8, True), (20000, 256, 16, False),
+                                        (19000, 64, 4, True)])
+def test_route_large_batch_kernel_bit_exact(R, T, E, k, ties):
+    """Batches of >= 4 x 148 x 32 tokens route with four lanes per token (route_quad_kernel); smaller ones with a
+    warp per token. Both give the same ids and weights bit for bit (the chunks below take the warp kernel), and the
+    oracle's ids."""
+    g = torch.Generator().manual_seed(T + E)
+    logits = (torch.randint(-3, 3, (T, E), generator=g).float() if ties else torch.randn(T, E, generator=g)).cuda()
+    scale = (torch.rand(E, generator=g) + 0.5).cuda()
+    w, ids = R.route(None, logits, k, True, scale)
+    parts = [R.route(None, logits[i:i + 4096].contiguous(), k, True, scale) for i in range(0, T, 4096)]
+    w_c = torch.cat([p[0] for p in parts])
+    ids_c = torch.cat([p[1] for p in parts])
+    assert torch.equal(ids, ids_c)
+    assert torch.equal(w.view(torch.int32), w_c.view(torch.int32))
+    sel = np.arange(0, T, 37)
+    wr, idr = O.route(logits.cpu().numpy()[sel], k, scale.cpu().numpy())
+    assert np.array_equal(ids.cpu().numpy()[sel], idr)
+
+
 def test_route_golden_vllm(R):
     d = np.load(os.path.join(G, "route_golden.npz"))
     for name in ("e128k8", "e64k4"):
