@@ -46,8 +46,8 @@ EP_TRANSPORT = "p2p"    # expert-parallel exchange: "nccl" (two all-to-alls) or 
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
 # workload summarised in profiles/dram_traffic_cfg2.md; None where no capture covers the workload.
-NCU_TRAFFIC = {"cfg2": {"gemm_w13": 957_964_000, "gemm_w2": 1_868_524_000, "permute_quant": 602_162_000,
-                        "combine": 1_792_187_000}}
+NCU_TRAFFIC = {"cfg2": {"gemm_w13": 849_161_984, "gemm_w2": 1_814_097_664, "permute_quant": 603_705_600,
+                        "combine": 1_794_828_800}}
 
 
 def load_peaks() -> dict:
