@@ -15,7 +15,12 @@
 //   warp 0      TMA producer, into a 4-deep ring of 54 KiB stages: A (routed FP4 rows, 128 x 256 K) and B (expert
 //               weights, 256 x 256 K) by 2D TMA with 128-byte swizzle, plus the stage's scale atoms as they lie in
 //               memory (engine/fp4.py 128x4 atoms, 512 B per 128 rows x 64-element k-chunk) by 1D bulk copies: the
-//               A scales of the m-tile's rows and the B scales of the n-tile's two 128-row blocks.
+//               A scales of the m-tile's rows and the B scales of the n-tile's two 128-row blocks. Resident-A layout
+//               (K <= 768, i.e. w2, with at least two m-tiles per CTA): the m-tile's whole A and its scale atoms
+//               (up to 3 slices of 256 K, 54 KiB) are loaded once per m-tile into a fixed region and read by all its
+//               n-tiles, and the ring stages (36 KiB) carry B and its scale atoms only. Each slice has its own
+//               full / empty barrier pair: the next m-tile's slice is loaded as soon as the last n-tile's MMAs on it
+//               are done (measured at config 2: w2 0.567 -> 0.548 ms).
 //   warp 1      allocates 512 TMEM columns (warps 2-3 idle); one thread issues tcgen05.mma.kind::mxf4nvf4.block_scale.block16
 //               (M=128, N=256, K=64; 4 per stage) into the fp32 accumulator and commits each stage to its empty
 //               barrier (which frees the stage's shared memory and its scale columns in TMEM).
@@ -68,13 +73,26 @@ static_assert(2 * 128 * REGS_CONTROL + 2 * 128 * REGS_EPILOGUE <= 65536, "regist
 constexpr int TMEM_COLS = 512;
 constexpr int SFA_COL = BN;                           // A scales of stage s: columns SFA_COL + 16 s + 4 kk
 constexpr int SFB_COL = SFA_COL + STAGES * 4 * KPS;   // B scales of stage s: columns SFB_COL + 32 s + 8 kk
-constexpr int NUM_BARS = 3 * STAGES + 3;
+// Resident A (problems with K <= 768, i.e. w2 at the 26B-A4B shapes): the m-tile's whole A -- at most RA_SLICES
+// slices of 256 K -- and its scale atoms are loaded once per work item into a fixed region and read by all the item's
+// n-tiles; the ring then carries B and its scale atoms only (36 instead of 54 KiB a stage).
+constexpr int RA_SLICES = 3;
+constexpr int RA_BYTES = RA_SLICES * (A_BYTES + SFA_BYTES);
+constexpr int NUM_BARS = 3 * STAGES + 3 + 2 * RA_SLICES;
 constexpr int SMEM_TABLE_INTS = 4 * (kMaxExperts + 1);
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + SMEM_TABLE_INTS * 4;
-static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned for the 128B swizzle");
+template <bool RA>
+struct Layout {
+  static constexpr int stage = RA ? B_BYTES + SFB_BYTES : STAGE_BYTES;  // bytes of one ring stage
+  static constexpr int ring = RA ? RA_BYTES : 0;                        // offset of stage 0
+  static constexpr int b_off = RA ? 0 : A_BYTES;                        // B tile inside a stage
+  static constexpr int sfb_off = RA ? B_BYTES : A_BYTES + B_BYTES + SFA_BYTES;
+  static constexpr int bars = ring + STAGES * stage;
+  static constexpr int smem = 1024 + bars + 256 + SMEM_TABLE_INTS * 4;
+  static_assert(stage % 1024 == 0 && ring % 1024 == 0, "tiles must stay 1024-byte aligned for the 128B swizzle");
+  static_assert(smem <= 227 * 1024, "shared memory budget");
+};
 static_assert(SFB_COL + STAGES * 8 * KPS <= TMEM_COLS, "TMEM budget");
 static_assert(NUM_BARS * 8 + 8 <= 256, "barrier area");
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 // Instruction descriptor of tcgen05.mma.kind::mxf4nvf4 (block-scaled): A/B = e2m1 (MXF4 format 1) at bits
 // [7,10) / [10,13), K-major both, N >> 3 at [17,23), scale type ue4m3 (0) at bit 23, M >> 4 at [24,29),
@@ -185,18 +203,22 @@ __device__ __forceinline__ uint32_t act_quant32(const uint32_t (&x0)[32], const 
   return sbytes;
 }
 
-template <int MODE, int ACT>
+template <int MODE, int ACT, bool RA>
 __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+  using L = Layout<RA>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* ring = smem + L::ring;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::bars);
   uint64_t* full = bars;                 // [STAGES] A, B and the scale atoms landed (TMA tx)
   uint64_t* empty = bars + STAGES;       // [STAGES] MMAs of the stage done: smem stage and its TMEM scales free
   uint64_t* sff = empty + STAGES;        // [STAGES] the stage's scales written to TMEM (4 scale-writer warps)
   uint64_t* accf = sff + STAGES;         // accumulator ready for the epilogue
   uint64_t* acce = accf + 1;             // accumulator drained by the epilogue
   uint64_t* drain_mma = acce + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_mma + 1);
+  uint64_t* afull = drain_mma + 1;       // [RA_SLICES] resident A slice and its scale atoms landed
+  uint64_t* aempty = afull + RA_SLICES;  // [RA_SLICES] the item's last MMAs on the slice done: slice free
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(aempty + RA_SLICES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   int* s_tp = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + 256);
   int* s_cnt = s_tp + (kMaxExperts + 1);
@@ -223,6 +245,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     mbar_init(smem_u32(accf), 1);
     mbar_init(smem_u32(acce), NUM_EPI_WARPS);
     mbar_init(smem_u32(drain_mma), 1);
+    for (int s = 0; s < RA_SLICES; ++s) {
+      mbar_init(smem_u32(&afull[s]), 1);
+      mbar_init(smem_u32(&aempty[s]), 1);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tmA)) : "memory");
@@ -258,12 +284,14 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         int stage = 0;
         uint32_t phase = 0;
         long fills = 0;
+        int a_fills[RA_SLICES] = {0, 0, 0};
         bool ok = true;
-        for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
+        for (int u = blockIdx.x, it = 0; u < items && ok; u += gridDim.x, ++it) {
           const int gm = by_unit ? u / n_tiles : u;
           const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
           const uint8_t* sfa = p.sfA + (size_t)M.sfblk * k_chunks * SF_ATOM;
-          for (int nt = by_unit ? u % n_tiles : 0, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
+          const int nt_first = by_unit ? u % n_tiles : 0;
+          for (int nt = nt_first, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
             const int brow = M.e * p.N + nt * BN;
             const bool b1 = has_block1(nt);
             const uint8_t* sfb0 = p.sfB + ((size_t)M.e * p.n_blocks + 2 * nt) * k_chunks * SF_ATOM;
@@ -271,20 +299,38 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
             for (int ks = 0; ks < k_stages; ++ks) {
               const int kc0 = ks * KPS;
               const int nk = min(KPS, k_chunks - kc0);
+              const uint32_t sf_bytes = (uint32_t)(nk * SF_ATOM);
+              if (RA && nt == nt_first) {
+                // the item's A slice ks, once the previous item's MMAs on it are done
+                if (!wait_bounded(smem_u32(&aempty[ks]), (uint32_t)(it & 1) ^ 1u, abort_flag, p.status,
+                                  p.timeout_ns)) {
+                  ok = false;
+                  break;
+                }
+                const uint32_t abar = smem_u32(&afull[ks]);
+                mbar_expect_tx(abar, (uint32_t)A_BYTES + sf_bytes);
+                tma_load_2d(smem_u32(smem + ks * A_BYTES), &p.tmA, abar, kc0 * (KSTEP / 2), M.row0);
+                bulk_load(smem_u32(smem + RA_SLICES * A_BYTES + ks * SFA_BYTES), sfa + (size_t)kc0 * SF_ATOM,
+                          sf_bytes, abar);
+                ++a_fills[ks];
+              }
               if (!wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
                 ok = false;
                 break;
               }
-              uint8_t* st = smem + stage * STAGE_BYTES;
+              uint8_t* st = ring + stage * L::stage;
               const uint32_t bar = smem_u32(&full[stage]);
-              const uint32_t sf_bytes = (uint32_t)(nk * SF_ATOM);
-              mbar_expect_tx(bar, (uint32_t)(A_BYTES + B_BYTES) + sf_bytes * (b1 ? 3u : 2u));
-              tma_load_2d(smem_u32(st), &p.tmA, bar, kc0 * (KSTEP / 2), M.row0);
-              tma_load_2d(smem_u32(st + A_BYTES), &p.tmB, bar, kc0 * (KSTEP / 2), brow);
-              uint8_t* sf_st = st + A_BYTES + B_BYTES;
-              bulk_load(smem_u32(sf_st), sfa + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
-              bulk_load(smem_u32(sf_st + SFA_BYTES), sfb0 + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
-              if (b1) bulk_load(smem_u32(sf_st + SFA_BYTES + KPS * SF_ATOM), sfb1 + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
+              uint8_t* sfb_st = st + L::sfb_off;
+              if constexpr (RA) {
+                mbar_expect_tx(bar, (uint32_t)B_BYTES + sf_bytes * (b1 ? 2u : 1u));
+              } else {
+                mbar_expect_tx(bar, (uint32_t)(A_BYTES + B_BYTES) + sf_bytes * (b1 ? 3u : 2u));
+                tma_load_2d(smem_u32(st), &p.tmA, bar, kc0 * (KSTEP / 2), M.row0);
+                bulk_load(smem_u32(st + A_BYTES + B_BYTES), sfa + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
+              }
+              tma_load_2d(smem_u32(st + L::b_off), &p.tmB, bar, kc0 * (KSTEP / 2), brow);
+              bulk_load(smem_u32(sfb_st), sfb0 + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
+              if (b1) bulk_load(smem_u32(sfb_st + KPS * SF_ATOM), sfb1 + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
               ++fills;
               if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
@@ -293,6 +339,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         // let the last fills land before the CTA may exit (only matters after an abort)
         for (long f = fills - 1; f >= 0 && f >= fills - STAGES; --f)
           wait_drain(smem_u32(&full[f % STAGES]), (uint32_t)((f / STAGES) & 1));
+        if constexpr (RA) {
+          for (int ks = 0; ks < RA_SLICES; ++ks)
+            if (a_fills[ks] > 0) wait_drain(smem_u32(&afull[ks]), (uint32_t)((a_fills[ks] - 1) & 1));
+        }
       }
     } else if (warp == 1) {
       // ------------------------------------------------------------------ MMA issuer (one thread)
@@ -319,13 +369,16 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                 break;
               }
               tc_fence_after();
-              const uint32_t a_s = smem_u32(smem + stage * STAGE_BYTES);
-              const uint32_t b_s = a_s + A_BYTES;
+              const uint32_t st = smem_u32(ring + stage * L::stage);
+              const uint32_t a_s = RA ? smem_u32(smem + ks * A_BYTES) : st;
+              const uint32_t b_s = st + L::b_off;
               for (int kk = 0; kk < nk; ++kk)
                 tc_mma_fp4(tmem, desc_sw128(a_s + kk * (KSTEP / 2)), desc_sw128(b_s + kk * (KSTEP / 2)), idesc,
                            tmem + SFA_COL + 4 * (KPS * stage + kk), tmem + SFB_COL + 8 * (KPS * stage + kk),
                            (ks | kk) != 0 ? 1u : 0u);
               tc_commit(smem_u32(&empty[stage]));
+              // the item's last MMAs on the resident slice: it may be refilled once they complete
+              if (RA && nt == nt_end - 1) tc_commit(smem_u32(&aempty[ks]));
             }
             if (!ok) break;
             tc_commit(smem_u32(accf));
@@ -344,27 +397,36 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
       long n = 0;
       bool ok = true;
       const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-      for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
-        for (int nt = by_unit ? u % n_tiles : 0, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
+      for (int u = blockIdx.x, it = 0; u < items && ok; u += gridDim.x, ++it) {
+        const int nt_first = by_unit ? u % n_tiles : 0;
+        for (int nt = nt_first, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
           const bool b1 = has_block1(nt);
           for (int ks = 0; ks < k_stages; ++ks, ++n) {
             const int stage = (int)(n % STAGES);
             const int nk = min(KPS, k_chunks - ks * KPS);
-            // one lane waits, the warp follows its verdict (the stores below are warp-collective)
-            bool landed = lane == 0 ? wait_bounded(smem_u32(&full[stage]), (uint32_t)((n / STAGES) & 1), abort_flag,
-                                                   p.status, p.timeout_ns)
-                                    : false;
+            // one lane waits, the warp follows its verdict (the stores below are warp-collective); with a resident
+            // A, the item's first n-tile also waits for the A slice (its scale atoms are read below, and the MMA
+            // issuer, which waits for this warp's arrival, reads the slice)
+            bool landed = false;
+            if (lane == 0) {
+              landed = !(RA && nt == nt_first) ||
+                       wait_bounded(smem_u32(&afull[ks]), (uint32_t)(it & 1), abort_flag, p.status, p.timeout_ns);
+              landed = landed && wait_bounded(smem_u32(&full[stage]), (uint32_t)((n / STAGES) & 1), abort_flag,
+                                              p.status, p.timeout_ns);
+            }
             landed = __shfl_sync(0xffffffffu, landed ? 1 : 0, 0) != 0;
             if (!landed) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint8_t* sf_st = smem + stage * STAGE_BYTES + A_BYTES + B_BYTES + lane * 16;
+            const uint8_t* sfa_st = (RA ? smem + RA_SLICES * A_BYTES + ks * SFA_BYTES
+                                        : ring + stage * L::stage + A_BYTES + B_BYTES) + lane * 16;
+            const uint8_t* sfb_st = ring + stage * L::stage + L::sfb_off + lane * 16;
             for (int kk = 0; kk < nk; ++kk) {
-              const uint4 a = *reinterpret_cast<const uint4*>(sf_st + kk * SF_ATOM);
-              const uint4 b0 = *reinterpret_cast<const uint4*>(sf_st + SFA_BYTES + kk * SF_ATOM);
-              const uint4 bb = b1 ? *reinterpret_cast<const uint4*>(sf_st + SFA_BYTES + (KPS + kk) * SF_ATOM) : zero;
+              const uint4 a = *reinterpret_cast<const uint4*>(sfa_st + kk * SF_ATOM);
+              const uint4 b0 = *reinterpret_cast<const uint4*>(sfb_st + kk * SF_ATOM);
+              const uint4 bb = b1 ? *reinterpret_cast<const uint4*>(sfb_st + (KPS + kk) * SF_ATOM) : zero;
               tc_st_32x32b_x4(tq + SFA_COL + 4 * (KPS * stage + kk), a);
               tc_st_32x32b_x8(tq + SFB_COL + 8 * (KPS * stage + kk), b0, bb);
             }
@@ -502,13 +564,19 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
 }
 
 // ---------------------------------------------------------------- host side
-template <int MODE, int ACT>
-static int launch_t(const Params& prm, int grid, cudaStream_t s) {
-  auto kfn = grouped_gemm_kernel<MODE, ACT>;
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+template <int MODE, int ACT, bool RA>
+static int launch_ra(const Params& prm, int grid, cudaStream_t s) {
+  auto kfn = grouped_gemm_kernel<MODE, ACT, RA>;
+  constexpr int smem = Layout<RA>::smem;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return REAXMOE_ERR_CUDA;
-  kfn<<<grid, THREADS, SMEM_BYTES, s>>>(prm);
+  kfn<<<grid, THREADS, smem, s>>>(prm);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : REAXMOE_ERR_CUDA;
+}
+template <int MODE, int ACT>
+static int launch_t(const Params& prm, int grid, bool ra, cudaStream_t s) {
+  if (ra) return launch_ra<MODE, ACT, true>(prm, grid, s);
+  return launch_ra<MODE, ACT, false>(prm, grid, s);
 }
 
 }  // namespace gemm
@@ -548,9 +616,13 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   prm.n_blocks = g.N / 128;
   const int64_t max_units = (g.slots / BM + g.E + 1) * prm.n_tiles;
   const int grid = (int)(max_units < num_sms ? max_units : num_sms);
-  if (g.mode == 0) return launch_t<0, 0>(prm, grid, s);
-  if (g.act == REAXMOE_ACT_GELU_TANH) return launch_t<1, REAXMOE_ACT_GELU_TANH>(prm, grid, s);
-  return launch_t<1, REAXMOE_ACT_SILU>(prm, grid, s);
+  // The resident-A layout where the m-tile's A fits it and every CTA gets at least two m-tiles (then the kernel
+  // hands out whole m-tiles and each resident A serves all their n-tiles). A small batch, handed out as single
+  // (m-tile, n-tile) units, keeps the 4-deep ring of A and B: a resident slice would only be reused by one n-tile.
+  const bool ra = (prm.k_chunks + KPS - 1) / KPS <= RA_SLICES && g.slots / BM >= 2 * (int64_t)grid;
+  if (g.mode == 0) return launch_t<0, 0>(prm, grid, ra, s);
+  if (g.act == REAXMOE_ACT_GELU_TANH) return launch_t<1, REAXMOE_ACT_GELU_TANH>(prm, grid, ra, s);
+  return launch_t<1, REAXMOE_ACT_SILU>(prm, grid, ra, s);
 }
 
 }  // namespace reaxmoe

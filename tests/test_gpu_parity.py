@@ -190,7 +190,10 @@ def _ulp_close(got, ref, frac_exact=0.99):
     assert (got == ref).mean() >= frac_exact
 
 
-@pytest.mark.parametrize("shape", [(256, 256, 8, 2, 256), (512, 2048, 64, 4, 1024), (300, 2816, 128, 8, 704)])
+# (20000, 1152, 8, 2, 640): more than two m-tiles per CTA, so the items chain through the resident A slices (the
+# last one partial), and a narrow last n-tile
+@pytest.mark.parametrize("shape", [(256, 256, 8, 2, 256), (512, 2048, 64, 4, 1024), (300, 2816, 128, 8, 704),
+                                   (20000, 1152, 8, 2, 640)])
 def test_gemm_w2_matches_oracle(R, shape):
     T, H, E, k, inter = shape
     c = make_case(T, H, E, k, inter, "gelu_tanh", seed=21)
@@ -216,7 +219,7 @@ def test_gemm_w2_matches_oracle(R, shape):
 
 
 @pytest.mark.parametrize("act", ["gelu_tanh", "silu"])
-@pytest.mark.parametrize("shape", [(256, 256, 8, 2, 256), (300, 2816, 128, 8, 704)])
+@pytest.mark.parametrize("shape", [(256, 256, 8, 2, 256), (300, 2816, 128, 8, 704), (20000, 512, 8, 2, 320)])
 def test_gemm_w13_fused_matches_oracle(R, act, shape):
     T, H, E, k, inter = shape
     c = make_case(T, H, E, k, inter, act, seed=31)
