@@ -568,7 +568,7 @@ def run_ours(args, wl: dict) -> None:
         r = reference_cpu_run(wl, steps=3, warmup=1)
         cpu = dict(value=r["value"], unit="tokens/s", cores=r["threads"], kind="port",
                    sample=r["sample"] + f"; 3 steps, {r['seconds']:.2f} s")
-    launches_per_step = 8   # route, count, plan, permute_quant, swizzle_scales, gemm_w13, gemm_w2, combine
+    launches_per_step = 9   # route, count, plan, assign_slots, quant_scatter, swizzle_scales, gemm_w13, gemm_w2, combine
     line = dict(metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
                 ms_per_step=ms_step, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="nvfp4 (e2m1)",
                 data="synthetic",

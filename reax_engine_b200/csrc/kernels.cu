@@ -275,49 +275,55 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
 }
 
 // ------------------------------------------------------------------------------------------------------
-// K3 permute_quant: `parts` CTAs per segment (parts > 1 only when segments are fewer than two per SM).
-//  Phase A (warp 0, segment_slots): canonical slot of every (token, j) pair of the segment, token-major inside
-//  an expert, starting from run[e] = expert_offsets[e] + seg_base[seg][e]. Every CTA of the segment computes it
-//  (a scan of the segment's ids); part 0 writes c_map.
-//  Phase B (all warps): each token row is NVFP4-quantised once per distinct expert input scale and written
-//  to its k slots (FP4 bytes + the two scale bytes of each 32-element unit), the same bytes as vLLM's per-slot
-//  quant of the shuffled rows (blink_moe.py:301-323, cutlass_moe.py:585-593).
+// K3 permute_quant, in two kernels.
+//  assign_slots (one warp per segment): canonical slot of every (token, j) pair of the segment, token-major inside
+//  an expert, starting from run[e] = expert_offsets[e] + seg_base[seg][e] (segment_slots); writes c_map.
+//  quant_scatter (a flat grid of 3 CTAs per SM, one warp per token, tokens strided over all warps): each token row
+//  is NVFP4-quantised once per distinct expert input scale and written to its k slots (FP4 bytes + the two scale
+//  bytes of each 32-element unit), the same bytes as vLLM's per-slot quant of the shuffled rows
+//  (blink_moe.py:301-323, cutlass_moe.py:585-593). The grid does not depend on the segments, so every SM gets the
+//  same share of tokens in one wave.
 // ------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256, 3) permute_quant_kernel(
-    const __nv_bfloat16* __restrict__ a, const float* __restrict__ a1_gscale, const int* __restrict__ ids,
-    const int* __restrict__ seg_base, const int* __restrict__ eoff, const int* __restrict__ boff, int m, int H,
-    int E, int k, uint8_t* __restrict__ rep_fp4, uint8_t* __restrict__ lin_sf, int* __restrict__ c_map, int parts) {
+__global__ void __launch_bounds__(32) assign_slots_kernel(const int* __restrict__ ids, const int* __restrict__ seg_base,
+                                                         const int* __restrict__ eoff, int m, int E, int k,
+                                                         int* __restrict__ c_map) {
   __shared__ int run[kMaxExperts];
   __shared__ uint32_t mask[kMaxExperts];
-  __shared__ float gq[kMaxExperts];
   __shared__ int pos_s[kSegTokens * kMaxTopk];
   __shared__ short exp_s[kSegTokens * kMaxTopk];
-  __shared__ int sl_pos[8][kMaxTopk];           // per warp: the current token's slots
-  __shared__ float sl_g[8][kMaxTopk];
-  const int seg = blockIdx.x / parts;
-  const int part = blockIdx.x - seg * parts;
+  const int seg = blockIdx.x;
   const int64_t t0 = (int64_t)seg * kSegTokens;
   const int nt = (int)(kSegTokens < m - t0 ? (int64_t)kSegTokens : m - t0);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+  for (int e = threadIdx.x; e < E; e += 32) {
     run[e] = eoff[e] + seg_base[(int64_t)seg * E + e];
     mask[e] = 0u;
-    gq[e] = __fdiv_rn(1.0f, a1_gscale[e]);
   }
+  __syncwarp();
+  segment_slots(ids, t0, nt, k, E, run, mask, pos_s, exp_s, c_map);
+}
+
+constexpr int kQuantCtasPerSm = 3;
+
+// Lanes j < k put slot j and its input scale into the warp's shared slot table; lanes own 32-element units (16 FP4
+// bytes + 2 scale bytes per slot). A unit is quantised once per distinct input scale among the slots (once for a
+// uniform scale) with the bf16x2 quantiser, then stored to every slot: FP4 bytes into the slot's row, scale bytes
+// into the slot's row of the linear scale buffer (full-sector stores; the atoms are written from it by
+// swizzle_scales_kernel).
+__global__ void __launch_bounds__(256, kQuantCtasPerSm) quant_scatter_kernel(
+    const __nv_bfloat16* __restrict__ a, const float* __restrict__ a1_gscale, const int* __restrict__ ids,
+    const int* __restrict__ c_map, int m, int H, int E, int k, uint8_t* __restrict__ rep_fp4,
+    uint8_t* __restrict__ lin_sf) {
+  __shared__ float gq[kMaxExperts];
+  __shared__ int sl_pos[8][kMaxTopk];           // per warp: the current token's slots
+  __shared__ float sl_g[8][kMaxTopk];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) gq[e] = __fdiv_rn(1.0f, a1_gscale[e]);
   __syncthreads();
-  if (warp == 0) segment_slots(ids, t0, nt, k, E, run, mask, pos_s, exp_s, part == 0 ? c_map : nullptr);
-  __syncthreads();
-  // phase B: one warp per token (the segment's tokens strided over its parts' warps). Lanes j < k put slot j and its input scale into the warp's shared slot table; lanes
-  // own 32-element units (16 FP4 bytes + 2 scale bytes per slot). A unit is quantised once per distinct input scale
-  // among the slots (once for a uniform scale) with the bf16x2 quantiser, then stored to every slot: FP4 bytes into
-  // the slot's row, scale bytes into the slot's row of the linear scale buffer (full-sector stores; the atoms are
-  // written from it by swizzle_scales_kernel).
   const int units = H / 32;
   const int k16 = H / 16;
-  const int nwarps = blockDim.x >> 5;
-  for (int tl = warp + part * nwarps; tl < nt; tl += nwarps * parts) {
-    const int64_t t = t0 + tl;
-    const uint4* src = reinterpret_cast<const uint4*>(a + t * H);
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  for (int t = blockIdx.x * (blockDim.x >> 5) + warp; t < m; t += nwarps) {
+    const uint4* src = reinterpret_cast<const uint4*>(a + (int64_t)t * H);
     uint4 raw[kPermUnits][4];
 #pragma unroll
     for (int it = 0; it < kPermUnits; ++it) {
@@ -328,9 +334,10 @@ __global__ void __launch_bounds__(256, 3) permute_quant_kernel(
       }
     }
     if (lane < k) {
-      const int e = exp_s[tl * k + lane];
-      sl_pos[warp][lane] = e >= 0 ? pos_s[tl * k + lane] : -1;
-      sl_g[warp][lane] = e >= 0 ? gq[e] : 0.0f;
+      const int64_t pair = (int64_t)t * k + lane;
+      const int pos = c_map[pair];   // -1 for an id outside [0, E)
+      sl_pos[warp][lane] = pos;
+      sl_g[warp][lane] = pos >= 0 ? gq[ids[pair]] : 0.0f;
     }
     __syncwarp();
 #pragma unroll
@@ -441,10 +448,29 @@ __global__ void __launch_bounds__(256) swizzle_scales_kernel(const uint8_t* __re
   const int rows = min(128, counts[e] - mt * 128);
   const int k64 = H / 64;             // 4-byte words per row
   const int stride = k64 + 1;         // odd: conflict-free column reads
-  const uint32_t* src = reinterpret_cast<const uint32_t*>(lin + ((int64_t)eoff[e] + mt * 128) * (H / 16));
-  for (int i = threadIdx.x; i < 128 * k64; i += blockDim.x) {
-    const int r = i / k64, c = i - r * k64;
-    tile[r * stride + c] = r < rows ? __ldg(src + i) : 0u;
+  // vector loads: 16 bytes when a row of H/16 scale bytes is a multiple of 16 (H % 256 == 0), else 8 bytes (H is a
+  // multiple of 128); stored as words at the odd stride
+  const uint8_t* src = lin + ((int64_t)eoff[e] + mt * 128) * (H / 16);
+  if (k64 % 4 == 0) {
+    const int k256 = k64 / 4;
+    for (int i = threadIdx.x; i < 128 * k256; i += blockDim.x) {
+      const int r = i / k256, c = (i - r * k256) * 4;
+      const uint4 v = r < rows ? __ldg(reinterpret_cast<const uint4*>(src) + i) : make_uint4(0u, 0u, 0u, 0u);
+      uint32_t* d = tile + r * stride + c;
+      d[0] = v.x;
+      d[1] = v.y;
+      d[2] = v.z;
+      d[3] = v.w;
+    }
+  } else {
+    const int k128 = k64 / 2;
+    for (int i = threadIdx.x; i < 128 * k128; i += blockDim.x) {
+      const int r = i / k128, c = (i - r * k128) * 2;
+      const uint2 v = r < rows ? __ldg(reinterpret_cast<const uint2*>(src) + i) : make_uint2(0u, 0u);
+      uint32_t* d = tile + r * stride + c;
+      d[0] = v.x;
+      d[1] = v.y;
+    }
   }
   __syncthreads();
   uint4* dst = reinterpret_cast<uint4*>(sf + (int64_t)gm * k64 * 512);
@@ -696,16 +722,16 @@ int launch_plan(const int* seg_counts, int nseg, int E, int* seg_base, int* coun
 int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const int* seg_base,
                          const int* eoff, const int* boff, int m, int H, int E, int k, uint8_t* rep_fp4,
                          uint8_t* lin_sf, int* c_map, cudaStream_t s) {
+  (void)boff;
+  if (m == 0) return 0;
   const int nseg = (int)ceil_div64(m, kSegTokens);
-  // segments fewer than two per SM (small batches): split each segment's tokens over more CTAs
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int parts = nseg >= 2 * sms ? 1 : (int)ceil_div64(2 * sms, nseg);
-  parts = parts < 1 ? 1 : parts > 16 ? 16 : parts;
-  if (nseg > 0)
-    permute_quant_kernel<<<nseg * parts, 256, 0, s>>>(a, a1_gscale, ids, seg_base, eoff, boff, m, H, E, k, rep_fp4,
-                                                      lin_sf, c_map, parts);
+  assign_slots_kernel<<<nseg, 32, 0, s>>>(ids, seg_base, eoff, m, E, k, c_map);
+  const int64_t want = ceil_div64(m, 8), cap = (int64_t)kQuantCtasPerSm * sms;
+  quant_scatter_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, s>>>(a, a1_gscale, ids, c_map, m, H, E, k,
+                                                                          rep_fp4, lin_sf);
   return 0;
 }
 

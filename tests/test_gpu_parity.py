@@ -146,9 +146,12 @@ def _plan_permute(R, c):
     return st, w, ids
 
 
-@pytest.mark.parametrize("T,skew", [(1, None), (130, None), (389, None), (1024, 1.0), (16, 1.0)])
-def test_plan_and_permute_bit_exact(R, T, skew):
-    c = make_case(T, 256, 64, 4, 256, "silu", seed=T, skew=skew)
+# T = 5000 and 4000: more tokens than the quantise kernel's warps, so each warp takes several; H = 1152: scale rows
+# of 72 bytes (not a multiple of 16)
+@pytest.mark.parametrize("T,H,skew", [(1, 256, None), (130, 256, None), (389, 256, None), (1024, 256, 1.0),
+                                      (16, 256, 1.0), (5000, 1152, None), (4000, 256, 1.0)])
+def test_plan_and_permute_bit_exact(R, T, H, skew):
+    c = make_case(T, H, 64, 4, 256, "silu", seed=T, skew=skew)
     st, w, ids = _plan_permute(R, c)
     n = c["np"]
     wr, idr = O.route(n["logits"], c["k"])
