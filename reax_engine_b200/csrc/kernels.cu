@@ -87,8 +87,49 @@ __global__ void __launch_bounds__(128) route_quad_kernel(const float* __restrict
   const int stride = E + ((4 - E) % 32 + 32) % 32;
   const int64_t t0 = (int64_t)blockIdx.x * kRouteTokens;
   const int nt = (int)((T - t0) < kRouteTokens ? (T - t0) : kRouteTokens);
-  for (int tl = 0; tl < nt; ++tl)
-    for (int e = threadIdx.x; e < E; e += blockDim.x) tile[tl * stride + e] = logits[(t0 + tl) * E + e];
+  {
+    // the CTA's rows are nt * E contiguous floats: every thread issues all its loads before its first store, so
+    // the loads' DRAM latency is paid once per CTA, not once per row
+    constexpr int U = 8;
+    const float* src = logits + t0 * E;
+    const int total = nt * E;
+    if ((E & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+      const int n4 = total >> 2;   // stride and E are multiples of 4: a float4 never straddles two rows
+      for (int base = threadIdx.x; base < n4; base += blockDim.x * U) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * blockDim.x;
+          if (i < n4) v[u] = __ldg(reinterpret_cast<const float4*>(src) + i);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * blockDim.x;
+          if (i < n4) {
+            const int tl = (4 * i) / E, e = 4 * i - tl * E;
+            *reinterpret_cast<float4*>(tile + tl * stride + e) = v[u];
+          }
+        }
+      }
+    } else {
+      for (int base = threadIdx.x; base < total; base += blockDim.x * U) {
+        float v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * blockDim.x;
+          if (i < total) v[u] = __ldg(src + i);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = base + u * blockDim.x;
+          if (i < total) {
+            const int tl = i / E;
+            tile[tl * stride + (i - tl * E)] = v[u];
+          }
+        }
+      }
+    }
+  }
   __syncthreads();
   const int tl = threadIdx.x >> 2, q = threadIdx.x & 3;
   const bool active = tl < nt;

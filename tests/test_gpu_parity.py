@@ -54,14 +54,20 @@ def test_route_ties_go_to_lower_expert(R):
     np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-7)
 
 
-@pytest.mark.parametrize("T,E,k,ties", [(40000, 128, 8, False), (40000, 128, 8, True), (20000, 256, 16, False),
-                                        (19000, 64, 4, True)])
-def test_route_large_batch_kernel_bit_exact(R, T, E, k, ties):
+# (19500, 62, 6): rows of 62 floats, and the shifted view: a base 4 bytes past a 16-byte boundary -- both stage the
+# logits with scalar loads instead of 16-byte ones
+@pytest.mark.parametrize("T,E,k,ties,shift", [(40000, 128, 8, False, False), (40000, 128, 8, True, False),
+                                              (20000, 256, 16, False, False), (19000, 64, 4, True, False),
+                                              (19500, 62, 6, False, False), (19000, 128, 8, False, True)])
+def test_route_large_batch_kernel_bit_exact(R, T, E, k, ties, shift):
     """Batches of >= 4 x 148 x 32 tokens route with four lanes per token (route_quad_kernel); smaller ones with a
     warp per token. Both give the same ids and weights bit for bit (the chunks below take the warp kernel), and the
     oracle's ids."""
     g = torch.Generator().manual_seed(T + E)
     logits = (torch.randint(-3, 3, (T, E), generator=g).float() if ties else torch.randn(T, E, generator=g)).cuda()
+    if shift:
+        logits = torch.cat([torch.zeros(1, device="cuda"), logits.flatten()])[1:].view(T, E)
+        assert logits.data_ptr() % 16 == 4
     scale = (torch.rand(E, generator=g) + 0.5).cuda()
     w, ids = R.route(None, logits, k, True, scale)
     parts = [R.route(None, logits[i:i + 4096].contiguous(), k, True, scale) for i in range(0, T, 4096)]
