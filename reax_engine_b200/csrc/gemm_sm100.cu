@@ -9,9 +9,11 @@
 //                 expert's intermediate scale (engine/fp4.py numerics) -> FP4 rows + 128x4 scale atoms.
 //
 // Design (one CTA per SM, persistent). Work is handed out round-robin over the CTAs: one m-tile (expert, 128 routed
-// rows) with all its n-tiles (256 output columns each; a narrower last n-tile of 128 when N % 256 == 128) per item;
-// for a small batch (fewer than two m-tiles per CTA) one (m-tile, n-tile) unit per item instead, so that every SM
-// takes part in reading the weights (measured at 1024 skewed tokens: 0.378 -> 0.215 ms per layer).
+// rows) with all its n-tiles (256 output columns each; a narrower last n-tile of 128 when N % 256 == 128) per item,
+// in full waves of one m-tile per CTA; the m-tiles left after the last full wave go out as single (m-tile, n-tile)
+// units, so that the kernel's tail is a fraction of an m-tile on every CTA instead of a whole m-tile on some. A small
+// batch (fewer than two m-tiles per CTA) is all units, so that every SM takes part in reading the weights (measured
+// at 1024 skewed tokens: 0.378 -> 0.215 ms per layer).
 //   warp 0      TMA producer, into a 4-deep ring of 54 KiB stages: A (routed FP4 rows, 128 x 256 K) and B (expert
 //               weights, 256 x 256 K) by 2D TMA with 128-byte swizzle, plus the stage's scale atoms as they lie in
 //               memory (engine/fp4.py 128x4 atoms, 512 B per 128 rows x 64-element k-chunk) by 1D bulk copies: the
@@ -266,11 +268,15 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
   const uint32_t tmem = *tmem_holder;
   const int n_tiles = p.n_tiles;
   const int total_mtiles = s_tp[E];
-  // Work items: with at least two m-tiles per CTA, one m-tile with all its n-tiles (the CTA's B reads stay on one
-  // expert); with fewer (a small batch), one (m-tile, n-tile) unit, so that every SM takes part in the weight reads.
-  const bool by_unit = total_mtiles < 2 * (int)gridDim.x;
-  const int items = by_unit ? total_mtiles * n_tiles : total_mtiles;
-  const int per_item = by_unit ? 1 : n_tiles;
+  // Work items, handed out round-robin (so that the CTAs in flight share a few experts' weights in L2): whole
+  // m-tiles with all their n-tiles in full waves of gridDim.x, then the remaining m-tiles as single (m-tile, n-tile)
+  // units spread over all CTAs, so that no CTA runs a whole extra m-tile while the others idle. A small batch (fewer
+  // than two m-tiles per CTA) is all units, so that every SM takes part in the weight reads.
+  const int whole = total_mtiles < 2 * (int)gridDim.x ? 0 : total_mtiles / (int)gridDim.x * (int)gridDim.x;
+  const int items = whole + (total_mtiles - whole) * n_tiles;
+  auto item_mtile = [&](int u) { return u < whole ? u : whole + (u - whole) / n_tiles; };
+  auto item_nt0 = [&](int u) { return u < whole ? 0 : (u - whole) % n_tiles; };
+  auto item_nts = [&](int u) { return u < whole ? n_tiles : 1; };
   const int k_chunks = p.k_chunks;
   const int k_stages = (k_chunks + KPS - 1) / KPS;
   // the n-tile's second 128-row block of B exists unless it is the narrow last tile
@@ -287,11 +293,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         int a_fills[RA_SLICES] = {0, 0, 0};
         bool ok = true;
         for (int u = blockIdx.x, it = 0; u < items && ok; u += gridDim.x, ++it) {
-          const int gm = by_unit ? u / n_tiles : u;
-          const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
+          const MTile M = decode_mtile(item_mtile(u), E, s_tp, s_cnt, s_eoff, s_boff);
           const uint8_t* sfa = p.sfA + (size_t)M.sfblk * k_chunks * SF_ATOM;
-          const int nt_first = by_unit ? u % n_tiles : 0;
-          for (int nt = nt_first, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
+          const int nt_first = item_nt0(u);
+          for (int nt = nt_first, nt_end = nt + item_nts(u); nt < nt_end && ok; ++nt) {
             const int brow = M.e * p.N + nt * BN;
             const bool b1 = has_block1(nt);
             const uint8_t* sfb0 = p.sfB + ((size_t)M.e * p.n_blocks + 2 * nt) * k_chunks * SF_ATOM;
@@ -351,7 +356,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         uint32_t acc_phase = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
-          for (int nt = by_unit ? u % n_tiles : 0, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
+          for (int nt = item_nt0(u), nt_end = nt + item_nts(u); nt < nt_end && ok; ++nt) {
             const uint32_t idesc = idesc_for(nt == n_tiles - 1 ? p.tail_n : BN);
             if (!wait_bounded(smem_u32(acce), acc_phase ^ 1u, abort_flag, p.status, p.timeout_ns)) {
               ok = false;
@@ -398,8 +403,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
       bool ok = true;
       const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
       for (int u = blockIdx.x, it = 0; u < items && ok; u += gridDim.x, ++it) {
-        const int nt_first = by_unit ? u % n_tiles : 0;
-        for (int nt = nt_first, nt_end = nt + per_item; nt < nt_end && ok; ++nt) {
+        const int nt_first = item_nt0(u);
+        for (int nt = nt_first, nt_end = nt + item_nts(u); nt < nt_end && ok; ++nt) {
           const bool b1 = has_block1(nt);
           for (int ks = 0; ks < k_stages; ++ks, ++n) {
             const int stage = (int)(n % STAGES);
@@ -447,8 +452,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
     uint32_t acc_phase = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
-      const int gm = by_unit ? u / n_tiles : u;
-      const MTile M = decode_mtile(gm, E, s_tp, s_cnt, s_eoff, s_boff);
+      const MTile M = decode_mtile(item_mtile(u), E, s_tp, s_cnt, s_eoff, s_boff);
       const int64_t row = (int64_t)M.row0 + r;
       // expert-parallel receiver: a slot that is its record's only local pair is written as the finished row
       uint64_t direct = 0ull;
@@ -459,7 +463,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
           wdir = bf16r(p.direct_w[row]);
         }
       }
-      for (int nt = by_unit ? u % n_tiles : 0, nt_end = nt + per_item; nt < nt_end; ++nt) {
+      for (int nt = item_nt0(u), nt_end = nt + item_nts(u); nt < nt_end; ++nt) {
         const int un = (nt == n_tiles - 1) ? p.tail_n : BN;
         if (!wait_bounded(smem_u32(accf), acc_phase, abort_flag, p.status, p.timeout_ns)) {
           ok = false;
