@@ -104,8 +104,8 @@ __host__ __device__ constexpr uint32_t idesc_for(int n) {
 }
 
 struct Params {
-  CUtensorMap tmA;  // [slots, K/2] u8, box 128 x 128 rows, 128B swizzle
-  CUtensorMap tmB;  // [E*N, K/2] u8, same box
+  CUtensorMap tmA;  // [slots, K/2] u8, box 128 bytes x 128 rows, 128B swizzle
+  CUtensorMap tmB;  // [E*N, K/2] u8, box 128 bytes x 256 rows, 128B swizzle
   const uint8_t* sfA;   // A scale atoms [row blocks][k_chunks][512] (blockscale_offsets rows)
   const uint8_t* sfB;   // B scale atoms as engine/fp4.py lays them out: [E][N/128][k_chunks][512]
   const float* alphas;
@@ -158,45 +158,89 @@ __device__ __forceinline__ MTile decode_mtile(int gm, int E, const int* s_tp, co
   return r;
 }
 
-// tanh from its definition, tanh(y) = 1 - 2 / (1 + e^(2y)), with the hardware exp2 and reciprocal approximations
-// (relative error ~1e-7 away from 0, absolute ~1e-7 near 0); saturates correctly at +-1.
-__device__ __forceinline__ float tanh_fast(float y) {
-  const float e = exp2f(2.8853900817779268f * y);  // e^(2y)
-  return 1.0f - __fdividef(2.0f, 1.0f + e);
+// Two fp32 lanes in one 64-bit register, for Blackwell's packed fp32x2 instructions (each lane rounds exactly as
+// the scalar instruction would).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
 }
-// GELU with the tanh approximation: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) (blink_moegemm.cu:349-355).
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float kBeta = 0.7978845608028654f, kKappa = 0.044715f;
-  const float inner = kBeta * fmaf(kKappa * x, x * x, x);
-  return 0.5f * x * (1.0f + tanh_fast(inner));
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
-__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
-
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// the hardware base-2 exponential and reciprocal approximations (ex2.approx, rcp.approx; about 2^-22 relative)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 1 / (1 + 2^z) on both lanes
+__device__ __forceinline__ uint64_t f2_rcp_one_plus_ex2(uint64_t z) {
+  float zl, zh, dl, dh;
+  f2_unpack(z, zl, zh);
+  f2_unpack(f2_add(f2_pack(ex2_approx(zl), ex2_approx(zh)), f2_pack(1.0f, 1.0f)), dl, dh);
+  return f2_pack(rcp_approx(dl), rcp_approx(dh));
+}
+// The gate activation on two lanes, from the definitions:
+//   GELU with the tanh approximation (blink_moegemm.cu:349-355): 0.5 x (1 + tanh(y)), y = sqrt(2/pi) (x + 0.044715 x^3).
+//     With tanh(y) = 1 - 2 r, r = 1 / (1 + e^(2y)): 0.5 x (1 + tanh(y)) = x - x r, and e^(2y) = 2^z with
+//     z = x (C + 0.044715 C x^2), C = 2 sqrt(2/pi) log2(e). Saturates to x (r = 0) and to 0 (r = 1).
+//   SiLU: x / (1 + e^(-x)) = x r, r = 1 / (1 + 2^(-x log2(e))).
 template <int ACT>
-__device__ __forceinline__ float act_fn(float x) {
-  if constexpr (ACT == REAXMOE_ACT_GELU_TANH) return gelu_tanh(x);
-  else return silu(x);
+__device__ __forceinline__ uint64_t act2(uint64_t x) {
+  if constexpr (ACT == REAXMOE_ACT_GELU_TANH) {
+    constexpr float kC = 2.302208185195923f;       // 2 sqrt(2/pi) log2(e)
+    constexpr float kKC = 0.10294324159622192f;    // 0.044715 C
+    const uint64_t z = f2_mul(x, f2_fma(f2_pack(kKC, kKC), f2_mul(x, x), f2_pack(kC, kC)));
+    return f2_fma(x ^ 0x8000000080000000ull, f2_rcp_one_plus_ex2(z), x);
+  } else {
+    constexpr float kNL = -1.4426950216293335f;    // -log2(e)
+    return f2_mul(x, f2_rcp_one_plus_ex2(f2_mul(x, f2_pack(kNL, kNL))));
+  }
 }
 
 // Fused w13 epilogue for one thread: 32 gate and 32 up accumulators of one row -> 16 packed FP4 bytes + 2 scale
 // bytes. gate/up = bf16(alpha * acc); h = bf16(bf16(act(gate)) * up) (a bf16 product of two bf16 values rounds
 // exactly like the fp32 product rounded to bf16); NVFP4 quantisation of h with engine/fp4.py numerics, by the bf16x2
-// quantiser (h is exactly bf16).
+// quantiser (h is exactly bf16). The fp32 work runs on lane pairs (fp32x2 instructions).
 template <int ACT>
 __device__ __forceinline__ uint32_t act_quant32(const uint32_t (&x0)[32], const uint32_t (&x1)[32], float alpha,
                                                 float g, uint32_t (&w)[4]) {
+  const uint64_t al = f2_pack(alpha, alpha);
   uint32_t sbytes = 0u;
 #pragma unroll
   for (int b = 0; b < 2; ++b) {
     uint32_t hw[8];
 #pragma unroll
     for (int i = 0; i < 16; i += 2) {
-      const __nv_bfloat162 gb = __floats2bfloat162_rn(alpha * __uint_as_float(x0[16 * b + i]),
-                                                      alpha * __uint_as_float(x0[16 * b + i + 1]));
-      const __nv_bfloat162 ub = __floats2bfloat162_rn(alpha * __uint_as_float(x1[16 * b + i]),
-                                                      alpha * __uint_as_float(x1[16 * b + i + 1]));
+      float gl, gh, ul, uh, al_, ah;
+      f2_unpack(f2_mul(f2_pack(__uint_as_float(x0[16 * b + i]), __uint_as_float(x0[16 * b + i + 1])), al), gl, gh);
+      f2_unpack(f2_mul(f2_pack(__uint_as_float(x1[16 * b + i]), __uint_as_float(x1[16 * b + i + 1])), al), ul, uh);
+      const __nv_bfloat162 gb = __floats2bfloat162_rn(gl, gh);
+      const __nv_bfloat162 ub = __floats2bfloat162_rn(ul, uh);
       const float2 gf = __bfloat1622float2(gb);
-      const __nv_bfloat162 ab = __floats2bfloat162_rn(act_fn<ACT>(gf.x), act_fn<ACT>(gf.y));
+      f2_unpack(act2<ACT>(f2_pack(gf.x, gf.y)), al_, ah);
+      const __nv_bfloat162 ab = __floats2bfloat162_rn(al_, ah);
       const __nv_bfloat162 h2 = __hmul2(ab, ub);
       hw[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
     }

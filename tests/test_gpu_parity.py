@@ -228,7 +228,10 @@ def test_gemm_w2_matches_oracle(R, shape):
 
 
 @pytest.mark.parametrize("act", ["gelu_tanh", "silu"])
-@pytest.mark.parametrize("shape", [(256, 256, 8, 2, 256), (300, 2816, 128, 8, 704), (20000, 512, 8, 2, 320)])
+# (20000, 1024, 7, 2, 704): K too long for a resident A, more than two m-tiles per CTA, experts with odd m-tile
+# counts, a narrow last n-tile and the tail units
+@pytest.mark.parametrize("shape", [(256, 256, 8, 2, 256), (300, 2816, 128, 8, 704), (20000, 512, 8, 2, 320),
+                                   (20000, 1024, 7, 2, 704)])
 def test_gemm_w13_fused_matches_oracle(R, act, shape):
     T, H, E, k, inter = shape
     c = make_case(T, H, E, k, inter, act, seed=31)
