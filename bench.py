@@ -34,7 +34,7 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 METRIC = "MoE-layer tokens/s (NVFP4 26B-A4B-shaped layer)"
-E2E_CHUNK = 4096   # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
+E2E_CHUNK = 12288  # tokens per chunk of the host-resident e2e pipeline (HostStreamedMoE)
 DECISION_PROMPTS, DECISION_WARMUP, DECISION_STEPS = 64, 2, 3   # config 3 decision forward
 EP_SM_RESERVE = 0   # SMs the persistent kernels leave to the NCCL exchanges in expert-parallel runs
 EP_E2E_CHUNKS = 4   # token parts per rank in the expert-parallel end-to-end pipeline (HostStreamedEP)
@@ -501,6 +501,32 @@ def run_ours(args, wl: dict) -> None:
         if world > 1:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
         e2e_value = world * T * args.steps / (float(ems.item()) / 1000.0)
+        # the same step's copies alone, inputs in and output out on two streams at once: the PCIe bound of e2e
+        xd, lgd = torch.empty_like(inp["x"]), torch.empty_like(inp["logits"])
+        od = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+        def copy_steps(n):
+            c0 = torch.cuda.Event(enable_timing=True)
+            c1 = torch.cuda.Event(enable_timing=True)
+            c0.record(s)
+            s_in.wait_event(c0)
+            s_out.wait_event(c0)
+            for _ in range(n):
+                with torch.cuda.stream(s_in):
+                    xd.copy_(x_h, non_blocking=True)
+                    lgd.copy_(lg_h, non_blocking=True)
+                with torch.cuda.stream(s_out):
+                    out_h.copy_(od, non_blocking=True)
+            s.wait_stream(s_in)
+            s.wait_stream(s_out)
+            c1.record(s)
+            torch.cuda.synchronize(dev)
+            return c0.elapsed_time(c1)
+
+        copy_steps(2)
+        copy_bound = T * args.steps / (copy_steps(args.steps) / 1000.0)
+        del xd, lgd, od
 
     # ---- the fused Gemma-4 router + top-k (reax_engine_b200.router_topk) on the same x: outside the step, whose
     # metric starts from router logits; one launch at a time, L2 flushed before each
@@ -577,7 +603,10 @@ def run_ours(args, wl: dict) -> None:
                     value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * H * 2 + T * E * 4,
                     d2h_bytes_per_step=T * H * 2,
                     api=f"reax_engine_b200.HostStreamedMoE: pinned host x + logits in, output out, {E2E_CHUNK}-token "
-                        "chunks with the copies overlapped with route + run_moe_nvfp4"),
+                        "chunks with the copies overlapped with route + run_moe_nvfp4",
+                    copy_bound=copy_bound, frac_of_copy_bound=e2e_value / copy_bound,
+                    copy_bound_note="the same step's host<->device copies alone on this box (both directions in "
+                                    "flight, no layer): the PCIe limit of e2e"),
                 gpu_launches=launches_per_step * args.steps, roofline=roof, layer=layer, kernels=kernels,
                 router_topk=router, decision=decision, other_configs=extra,
                 cpu_baseline=cpu, clocks=clk.summary())
