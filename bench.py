@@ -341,7 +341,7 @@ def measure_workload(name: str, dev, steps: int, warmup: int) -> dict:
     wl = workload(name)
     inp = build_inputs(wl, dev)
     T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
-    st = R.Stages(T, H, I, E, k, wl["act"], dev)
+    st = R.Stages(T, H, I, E, k, wl["act"], dev, gather=True)
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     s = torch.cuda.current_stream(dev)
     names = ["route", "plan", "permute_quant", "gemm_w13", "gemm_w2", "combine"]
@@ -421,7 +421,8 @@ def run_ours(args, wl: dict) -> None:
     torch.cuda.set_device(dev)
     inp = build_inputs(wl, dev, seed=rank)
     T, H, E, k, I = wl["T"], wl["H"], wl["E"], wl["k"], wl["I"]
-    st = R.Stages(T, H, I, E, k, wl["act"], dev)
+    # the layer's stages as reaxmoe_forward runs them (gather layout of the w13 A operand), each on its own event
+    st = R.Stages(T, H, I, E, k, wl["act"], dev, gather=True)
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     s = torch.cuda.current_stream(dev)
 
@@ -565,7 +566,9 @@ def run_ours(args, wl: dict) -> None:
     fp4_peak = 4.0 * peaks["bf16"]
     flops = {"gemm_w13": 2.0 * slots * H * 2 * I, "gemm_w2": 2.0 * slots * I * H}
     hbm = {"route": T * E * 4 + T * k * 8, "plan": T * k * 4,
-           "permute_quant": T * H * 2 + slots * (H // 2 + H // 16) + slots * 4,
+           # x read once; token-major FP4 rows written once; the slot-ordered scale atoms; c_map and the slot ->
+           # token map (the gather layout of the w13 A operand)
+           "permute_quant": T * H * 2 + T * (H // 2) + slots * (H // 16) + slots * 8,
            "combine": slots * H * 2 + slots * 8 + T * H * 2}
     kernels = {}
     for n in names:

@@ -99,7 +99,9 @@ typedef struct reaxmoe_forward_args {
 size_t reaxmoe_workspace_size(const reaxmoe_problem* p);
 
 /* The whole layer: plan -> permute_quant -> gemm_w13 -> gemm_w2 -> combine
- * (run_cutlass_moe_fp4, cutlass_moe.py:481-664; blink_moe.py:434-567). */
+ * (run_cutlass_moe_fp4, cutlass_moe.py:481-664; blink_moe.py:434-567). When every expert has the same input scale
+ * (a1_gscale), each token row is quantised once and w13 reads its A rows through the slot -> token map (the
+ * gather layout of reaxmoe_permute_quant with rep_fp4 == NULL); otherwise the rows are replicated per slot. */
 int reaxmoe_forward(const reaxmoe_forward_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
 /* The same layer on token rows quantised upstream (reaxmoe_rmsnorm_nvfp4; the quant-once path of
@@ -172,14 +174,19 @@ int reaxmoe_plan(const reaxmoe_problem* p, const int32_t* topk_ids, void* worksp
 
 /* Quantise every token row once per distinct expert scale and scatter it to its top-k slots (FP4 rows +
  * swizzled scales) in the canonical order; writes c_map[t*topk + j] = slot (blink_moe.py:301-323). Needs the
- * plan of the same workspace. rep_fp4 [tokens*topk, hidden/2]; rep_sf scale atoms over blockscale_offsets. */
+ * plan of the same workspace. rep_fp4 [tokens*topk, hidden/2]; rep_sf scale atoms over blockscale_offsets.
+ * rep_fp4 == NULL selects the gather layout (the reference's gather-A path, blink_moegemm.cu:532-647): when every
+ * expert has the same a1_gscale, each token row is quantised once into the workspace, token-major, with a
+ * slot -> token map beside it; when the scales differ, the per-slot rows go to the workspace instead. rep_sf and
+ * c_map are written either way. reaxmoe_gemm_w13 with rep_fp4 == NULL then reads the layout this call chose. */
 int reaxmoe_permute_quant(const reaxmoe_problem* p, const void* a, const float* a1_gscale, const int32_t* topk_ids,
                           void* workspace, size_t workspace_bytes, void* rep_fp4, void* rep_sf, int32_t* c_map,
                           void* stream);
 
 /* Grouped NVFP4 GEMM w13 with the fused activation(gate) * up and NVFP4 re-quantisation epilogue
  * (blink_moegemm.cu:472-934 MODE 1). Needs the plan of the same workspace. w1_fp4 is interleaved
- * (reaxmoe_prepack_w13) with its scale atoms. hidden <= 3072. */
+ * (reaxmoe_prepack_w13) with its scale atoms. hidden <= 3072. rep_fp4 == NULL: A rows from the gather layout that
+ * reaxmoe_permute_quant (rep_fp4 == NULL) left in the same workspace. */
 int reaxmoe_gemm_w13(const reaxmoe_problem* p, const void* rep_fp4, const void* rep_sf, const void* w1_fp4,
                      const void* w1_sf, const float* w1_alphas, const float* a2_gscale, void* workspace,
                      size_t workspace_bytes, void* int_fp4, void* int_sf, void* stream);

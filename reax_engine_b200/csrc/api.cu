@@ -70,7 +70,7 @@ int check_problem_shape(const reaxmoe_problem* p) { return check_problem(p); }
 // Workspace regions, each 256-byte aligned.
 struct Layout {
   size_t status, seg_counts, seg_base, counts, eoff, boff, tile_prefix, c_map, rep_fp4, lin_sf, rep_sf, int_fp4,
-      int_sf, c3, total;
+      int_sf, c3, tok_fp4, tok_sf, row_token, ga_flag, total;
 };
 
 static size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -101,6 +101,10 @@ static Layout layout(const reaxmoe_problem* p) {
   L.int_fp4 = take((size_t)slots * (I / 2));
   L.int_sf = take((size_t)sfblk * (I / 64) * 512);
   L.c3 = take((size_t)slots * H * 2);
+  L.tok_fp4 = take((size_t)m * (H / 2));
+  L.tok_sf = take((size_t)m * (H / 16));
+  L.row_token = take((size_t)slots * 4);
+  L.ga_flag = take(64);
   L.total = off;
   return L;
 }
@@ -120,6 +124,7 @@ struct WS {
   uint8_t* int_fp4;
   uint8_t* int_sf;
   __nv_bfloat16* c3;
+  GatherRows ga;    // the gather layout of the w13 A operand (token-major rows, slot -> token map, layout flag)
 };
 
 static WS carve(void* ws, const Layout& L) {
@@ -139,6 +144,10 @@ static WS carve(void* ws, const Layout& L) {
   w.int_fp4 = b + L.int_fp4;
   w.int_sf = b + L.int_sf;
   w.c3 = reinterpret_cast<__nv_bfloat16*>(b + L.c3);
+  w.ga.tok_fp4 = b + L.tok_fp4;
+  w.ga.tok_sf = b + L.tok_sf;
+  w.ga.row_token = reinterpret_cast<int*>(b + L.row_token);
+  w.ga.flag = reinterpret_cast<int*>(b + L.ga_flag);
   return w;
 }
 
@@ -255,6 +264,19 @@ static GemmLaunch w13_launch(const reaxmoe_problem* p, const WS& w, const void* 
   g.q_gscale = a2_gscale;
   g.status = w.status;
   g.timeout_ns = device_timeout_ns();
+  return g;
+}
+
+// The w13 launch of the gather layout: A rows through the workspace's slot -> token map, from tok (token-major
+// [tokens, hidden/2]) when the permute stage wrote that layout, else from the per-slot rows rep.
+static GemmLaunch w13_gather_launch(const reaxmoe_problem* p, const WS& w, const void* tok, const void* rep,
+                                    const void* rep_sf, const void* w1, const void* w1_sf, const float* alphas,
+                                    const float* a2_gscale, void* int_fp4, void* int_sf) {
+  GemmLaunch g = w13_launch(p, w, rep, rep_sf, w1, w1_sf, alphas, a2_gscale, int_fp4, int_sf);
+  g.a_tok = tok;
+  g.row_token = w.ga.row_token;
+  g.ga_flag = w.ga.flag;
+  g.tokens = p->tokens;
   return g;
 }
 
@@ -446,12 +468,21 @@ int reaxmoe_permute_quant(const reaxmoe_problem* p, const void* a, const float* 
   Layout L;
   if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
   if (p->tokens == 0) return 0;
-  if (!a || !a1_gscale || !topk_ids || !rep_fp4 || !rep_sf || !c_map)
+  if (!a || !a1_gscale || !topk_ids || !rep_sf || !c_map)
     return fail(REAXMOE_ERR_NULL, "permute_quant: NULL pointer");
   if (!aligned16(a) || !aligned16(rep_fp4) || !aligned16(rep_sf))
     return fail(REAXMOE_ERR_MISALIGNED, "permute_quant: a, rep_fp4 and rep_sf must be 16-byte aligned");
   const WS w = carve(workspace, L);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rep_fp4 == nullptr) {
+    // gather layout, kept in the workspace for reaxmoe_gemm_w13 with rep_fp4 == NULL
+    launch_permute_quant(static_cast<const __nv_bfloat16*>(a), a1_gscale, topk_ids, w.seg_base, w.eoff, w.boff,
+                         p->tokens, p->hidden, p->experts, p->topk, w.rep_fp4, w.lin_sf, c_map, s, &w.ga);
+    launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
+                          (int64_t)p->tokens * p->topk, static_cast<uint8_t*>(rep_sf), s, w.ga.row_token, w.ga.flag,
+                          w.ga.tok_sf, p->tokens);
+    return cuda_check("permute_quant");
+  }
   launch_permute_quant(static_cast<const __nv_bfloat16*>(a), a1_gscale, topk_ids, w.seg_base, w.eoff, w.boff,
                        p->tokens, p->hidden, p->experts, p->topk, static_cast<uint8_t*>(rep_fp4), w.lin_sf, c_map, s);
   launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
@@ -467,12 +498,17 @@ int reaxmoe_gemm_w13(const reaxmoe_problem* p, const void* rep_fp4, const void* 
   Layout L;
   if ((rc = check_ws(p, workspace, workspace_bytes, &L))) return rc;
   if (p->tokens == 0) return 0;
-  if (!rep_fp4 || !rep_sf || !w1_fp4 || !w1_sf || !w1_alphas || !a2_gscale || !int_fp4 || !int_sf)
+  if (!rep_sf || !w1_fp4 || !w1_sf || !w1_alphas || !a2_gscale || !int_fp4 || !int_sf)
     return fail(REAXMOE_ERR_NULL, "gemm_w13: NULL pointer");
   if (!aligned16(rep_fp4) || !aligned16(rep_sf) || !aligned16(w1_fp4) || !aligned16(w1_sf) || !aligned16(int_fp4))
     return fail(REAXMOE_ERR_MISALIGNED, "gemm_w13: operands must be 16-byte aligned");
   const WS w = carve(workspace, L);
-  const GemmLaunch g = w13_launch(p, w, rep_fp4, rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, int_fp4, int_sf);
+  // rep_fp4 == NULL: the gather layout that reaxmoe_permute_quant left in this workspace
+  const GemmLaunch g =
+      rep_fp4 != nullptr
+          ? w13_launch(p, w, rep_fp4, rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, int_fp4, int_sf)
+          : w13_gather_launch(p, w, w.ga.tok_fp4, w.rep_fp4, rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, int_fp4,
+                              int_sf);
   if ((rc = launch_grouped_gemm(g, num_sms(), static_cast<cudaStream_t>(stream))))
     return fail(rc, "gemm_w13 launch failed: %s", cudaGetErrorString(cudaPeekAtLastError()));
   return cuda_check("gemm_w13");
@@ -525,14 +561,17 @@ int reaxmoe_forward(const reaxmoe_forward_args* args, void* workspace, size_t wo
   const WS w = carve(workspace, L);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = do_plan(p, args->topk_ids, w, nullptr, nullptr, s))) return rc;
+  // gather layout: token rows quantised once when the experts share their input scale, else per slot
   launch_permute_quant(static_cast<const __nv_bfloat16*>(args->a), args->a1_gscale, args->topk_ids, w.seg_base,
-                       w.eoff, w.boff, p->tokens, p->hidden, p->experts, p->topk, w.rep_fp4, w.lin_sf, w.c_map, s);
+                       w.eoff, w.boff, p->tokens, p->hidden, p->experts, p->topk, w.rep_fp4, w.lin_sf, w.c_map, s,
+                       &w.ga);
   launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
-                        (int64_t)p->tokens * p->topk, w.rep_sf, s);
+                        (int64_t)p->tokens * p->topk, w.rep_sf, s, w.ga.row_token, w.ga.flag, w.ga.tok_sf,
+                        p->tokens);
   if ((rc = cuda_check("permute_quant"))) return rc;
   const int sms = num_sms();
-  GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, args->w1_fp4, args->w1_sf, args->w1_alphas, args->a2_gscale,
-                             w.int_fp4, w.int_sf);
+  GemmLaunch g1 = w13_gather_launch(p, w, w.ga.tok_fp4, w.rep_fp4, w.rep_sf, args->w1_fp4, args->w1_sf,
+                                    args->w1_alphas, args->a2_gscale, w.int_fp4, w.int_sf);
   if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "forward: gemm_w13 launch failed");
   GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, args->w2_fp4, args->w2_sf, args->w2_alphas, w.c3);
   if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "forward: gemm_w2 launch failed");
@@ -563,15 +602,17 @@ int reaxmoe_forward_prequant(const reaxmoe_forward_args* args, const void* a_sca
   const WS w = carve(workspace, L);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = do_plan(p, args->topk_ids, w, nullptr, nullptr, s))) return rc;
+  // gather layout: the GEMM and the scale swizzle read the caller's token rows in place through the slot map
   launch_permute_fp4(static_cast<const uint8_t*>(args->a), static_cast<const uint8_t*>(a_scales), a_gscale,
                      args->a1_gscale, args->topk_ids, w.seg_base, w.eoff, p->tokens, p->hidden, p->experts, p->topk,
-                     w.rep_fp4, w.lin_sf, w.c_map, w.status, s);
+                     w.rep_fp4, w.lin_sf, w.c_map, w.status, s, &w.ga);
   launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
-                        (int64_t)p->tokens * p->topk, w.rep_sf, s);
+                        (int64_t)p->tokens * p->topk, w.rep_sf, s, w.ga.row_token, w.ga.flag,
+                        static_cast<const uint8_t*>(a_scales), p->tokens);
   if ((rc = cuda_check("permute_fp4"))) return rc;
   const int sms = num_sms();
-  GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, args->w1_fp4, args->w1_sf, args->w1_alphas, args->a2_gscale,
-                             w.int_fp4, w.int_sf);
+  GemmLaunch g1 = w13_gather_launch(p, w, args->a, w.rep_fp4, w.rep_sf, args->w1_fp4, args->w1_sf, args->w1_alphas,
+                                    args->a2_gscale, w.int_fp4, w.int_sf);
   if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "forward_prequant: gemm_w13 launch failed");
   GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, args->w2_fp4, args->w2_sf, args->w2_alphas, w.c3);
   if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "forward_prequant: gemm_w2 launch failed");

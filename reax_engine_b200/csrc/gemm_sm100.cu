@@ -23,7 +23,12 @@
 //               n-tiles, and the ring stages (36 KiB) carry B and its scale atoms only. Each slice has its own
 //               full / empty barrier pair: the next m-tile's slice is loaded as soon as the last n-tile's MMAs on it
 //               are done (measured at config 2: w2 0.567 -> 0.548 ms).
-//   warp 1      allocates 512 TMEM columns (warps 2-3 idle); one thread issues tcgen05.mma.kind::mxf4nvf4.block_scale.block16
+//   warps 2-3   gather layout (w13 when every expert quantises its input with the same scale): the A tile of each
+//               stage by 16-byte cp.async from token-major FP4 rows through the slot -> token map, written in the
+//               128-byte-swizzled layout a TMA box gives, then one cp.async arrive per thread on the stage's full
+//               barrier. The routed rows are then never replicated in HBM (the reference's gather-A variant,
+//               blink_moegemm.cu:532-647, reads its A rows through a_map the same way). Idle otherwise.
+//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.mma.kind::mxf4nvf4.block_scale.block16
 //               (M=128, N=256, K=64; 4 per stage) into the fp32 accumulator and commits each stage to its empty
 //               barrier (which frees the stage's shared memory and its scale columns in TMEM).
 //   warps 4-7   scale writers, one per TMEM lane quarter: each lane reads one 16-byte row of every scale atom of the
@@ -66,6 +71,8 @@ constexpr int STAGES = 4;
 // Launched with 128 registers a thread; warpgroups 0 and 1 hand registers to the epilogue with setmaxnreg
 // (2 x 128 x 56 + 2 x 128 x 200 = 65536, the launch's total).
 constexpr int SCALE_WARP0 = 4;
+constexpr int GA_WARP0 = 2;             // gather layout: warps 2-3 fetch the A rows by cp.async
+constexpr int GA_THREADS = 64;
 constexpr int EPI_WARP0 = 8;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int THREADS = (EPI_WARP0 + NUM_EPI_WARPS) * 32;
@@ -81,7 +88,8 @@ constexpr int SFB_COL = SFA_COL + STAGES * 4 * KPS;   // B scales of stage s: co
 constexpr int RA_SLICES = 3;
 constexpr int RA_BYTES = RA_SLICES * (A_BYTES + SFA_BYTES);
 constexpr int NUM_BARS = 3 * STAGES + 3 + 2 * RA_SLICES;
-constexpr int SMEM_TABLE_INTS = 4 * (kMaxExperts + 1);
+constexpr int GA_ROWS_INTS = 128;        // gather layout: the current item's 128 A source rows
+constexpr int SMEM_TABLE_INTS = 4 * (kMaxExperts + 1) + GA_ROWS_INTS;
 template <bool RA>
 struct Layout {
   static constexpr int stage = RA ? B_BYTES + SFB_BYTES : STAGE_BYTES;  // bytes of one ring stage
@@ -121,6 +129,14 @@ struct Params {
   unsigned long long timeout_ns;
   const uint64_t* direct_dst;  // mode 0: per slot row, its record's return address (0 = write c3)
   const float* direct_w;
+  // gather layout (mode 1): A rows from ga_tok [ga_tokens, K/2] through row_token when *ga_flag is set, else from the
+  // per-slot rows ga_rep [slots, K/2]
+  const uint8_t* ga_tok;
+  const uint8_t* ga_rep;
+  const int* row_token;
+  const int* ga_flag;
+  int64_t ga_tokens;
+  int64_t slots;
   int topk;
   int E, N, K, n_tiles, k_chunks, n_blocks;
   int tail_n;           // width of the last n-tile (256, or 128 when N % 256 == 128)
@@ -249,8 +265,9 @@ __device__ __forceinline__ uint32_t act_quant32(const uint32_t (&x0)[32], const 
   return sbytes;
 }
 
-template <int MODE, int ACT, bool RA>
+template <int MODE, int ACT, bool RA, bool GA>
 __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_constant__ Params p) {
+  static_assert(!(GA && RA), "the gather layout uses the ring for A");
   using L = Layout<RA>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -270,6 +287,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
   int* s_cnt = s_tp + (kMaxExperts + 1);
   int* s_eoff = s_cnt + (kMaxExperts + 1);
   int* s_boff = s_eoff + (kMaxExperts + 1);
+  uint32_t* s_garows = reinterpret_cast<uint32_t*>(s_boff + (kMaxExperts + 1));   // [8 r0][16 i]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -284,7 +302,8 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&full[s]), 1);
+      // gather layout: the producer's expect-tx arrive plus one cp.async arrive per gathering thread
+      mbar_init(smem_u32(&full[s]), GA ? 1 + GA_THREADS : 1);
       mbar_init(smem_u32(&empty[s]), 1);
       mbar_init(smem_u32(&sff[s]), 4);
     }
@@ -372,6 +391,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
               uint8_t* sfb_st = st + L::sfb_off;
               if constexpr (RA) {
                 mbar_expect_tx(bar, (uint32_t)B_BYTES + sf_bytes * (b1 ? 2u : 1u));
+              } else if constexpr (GA) {
+                // the A tile comes from the gathering warps
+                mbar_expect_tx(bar, (uint32_t)B_BYTES + sf_bytes * (b1 ? 3u : 2u));
+                bulk_load(smem_u32(st + A_BYTES + B_BYTES), sfa + (size_t)kc0 * SF_ATOM, sf_bytes, bar);
               } else {
                 mbar_expect_tx(bar, (uint32_t)(A_BYTES + B_BYTES) + sf_bytes * (b1 ? 3u : 2u));
                 tma_load_2d(smem_u32(st), &p.tmA, bar, kc0 * (KSTEP / 2), M.row0);
@@ -418,6 +441,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
                 break;
               }
               tc_fence_after();
+              if constexpr (GA) fence_proxy_async_smem();   // A was written by cp.async (generic proxy)
               const uint32_t st = smem_u32(ring + stage * L::stage);
               const uint32_t a_s = RA ? smem_u32(smem + ks * A_BYTES) : st;
               const uint32_t b_s = st + L::b_off;
@@ -438,6 +462,70 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
         tc_commit(smem_u32(drain_mma));
         wait_drain(smem_u32(drain_mma), 0);
       }
+    } else if (GA && warp >= GA_WARP0 && warp < GA_WARP0 + GA_THREADS / 32) {
+      // ------------------------------------------------------------------ A gather (gather layout, warps 2-3)
+      // Each stage's A tile, 128 rows x 128 bytes, by 16-byte cp.async into the 128-byte-swizzled layout a TMA load
+      // would give (16-byte piece c of row r at r * 128 + (c ^ (r % 8)) * 16). Thread g takes piece g % 8 of rows
+      // g / 8 + 8 i: one warp instruction reads four whole 128-byte row slices. The item's source rows are looked up
+      // once per work item into a shared table ([g / 8][i], filled by the eight lanes that share g / 8, in their
+      // own warp) and read back per stage. A row past the m-tile's routed rows repeats its first row (the epilogue
+      // drops it); source rows are clamped to the array.
+      constexpr int RPT = BM / 8;                                // rows per thread
+      const int g = threadIdx.x - GA_WARP0 * 32;
+      const int piece = g & 7, r0 = g >> 3;
+      const bool from_tok = *p.ga_flag != 0;
+      const uint8_t* base = from_tok ? p.ga_tok : p.ga_rep;
+      const int64_t nrows = from_tok ? p.ga_tokens : p.slots;
+      const uint32_t rb = (uint32_t)(p.K / 2);
+      const uint32_t dpiece = (uint32_t)((piece ^ r0) << 4);   // r % 8 == r0 for every row of this thread
+      uint32_t* rows_tab = s_garows + r0 * RPT;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
+        const MTile M = decode_mtile(item_mtile(u), E, s_tp, s_cnt, s_eoff, s_boff);
+        __syncwarp();   // the previous item's table reads are done
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int i = 2 * piece + j;
+          const int r = r0 + 8 * i;
+          const int64_t slot = (int64_t)M.row0 + (r < M.rows ? r : 0);
+          const int64_t v = from_tok ? (int64_t)__ldg(p.row_token + slot) : slot;
+          rows_tab[i] = (uint32_t)(v < 0 ? 0 : (v >= nrows ? nrows - 1 : v));
+        }
+        __syncwarp();
+        for (int nt = item_nt0(u), nt_end = nt + item_nts(u); nt < nt_end && ok; ++nt) {
+          for (int ks = 0; ks < k_stages; ++ks) {
+            const int kc0 = ks * KPS;
+            const int nk = min(KPS, k_chunks - kc0);
+            bool free_slot = false;
+            if (lane == 0)
+              free_slot = wait_bounded(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.status, p.timeout_ns);
+            if (__shfl_sync(0xffffffffu, free_slot ? 1 : 0, 0) == 0) {
+              ok = false;
+              break;
+            }
+            const uint32_t st = smem_u32(ring + stage * L::stage) + (uint32_t)(r0 * 128) + dpiece;
+            if (piece < 2 * nk) {
+              const uint8_t* col = base + kc0 * (KSTEP / 2) + piece * 16;
+#pragma unroll
+              for (int q = 0; q < RPT / 4; ++q) {
+                const uint4 sr = *reinterpret_cast<const uint4*>(rows_tab + 4 * q);
+                cp_async_16(st + (uint32_t)((4 * q + 0) * 8 * 128), col + (uint64_t)sr.x * rb);
+                cp_async_16(st + (uint32_t)((4 * q + 1) * 8 * 128), col + (uint64_t)sr.y * rb);
+                cp_async_16(st + (uint32_t)((4 * q + 2) * 8 * 128), col + (uint64_t)sr.z * rb);
+                cp_async_16(st + (uint32_t)((4 * q + 3) * 8 * 128), col + (uint64_t)sr.w * rb);
+              }
+            }
+            cp_async_arrive_noinc(smem_u32(&full[stage]));
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+      cp_async_wait_all();
     } else if (warp >= SCALE_WARP0 && warp < EPI_WARP0) {
       // ------------------------------------------------------------------ scale writers (one warp per lane quarter)
       // A stage's TMEM scale columns are free once its previous MMAs completed; the producer waited for that (the
@@ -612,9 +700,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
 }
 
 // ---------------------------------------------------------------- host side
-template <int MODE, int ACT, bool RA>
+template <int MODE, int ACT, bool RA, bool GA = false>
 static int launch_ra(const Params& prm, int grid, cudaStream_t s) {
-  auto kfn = grouped_gemm_kernel<MODE, ACT, RA>;
+  auto kfn = grouped_gemm_kernel<MODE, ACT, RA, GA>;
   constexpr int smem = Layout<RA>::smem;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return REAXMOE_ERR_CUDA;
@@ -625,6 +713,10 @@ template <int MODE, int ACT>
 static int launch_t(const Params& prm, int grid, bool ra, cudaStream_t s) {
   if (ra) return launch_ra<MODE, ACT, true>(prm, grid, s);
   return launch_ra<MODE, ACT, false>(prm, grid, s);
+}
+template <int ACT>
+static int launch_ga(const Params& prm, int grid, cudaStream_t s) {
+  return launch_ra<1, ACT, false, true>(prm, grid, s);
 }
 
 }  // namespace gemm
@@ -654,6 +746,12 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   prm.direct_dst = g.mode == 0 ? g.direct_dst : nullptr;
   prm.direct_w = g.direct_w;
   prm.topk = g.topk;
+  prm.ga_tok = static_cast<const uint8_t*>(g.a_tok);
+  prm.ga_rep = static_cast<const uint8_t*>(g.a);
+  prm.row_token = g.row_token;
+  prm.ga_flag = g.ga_flag;
+  prm.ga_tokens = g.tokens;
+  prm.slots = g.slots;
   prm.E = g.E;
   prm.N = g.N;
   prm.K = g.K;
@@ -669,6 +767,12 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   // (m-tile, n-tile) units, keeps the 4-deep ring of A and B: a resident slice would only be reused by one n-tile.
   const bool ra = (prm.k_chunks + KPS - 1) / KPS <= RA_SLICES && g.slots / BM >= 2 * (int64_t)grid;
   if (g.mode == 0) return launch_t<0, 0>(prm, grid, ra, s);
+  if (g.row_token != nullptr) {
+    // gather layout: A through the slot -> token map, in the ring (never resident)
+    if (g.ga_flag == nullptr || g.tokens < 1) return REAXMOE_ERR_BAD_SHAPE;
+    if (g.act == REAXMOE_ACT_GELU_TANH) return launch_ga<REAXMOE_ACT_GELU_TANH>(prm, grid, s);
+    return launch_ga<REAXMOE_ACT_SILU>(prm, grid, s);
+  }
   if (g.act == REAXMOE_ACT_GELU_TANH) return launch_t<1, REAXMOE_ACT_GELU_TANH>(prm, grid, ra, s);
   return launch_t<1, REAXMOE_ACT_SILU>(prm, grid, ra, s);
 }

@@ -350,16 +350,25 @@ constexpr int kQuantCtasPerSm = 3;
 // uniform scale) with the bf16x2 quantiser, then stored to every slot: FP4 bytes into the slot's row, scale bytes
 // into the slot's row of the linear scale buffer (full-sector stores; the atoms are written from it by
 // swizzle_scales_kernel).
+// Gather layout (tok_fp4 != nullptr): when every expert has the same input scale, the quantised row is the same for
+// all of a token's slots, so it is stored once, token-major: FP4 bytes into tok_fp4 [m, H/2] and scale bytes into
+// tok_sf [m, H/16]; row_token[slot] = token lets the w13 GEMM and the scale swizzle fetch a slot's row by its token.
+// *ga_flag (written by CTA 0) records which layout was written: 1 token-major, 0 per slot (scales differ).
 __global__ void __launch_bounds__(256, kQuantCtasPerSm) quant_scatter_kernel(
     const __nv_bfloat16* __restrict__ a, const float* __restrict__ a1_gscale, const int* __restrict__ ids,
     const int* __restrict__ c_map, int m, int H, int E, int k, uint8_t* __restrict__ rep_fp4,
-    uint8_t* __restrict__ lin_sf) {
+    uint8_t* __restrict__ lin_sf, uint8_t* __restrict__ tok_fp4, uint8_t* __restrict__ tok_sf,
+    int* __restrict__ row_token, int* __restrict__ ga_flag) {
   __shared__ float gq[kMaxExperts];
   __shared__ int sl_pos[8][kMaxTopk];           // per warp: the current token's slots
   __shared__ float sl_g[8][kMaxTopk];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int e = threadIdx.x; e < E; e += blockDim.x) gq[e] = __fdiv_rn(1.0f, a1_gscale[e]);
   __syncthreads();
+  bool same = true;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) same = same && __float_as_uint(gq[e]) == __float_as_uint(gq[0]);
+  const bool ga = __syncthreads_and(same ? 1 : 0) != 0 && tok_fp4 != nullptr;
+  if (tok_fp4 != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *ga_flag = ga ? 1 : 0;
   const int units = H / 32;
   const int k16 = H / 16;
   const int nwarps = gridDim.x * (blockDim.x >> 5);
@@ -373,6 +382,29 @@ __global__ void __launch_bounds__(256, kQuantCtasPerSm) quant_scatter_kernel(
 #pragma unroll
         for (int i = 0; i < 4; ++i) raw[it][i] = __ldg(src + un * 4 + i);
       }
+    }
+    if (ga) {
+      if (lane < k) {
+        const int pos = c_map[(int64_t)t * k + lane];
+        if (pos >= 0) row_token[pos] = (int)t;
+      }
+      const float g = gq[0];
+#pragma unroll
+      for (int it = 0; it < kPermUnits; ++it) {
+        const int un = lane + 32 * it;
+        if (un >= units) continue;
+        uint32_t w[4];
+        uint32_t sb = 0u;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const uint4 q0 = raw[it][2 * b], q1 = raw[it][2 * b + 1];
+          const uint32_t xw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          sb |= quant_block16_bf16(xw, g, w[2 * b], w[2 * b + 1]) << (8 * b);
+        }
+        *reinterpret_cast<uint4*>(tok_fp4 + (int64_t)t * (H / 2) + un * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint16_t*>(tok_sf + (int64_t)t * k16 + un * 2) = (uint16_t)sb;
+      }
+      continue;
     }
     if (lane < k) {
       const int64_t pair = (int64_t)t * k + lane;
@@ -415,13 +447,15 @@ __global__ void __launch_bounds__(256, kQuantCtasPerSm) quant_scatter_kernel(
 // norm + quantise upstream, e.g. add + RMSNorm + quant in one kernel as engine/fp4_triton.py:68-90 does): each slot
 // receives a byte copy of its token's FP4 row and linear scale row. The copy is exact only if every slot's expert
 // quantises with the scale the rows were made with (a1_gscale[e] == in_gscale); a slot whose expert differs flags
-// REAXMOE_ERR_UNSUPPORTED in the status word and is copied all the same.
+// REAXMOE_ERR_UNSUPPORTED in the status word and is copied all the same. Gather layout (row_token != nullptr): no
+// copies; row_token[slot] = token, and the w13 GEMM and the scale swizzle read the token rows in place.
 // ------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) permute_fp4_kernel(
     const uint8_t* __restrict__ a_fp4, const uint8_t* __restrict__ a_sf, float in_gscale,
     const float* __restrict__ a1_gscale, const int* __restrict__ ids, const int* __restrict__ seg_base,
     const int* __restrict__ eoff, int m, int H, int E, int k, uint8_t* __restrict__ rep_fp4,
-    uint8_t* __restrict__ lin_sf, int* __restrict__ c_map, int* status) {
+    uint8_t* __restrict__ lin_sf, int* __restrict__ c_map, int* status, int* __restrict__ row_token,
+    int* __restrict__ ga_flag) {
   __shared__ int run[kMaxExperts];
   __shared__ uint32_t mask[kMaxExperts];
   __shared__ int pos_s[kSegTokens * kMaxTopk];
@@ -437,6 +471,17 @@ __global__ void __launch_bounds__(256) permute_fp4_kernel(
   __syncthreads();
   if (warp == 0) segment_slots(ids, t0, nt, k, E, run, mask, pos_s, exp_s, c_map);
   __syncthreads();
+  if (row_token != nullptr) {
+    // gather layout: the token rows stay where they are; each slot records its token
+    if (seg == 0 && threadIdx.x == 0) *ga_flag = 1;
+    for (int i = threadIdx.x; i < nt * k; i += blockDim.x) {
+      const int e = exp_s[i];
+      if (e < 0) continue;
+      row_token[pos_s[i]] = (int)(t0 + i / k);
+      if (a1_gscale[e] != in_gscale) set_status(status, REAXMOE_ERR_UNSUPPORTED);
+    }
+    return;
+  }
   const int row16 = H / 32;          // 16-byte pieces of an FP4 row
   const int sf16 = H / 256;          // 16-byte pieces of a linear scale row
   constexpr int kMaxRow = 4;         // H <= 4096: <= 128 pieces, 4 per lane
@@ -468,6 +513,8 @@ __global__ void __launch_bounds__(256) permute_fp4_kernel(
 // of the 128x4 layout (blockscale_offsets[e] / 128 == tile_prefix[e]). Reads the tile's rows of the linear scale
 // buffer [slots, H/16] (contiguous) into shared memory and writes its H/64 atoms of 512 bytes with 16-byte stores
 // (atom row i = the 4 scale bytes of rows i, i+32, i+64, i+96). Rows past the expert's count are written as zero.
+// Gather layout (row_map != nullptr and *ga_flag set): the scale rows are read from the token-major buffer tok
+// [tokens, H/16], row r of the tile from token row_map[slot]; otherwise from lin.
 // ------------------------------------------------------------------------------------------------------
 constexpr int kSwzMaxWords = 128 * (48 + 1);   // 128 rows x (H/64 <= 48 words + 1 pad word)
 
@@ -475,7 +522,10 @@ __global__ void __launch_bounds__(256) swizzle_scales_kernel(const uint8_t* __re
                                                              const int* __restrict__ tile_prefix,
                                                              const int* __restrict__ counts,
                                                              const int* __restrict__ eoff, int E, int H,
-                                                             uint8_t* __restrict__ sf) {
+                                                             uint8_t* __restrict__ sf,
+                                                             const int* __restrict__ row_map,
+                                                             const int* __restrict__ ga_flag,
+                                                             const uint8_t* __restrict__ tok, int tok_rows) {
   __shared__ uint32_t tile[kSwzMaxWords];
   const int gm = blockIdx.x;
   if (gm >= tile_prefix[E]) return;
@@ -492,7 +542,22 @@ __global__ void __launch_bounds__(256) swizzle_scales_kernel(const uint8_t* __re
   // vector loads: 16 bytes when a row of H/16 scale bytes is a multiple of 16 (H % 256 == 0), else 8 bytes (H is a
   // multiple of 128); stored as words at the odd stride
   const uint8_t* src = lin + ((int64_t)eoff[e] + mt * 128) * (H / 16);
-  if (k64 % 4 == 0) {
+  if (row_map != nullptr && *ga_flag != 0) {
+    // gather layout: row r of the tile is token row_map[slot] of the token-major scale rows
+    const int* rm = row_map + eoff[e] + mt * 128;
+    const int k128 = k64 / 2;
+    for (int i = threadIdx.x; i < 128 * k128; i += blockDim.x) {
+      const int r = i / k128, c = (i - r * k128) * 2;
+      uint2 v = make_uint2(0u, 0u);
+      if (r < rows) {
+        const int t = min(max(__ldg(rm + r), 0), tok_rows - 1);   // clamped: never outside the token rows
+        v = __ldg(reinterpret_cast<const uint2*>(tok + (int64_t)t * (H / 16)) + (i - r * k128));
+      }
+      uint32_t* d = tile + r * stride + c;
+      d[0] = v.x;
+      d[1] = v.y;
+    }
+  } else if (k64 % 4 == 0) {
     const int k256 = k64 / 4;
     for (int i = threadIdx.x; i < 128 * k256; i += blockDim.x) {
       const int r = i / k256, c = (i - r * k256) * 4;
@@ -523,10 +588,12 @@ __global__ void __launch_bounds__(256) swizzle_scales_kernel(const uint8_t* __re
 }
 
 int launch_swizzle_scales(const uint8_t* lin, const int* tile_prefix, const int* counts, const int* eoff, int E, int H,
-                          int64_t slots, uint8_t* sf, cudaStream_t s) {
+                          int64_t slots, uint8_t* sf, cudaStream_t s, const int* row_map, const int* ga_flag,
+                          const uint8_t* tok_sf, int tok_rows) {
   if (slots == 0) return 0;
   const int64_t max_tiles = slots / 128 + E + 1;
-  swizzle_scales_kernel<<<(unsigned)max_tiles, 256, 0, s>>>(lin, tile_prefix, counts, eoff, E, H, sf);
+  swizzle_scales_kernel<<<(unsigned)max_tiles, 256, 0, s>>>(lin, tile_prefix, counts, eoff, E, H, sf, row_map,
+                                                            ga_flag, tok_sf, tok_rows);
   return 0;
 }
 
@@ -762,7 +829,7 @@ int launch_plan(const int* seg_counts, int nseg, int E, int* seg_base, int* coun
 
 int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const int* seg_base,
                          const int* eoff, const int* boff, int m, int H, int E, int k, uint8_t* rep_fp4,
-                         uint8_t* lin_sf, int* c_map, cudaStream_t s) {
+                         uint8_t* lin_sf, int* c_map, cudaStream_t s, const GatherRows* ga) {
   (void)boff;
   if (m == 0) return 0;
   const int nseg = (int)ceil_div64(m, kSegTokens);
@@ -771,18 +838,21 @@ int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const i
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   assign_slots_kernel<<<nseg, 32, 0, s>>>(ids, seg_base, eoff, m, E, k, c_map);
   const int64_t want = ceil_div64(m, 8), cap = (int64_t)kQuantCtasPerSm * sms;
-  quant_scatter_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, s>>>(a, a1_gscale, ids, c_map, m, H, E, k,
-                                                                          rep_fp4, lin_sf);
+  quant_scatter_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, s>>>(
+      a, a1_gscale, ids, c_map, m, H, E, k, rep_fp4, lin_sf, ga ? ga->tok_fp4 : nullptr, ga ? ga->tok_sf : nullptr,
+      ga ? ga->row_token : nullptr, ga ? ga->flag : nullptr);
   return 0;
 }
 
 int launch_permute_fp4(const uint8_t* a_fp4, const uint8_t* a_sf, float in_gscale, const float* a1_gscale,
                        const int* ids, const int* seg_base, const int* eoff, int m, int H, int E, int k,
-                       uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, int* status, cudaStream_t s) {
+                       uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, int* status, cudaStream_t s,
+                       const GatherRows* ga) {
   const int nseg = (int)ceil_div64(m, kSegTokens);
   if (nseg > 0)
     permute_fp4_kernel<<<nseg, 256, 0, s>>>(a_fp4, a_sf, in_gscale, a1_gscale, ids, seg_base, eoff, m, H, E, k,
-                                            rep_fp4, lin_sf, c_map, status);
+                                            rep_fp4, lin_sf, c_map, status, ga ? ga->row_token : nullptr,
+                                            ga ? ga->flag : nullptr);
   return 0;
 }
 

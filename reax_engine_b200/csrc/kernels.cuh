@@ -15,11 +15,22 @@ int launch_plan(const int* seg_counts, int nseg, int E, int* seg_base, int* coun
                 int* tile_prefix, int* ps1, int* ps2, int n1, int k1, int n2, int k2, cudaStream_t s);
 // The permute kernels write scale bytes to a linear buffer lin_sf [slots, H/16]; launch_swizzle_scales then writes
 // the 128x4 atoms of every m-tile (needs the plan's tile_prefix / counts / expert_offsets).
+// The gather layout of the w13 A operand: token-major FP4 rows and scale rows, quantised once per token, and the
+// slot -> token map through which the GEMM and the scale swizzle read them. flag (one int, written by the permute
+// stage) says whether the token-major layout was written (1) or, because the experts' input scales differ, the
+// per-slot rows (0).
+struct GatherRows {
+  uint8_t* tok_fp4;   // [tokens, H/2]
+  uint8_t* tok_sf;    // [tokens, H/16]
+  int* row_token;     // [slots]
+  int* flag;
+};
 int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const int* ids, const int* seg_base,
                          const int* eoff, const int* boff, int m, int H, int E, int k, uint8_t* rep_fp4,
-                         uint8_t* lin_sf, int* c_map, cudaStream_t s);
+                         uint8_t* lin_sf, int* c_map, cudaStream_t s, const GatherRows* ga = nullptr);
 int launch_swizzle_scales(const uint8_t* lin, const int* tile_prefix, const int* counts, const int* eoff, int E, int H,
-                          int64_t slots, uint8_t* sf, cudaStream_t s);
+                          int64_t slots, uint8_t* sf, cudaStream_t s, const int* row_map = nullptr,
+                          const int* ga_flag = nullptr, const uint8_t* tok_sf = nullptr, int tok_rows = 0);
 int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
                    __nv_bfloat16* out, int num_sms, cudaStream_t s);
 int launch_quantize(const void* x, bool f32, int64_t rows, int cols, int group_rows, const float* gscale,
@@ -100,6 +111,12 @@ struct GemmLaunch {
   const float* q_gscale;
   int* status;
   unsigned long long timeout_ns;
+  // mode 1, gather layout (row_token != nullptr): A rows are read through the slot -> token map from a_tok
+  // [tokens, K/2] when *ga_flag is set, else from the per-slot rows at `a` (the permute stage decides)
+  const void* a_tok;
+  const int* row_token;
+  const int* ga_flag;
+  int64_t tokens;
   // mode 0, expert-parallel receiver: slot rows whose direct_dst is non-zero are written as the record's finished
   // row, bf16(bf16(alpha * acc) * bf16(direct_w)) (+0 normalised when topk > 1, as the combine's sum does), at
   // direct_dst (a peer's return buffer over NVLink) instead of c3
@@ -138,6 +155,7 @@ int launch_rmsnorm_nvfp4(const void* a, const void* b, const void* w, const void
                          int cols, float gscale, void* out, uint8_t* packed, uint8_t* scales, cudaStream_t s);
 int launch_permute_fp4(const uint8_t* a_fp4, const uint8_t* a_sf, float in_gscale, const float* a1_gscale,
                        const int* ids, const int* seg_base, const int* eoff, int m, int H, int E, int k,
-                       uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, int* status, cudaStream_t s);
+                       uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, int* status, cudaStream_t s,
+                       const GatherRows* ga = nullptr);
 
 }  // namespace reaxmoe

@@ -51,6 +51,20 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm,
       : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only), and the arrive on an mbarrier once all of this thread's
+// earlier cp.async copies have landed (.noinc: the arrive counts toward the barrier's expected arrivals)
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// orders this thread's view of shared memory written by the generic proxy before later async-proxy reads
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // the same load with an L2 eviction-priority policy (from l2_evict_first / l2_evict_last)
 __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* tm, uint32_t bar, int x, int y,
                                                  uint64_t policy) {

@@ -312,9 +312,15 @@ def read_status(workspace: torch.Tensor, clear: bool = True) -> int:
 class Stages:
     """Stage-by-stage calls of the layer on caller-owned buffers (the per-stage C-ABI entry points), for parity
     tests and per-kernel timing. Buffers follow vLLM's layout: rep rows [m*topk, k/2], scale atoms over
-    blockscale_offsets, int rows [m*topk, n/2], c3 bf16 [m*topk, k]."""
+    blockscale_offsets, int rows [m*topk, n/2], c3 bf16 [m*topk, k].
 
-    def __init__(self, m: int, hidden: int, inter: int, experts: int, topk: int, activation, device):
+    ``gather=True`` runs the permute and the w13 GEMM in the gather layout that ``run_moe_nvfp4`` uses: when every
+    expert has the same input scale, each token row is quantised once into the workspace and w13 reads its A rows
+    through the slot -> token map (``rep_fp4`` is then not written)."""
+
+    def __init__(self, m: int, hidden: int, inter: int, experts: int, topk: int, activation, device,
+                 gather: bool = False):
+        self.gather = gather
         self.act = MoEActivation.parse(activation)
         self.p = L.problem(m, hidden, inter, experts, topk, int(self.act))
         self.m, self.hidden, self.inter, self.experts, self.topk = m, hidden, inter, experts, topk
@@ -349,17 +355,20 @@ class Stages:
 
     def permute_quant(self, a: torch.Tensor, a1_gscale: torch.Tensor):
         self._a1 = a1_gscale.float().contiguous()
+        rep = None if self.gather else self.rep_fp4.data_ptr()
         L.check(L.lib().reaxmoe_permute_quant(ctypes.byref(self.p), a.contiguous().data_ptr(), self._a1.data_ptr(),
-                                              self.ids.data_ptr(), self.ws.data_ptr(), self._wsb(),
-                                              self.rep_fp4.data_ptr(), self.rep_sf.data_ptr(), self.c_map.data_ptr(),
-                                              self._s()))
+                                              self.ids.data_ptr(), self.ws.data_ptr(), self._wsb(), rep,
+                                              self.rep_sf.data_ptr(), self.c_map.data_ptr(), self._s()))
 
     def gemm_w13(self, w1p: torch.Tensor, w1p_sf: torch.Tensor, w1_alphas: torch.Tensor, a2_gscale: torch.Tensor,
                  rep_fp4: torch.Tensor | None = None, rep_sf: torch.Tensor | None = None):
         self._al1, self._a2 = w1_alphas.float().contiguous(), a2_gscale.float().contiguous()
-        rf = self.rep_fp4 if rep_fp4 is None else rep_fp4
+        if rep_fp4 is not None:
+            rf = rep_fp4.data_ptr()
+        else:
+            rf = None if self.gather else self.rep_fp4.data_ptr()
         rs = self.rep_sf if rep_sf is None else rep_sf
-        L.check(L.lib().reaxmoe_gemm_w13(ctypes.byref(self.p), rf.data_ptr(), rs.data_ptr(), w1p.data_ptr(),
+        L.check(L.lib().reaxmoe_gemm_w13(ctypes.byref(self.p), rf, rs.data_ptr(), w1p.data_ptr(),
                                          w1p_sf.data_ptr(), self._al1.data_ptr(), self._a2.data_ptr(),
                                          self.ws.data_ptr(), self._wsb(), self.int_fp4.data_ptr(),
                                          self.int_sf.data_ptr(), self._s()))

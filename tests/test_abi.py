@@ -39,7 +39,10 @@ def test_workspace_size_matches_layout():
     n = R.workspace_size(m, H, I, E, k)
     slots = m * k
     sfblk = slots // 128 + E + 1
-    expect_min = slots * (H // 2 + H // 16 + I // 2 + 2 * H + 4) + sfblk * (H // 64 + I // 64) * 512
+    # per slot: replicated rows + linear scales, intermediate rows, c3, c_map, slot -> token map; per token: the
+    # token-major FP4 rows and scales of the gather layout; scale atoms of A and of the intermediate
+    expect_min = (slots * (H // 2 + H // 16 + I // 2 + 2 * H + 4 + 4) + m * (H // 2 + H // 16)
+                  + sfblk * (H // 64 + I // 64) * 512)
     assert expect_min <= n <= expect_min + 64 * 1024 + 2 * ((m + 127) // 128) * E * 4 + 4096
 
 
