@@ -46,7 +46,7 @@ EP_TRANSPORT = "p2p"    # expert-parallel exchange: "nccl" (two all-to-alls) or 
 NOMINAL_FP4_TFLOPS = 9000.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the one-pass ncu capture of the default
 # workload summarised in profiles/dram_traffic_cfg2.md; None where no capture covers the workload.
-NCU_TRAFFIC = {"cfg2": {"gemm_w13": 849_161_984, "gemm_w2": 1_814_097_664, "permute_quant": 603_705_600,
+NCU_TRAFFIC = {"cfg2": {"gemm_w13": 610_893_056, "gemm_w2": 1_814_784_768, "permute_quant": 245_481_984,
                         "combine": 1_794_828_800}}
 
 
