@@ -36,8 +36,9 @@ MID = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])            # engine/
 def e2m1_codes(q: torch.Tensor) -> torch.Tensor:
     """q already scaled into [-6, 6] -> uint8 codes (sign << 3 | index), ties to the even index (fp4.py:27-36)."""
     a = q.abs()
-    idx = torch.bucketize(a, MID, right=False)
-    on_mid = (idx < 7) & (a == MID[idx.clamp(max=6)])
+    mid = MID.to(q.device)
+    idx = torch.bucketize(a, mid, right=False)
+    on_mid = (idx < 7) & (a == mid[idx.clamp(max=6)])
     idx = torch.where(on_mid & (idx % 2 == 1), idx + 1, idx)
     return ((q < 0).to(torch.uint8) << 3) | idx.to(torch.uint8)
 
@@ -46,7 +47,7 @@ def quantize(x: torch.Tensor, g: torch.Tensor) -> tuple[torch.Tensor, torch.Tens
     """NVFP4 rows x [M, K] with per-row dequant-side global scale g [M] (or a scalar) -> (packed uint8 [M, K/2],
     linear e4m3 block scales uint8 [M, K/16]) with the numerics of engine/fp4.py:45-51."""
     M, K = x.shape
-    g = torch.as_tensor(g, dtype=torch.float32).reshape(-1, 1).expand(M, 1)
+    g = torch.as_tensor(g, dtype=torch.float32, device=x.device).reshape(-1, 1).expand(M, 1)
     blk = x.float().view(M, K // 16, 16)
     bamax = blk.abs().amax(-1)
     s = (bamax / (6.0 * g)).clamp(max=448.0).to(torch.float8_e4m3fn)
@@ -72,22 +73,22 @@ BYTE_VALUES = _byte_values()
 def dequant(packed: torch.Tensor, s8: torch.Tensor) -> torch.Tensor:
     """packed [M, K/2] uint8 + linear e4m3 scales [M, K/16] -> float32 [M, K] = e2m1 value * e4m3 scale."""
     M = packed.shape[0]
-    v = BYTE_VALUES[packed.to(torch.int64)].view(M, -1, 16)
+    v = BYTE_VALUES.to(packed.device)[packed.to(torch.int64)].view(M, -1, 16)
     s = s8.view(torch.float8_e4m3fn).float()
     return (v * s[..., None]).view(M, -1)
 
 
-def atom_offsets(rows: int, k16: int) -> torch.Tensor:
+def atom_offsets(rows: int, k16: int, device=None) -> torch.Tensor:
     """Byte offset of scale (row, 16-element block) in the 128x4 atoms of engine/fp4.py:16-24, [rows, k16]."""
     cb = -(-k16 // 4)
-    r = torch.arange(rows)[:, None]
-    c = torch.arange(k16)[None, :]
+    r = torch.arange(rows, device=device)[:, None]
+    c = torch.arange(k16, device=device)[None, :]
     return ((r // 128) * cb + c // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + (c % 4)
 
 
 def unswizzle(flat: torch.Tensor, rows: int, k16: int) -> torch.Tensor:
     """The 128x4 scale atoms of one matrix of `rows` rows -> linear [rows, k16] bytes."""
-    return flat.reshape(-1)[atom_offsets(rows, k16)]
+    return flat.reshape(-1)[atom_offsets(rows, k16, flat.device)]
 
 
 def route(logits: torch.Tensor, topk: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -122,16 +123,18 @@ def quantize_weights(w: torch.Tensor, experts_per_chunk: int = 8) -> tuple[torch
 class ReferenceMoE:
     """The layer's weights as the reference holds them (engine/fp4.py layout: per expert fp4 [N, K/2], 128x4 scale
     atoms, fp32 global scale), with the per-expert dequantised fp32 matrices a CPU engine would keep after loading
-    the model (built once, outside any timed region)."""
+    the model (built once, outside any timed region). Runs on the device its weight tensors are on: the CPU for the
+    timed baseline, a GPU (fp32 matmuls, TF32 off) for the full-size output checks of the tests."""
 
     def __init__(self, w1q, w1s, w2q, w2s, w1_alphas, w2_alphas, a1_gscale, a2_gscale, activation: str):
         E, N1, H2 = w1q.shape
         self.E, self.H, self.I = E, 2 * H2, N1 // 2
         self.act = activation
-        self.w1_alphas = torch.as_tensor(w1_alphas, dtype=torch.float32)
-        self.w2_alphas = torch.as_tensor(w2_alphas, dtype=torch.float32)
-        self.g1 = 1.0 / torch.as_tensor(a1_gscale, dtype=torch.float32)
-        self.g2 = 1.0 / torch.as_tensor(a2_gscale, dtype=torch.float32)
+        dev = w1q.device
+        self.w1_alphas = torch.as_tensor(w1_alphas, dtype=torch.float32, device=dev)
+        self.w2_alphas = torch.as_tensor(w2_alphas, dtype=torch.float32, device=dev)
+        self.g1 = 1.0 / torch.as_tensor(a1_gscale, dtype=torch.float32, device=dev)
+        self.g2 = 1.0 / torch.as_tensor(a2_gscale, dtype=torch.float32, device=dev)
         H, I = self.H, self.I
         self.w1 = [dequant(w1q[e], unswizzle(w1s[e], N1, H // 16)) for e in range(E)]   # model load, untimed
         self.w2 = [dequant(w2q[e], unswizzle(w2s[e], H, I // 16)) for e in range(E)]
@@ -152,7 +155,7 @@ class ReferenceMoE:
         flat = topk_ids.reshape(-1).to(torch.int64)
         order = torch.argsort(flat, stable=True)
         counts = torch.bincount(flat, minlength=self.E).tolist()
-        c3 = torch.empty(T * k, self.H, dtype=torch.bfloat16)
+        c3 = torch.empty(T * k, self.H, dtype=torch.bfloat16, device=x.device)
         uniform = bool((self.g1 == self.g1[0]).all())
         a_all = dequant(*quantize(x, self.g1[0])) if uniform else None
         r0 = 0
