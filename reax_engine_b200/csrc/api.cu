@@ -779,13 +779,17 @@ static int ep_expert_forward(const reaxmoe_problem* local, const void* recv_reco
   const int rec_bytes = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
   launch_ep_unpack_meta(rec, p->tokens, p->topk, p->hidden, rec_bytes, lid, lw, s);
   if ((rc = do_plan(p, lid, w, nullptr, nullptr, s))) return rc;
+  // gather layout: w13 and the scale swizzle read each slot's FP4 row and scale row inside its record
   launch_ep_permute(rec, lid, w.seg_base, w.eoff, p->tokens, p->hidden, p->experts, p->topk, rec_bytes, w.rep_fp4,
-                    w.lin_sf, w.c_map, s);
+                    w.lin_sf, w.c_map, s, &w.ga);
   launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
-                        (int64_t)p->tokens * p->topk, w.rep_sf, s);
+                        (int64_t)p->tokens * p->topk, w.rep_sf, s, w.ga.row_token, w.ga.flag, rec + p->hidden / 2,
+                        p->tokens, rec_bytes);
   if ((rc = cuda_check("ep_permute"))) return rc;
   const int sms = num_sms();
-  GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4, w.int_sf);
+  GemmLaunch g1 = w13_gather_launch(p, w, rec, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4,
+                                    w.int_sf);
+  g1.tok_stride = rec_bytes;
   if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "%s: gemm_w13 launch failed", who);
   GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, w2_fp4, w2_sf, w2_alphas, w.c3);
   if (route != nullptr && route->skip_single) {
@@ -872,13 +876,17 @@ int reaxmoe_ep_expert_gemms(const reaxmoe_problem* local, const void* recv_recor
   const int rec_bytes = (int)reaxmoe_ep_record_bytes(p->hidden, p->topk);
   launch_ep_unpack_meta(rec, p->tokens, p->topk, p->hidden, rec_bytes, lid, lw, s);
   if ((rc = do_plan(p, lid, w, nullptr, nullptr, s))) return rc;
+  // gather layout: w13 and the scale swizzle read each slot's FP4 row and scale row inside its record
   launch_ep_permute(rec, lid, w.seg_base, w.eoff, p->tokens, p->hidden, p->experts, p->topk, rec_bytes, w.rep_fp4,
-                    w.lin_sf, w.c_map, s);
+                    w.lin_sf, w.c_map, s, &w.ga);
   launch_swizzle_scales(w.lin_sf, w.tile_prefix, w.counts, w.eoff, p->experts, p->hidden,
-                        (int64_t)p->tokens * p->topk, w.rep_sf, s);
+                        (int64_t)p->tokens * p->topk, w.rep_sf, s, w.ga.row_token, w.ga.flag, rec + p->hidden / 2,
+                        p->tokens, rec_bytes);
   if ((rc = cuda_check("ep_expert_gemms permute"))) return rc;
   const int sms = sm_limit > 0 && sm_limit < num_sms() ? sm_limit : num_sms();
-  GemmLaunch g1 = w13_launch(p, w, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4, w.int_sf);
+  GemmLaunch g1 = w13_gather_launch(p, w, rec, w.rep_fp4, w.rep_sf, w1_fp4, w1_sf, w1_alphas, a2_gscale, w.int_fp4,
+                                    w.int_sf);
+  g1.tok_stride = rec_bytes;
   if ((rc = launch_grouped_gemm(g1, sms, s))) return fail(rc, "ep_expert_gemms: gemm_w13 launch failed");
   GemmLaunch g2 = w2_launch(p, w, w.int_fp4, w.int_sf, w2_fp4, w2_sf, w2_alphas, w.c3);
   if ((rc = launch_grouped_gemm(g2, sms, s))) return fail(rc, "ep_expert_gemms: gemm_w2 launch failed");

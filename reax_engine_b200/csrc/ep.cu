@@ -213,7 +213,8 @@ __global__ void __launch_bounds__(256) ep_permute_kernel(const uint8_t* __restri
                                                          const int* __restrict__ seg_base, const int* __restrict__ eoff,
                                                          int n, int H, int El, int k, int rec_bytes,
                                                          uint8_t* __restrict__ rep_fp4, uint8_t* __restrict__ lin_sf,
-                                                         int* __restrict__ c_map) {
+                                                         int* __restrict__ c_map, int* __restrict__ row_token,
+                                                         int* __restrict__ ga_flag) {
   __shared__ int run[kMaxExperts];
   __shared__ uint32_t mask[kMaxExperts];
   __shared__ int pos_s[kSegTokens * kMaxTopk];
@@ -229,6 +230,13 @@ __global__ void __launch_bounds__(256) ep_permute_kernel(const uint8_t* __restri
   __syncthreads();
   if (warp == 0) segment_slots(lid, t0, nt, k, El, run, mask, pos_s, exp_s, c_map);
   __syncthreads();
+  if (row_token != nullptr) {
+    // gather layout: the records stay where they landed; each slot records its record
+    if (seg == 0 && threadIdx.x == 0) *ga_flag = 1;
+    for (int i = threadIdx.x; i < nt * k; i += blockDim.x)
+      if (exp_s[i] >= 0) row_token[pos_s[i]] = (int)(t0 + i / k);
+    return;
+  }
   const int units = H / 32;
   const int k16 = H / 16;
   const int nwarps = blockDim.x >> 5;
@@ -380,11 +388,12 @@ int launch_ep_unpack_meta(const uint8_t* records, int n, int k, int H, int rec_b
 }
 
 int launch_ep_permute(const uint8_t* records, const int* lid, const int* seg_base, const int* eoff, int n, int H,
-                      int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, cudaStream_t s) {
+                      int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, cudaStream_t s,
+                      const GatherRows* ga) {
   const int nseg = (int)ceil_div64(n, kSegTokens);
   if (nseg > 0)
     ep_permute_kernel<<<nseg, 256, 0, s>>>(records, lid, seg_base, eoff, n, H, El, k, rec_bytes, rep_fp4, lin_sf,
-                                           c_map);
+                                           c_map, ga ? ga->row_token : nullptr, ga ? ga->flag : nullptr);
   return 0;
 }
 

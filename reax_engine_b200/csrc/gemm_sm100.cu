@@ -136,6 +136,7 @@ struct Params {
   const int* row_token;
   const int* ga_flag;
   int64_t ga_tokens;
+  int64_t ga_stride;    // bytes between consecutive gathered rows (K/2, or the expert-parallel record size)
   int64_t slots;
   int topk;
   int E, N, K, n_tiles, k_chunks, n_blocks;
@@ -476,7 +477,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_gemm_kernel(const __grid_c
       const bool from_tok = *p.ga_flag != 0;
       const uint8_t* base = from_tok ? p.ga_tok : p.ga_rep;
       const int64_t nrows = from_tok ? p.ga_tokens : p.slots;
-      const uint32_t rb = (uint32_t)(p.K / 2);
+      const uint32_t rb = (uint32_t)(from_tok ? p.ga_stride : p.K / 2);
       const uint32_t dpiece = (uint32_t)((piece ^ r0) << 4);   // r % 8 == r0 for every row of this thread
       uint32_t* rows_tab = s_garows + r0 * RPT;
       int stage = 0;
@@ -751,6 +752,7 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   prm.row_token = g.row_token;
   prm.ga_flag = g.ga_flag;
   prm.ga_tokens = g.tokens;
+  prm.ga_stride = g.tok_stride > 0 ? g.tok_stride : g.K / 2;
   prm.slots = g.slots;
   prm.E = g.E;
   prm.N = g.N;
@@ -769,7 +771,8 @@ int launch_grouped_gemm(const GemmLaunch& g, int num_sms, cudaStream_t s) {
   if (g.mode == 0) return launch_t<0, 0>(prm, grid, ra, s);
   if (g.row_token != nullptr) {
     // gather layout: A through the slot -> token map, in the ring (never resident)
-    if (g.ga_flag == nullptr || g.tokens < 1) return REAXMOE_ERR_BAD_SHAPE;
+    if (g.ga_flag == nullptr || g.tokens < 1 || (g.tok_stride > 0 && (g.tok_stride % 16 != 0 || g.tok_stride < g.K / 2)))
+      return REAXMOE_ERR_BAD_SHAPE;
     if (g.act == REAXMOE_ACT_GELU_TANH) return launch_ga<REAXMOE_ACT_GELU_TANH>(prm, grid, s);
     return launch_ga<REAXMOE_ACT_SILU>(prm, grid, s);
   }

@@ -513,8 +513,9 @@ __global__ void __launch_bounds__(256) permute_fp4_kernel(
 // of the 128x4 layout (blockscale_offsets[e] / 128 == tile_prefix[e]). Reads the tile's rows of the linear scale
 // buffer [slots, H/16] (contiguous) into shared memory and writes its H/64 atoms of 512 bytes with 16-byte stores
 // (atom row i = the 4 scale bytes of rows i, i+32, i+64, i+96). Rows past the expert's count are written as zero.
-// Gather layout (row_map != nullptr and *ga_flag set): the scale rows are read from the token-major buffer tok
-// [tokens, H/16], row r of the tile from token row_map[slot]; otherwise from lin.
+// Gather layout (row_map != nullptr and *ga_flag set): the scale rows are read from the token-major rows of tok
+// (tok_stride bytes apart: H/16 for packed scale rows, the record size for expert-parallel records), row r of the
+// tile from row row_map[slot]; otherwise from lin.
 // ------------------------------------------------------------------------------------------------------
 constexpr int kSwzMaxWords = 128 * (48 + 1);   // 128 rows x (H/64 <= 48 words + 1 pad word)
 
@@ -525,7 +526,8 @@ __global__ void __launch_bounds__(256) swizzle_scales_kernel(const uint8_t* __re
                                                              uint8_t* __restrict__ sf,
                                                              const int* __restrict__ row_map,
                                                              const int* __restrict__ ga_flag,
-                                                             const uint8_t* __restrict__ tok, int tok_rows) {
+                                                             const uint8_t* __restrict__ tok, int tok_rows,
+                                                             int64_t tok_stride) {
   __shared__ uint32_t tile[kSwzMaxWords];
   const int gm = blockIdx.x;
   if (gm >= tile_prefix[E]) return;
@@ -551,7 +553,7 @@ __global__ void __launch_bounds__(256) swizzle_scales_kernel(const uint8_t* __re
       uint2 v = make_uint2(0u, 0u);
       if (r < rows) {
         const int t = min(max(__ldg(rm + r), 0), tok_rows - 1);   // clamped: never outside the token rows
-        v = __ldg(reinterpret_cast<const uint2*>(tok + (int64_t)t * (H / 16)) + (i - r * k128));
+        v = __ldg(reinterpret_cast<const uint2*>(tok + (int64_t)t * tok_stride) + (i - r * k128));
       }
       uint32_t* d = tile + r * stride + c;
       d[0] = v.x;
@@ -589,11 +591,12 @@ __global__ void __launch_bounds__(256) swizzle_scales_kernel(const uint8_t* __re
 
 int launch_swizzle_scales(const uint8_t* lin, const int* tile_prefix, const int* counts, const int* eoff, int E, int H,
                           int64_t slots, uint8_t* sf, cudaStream_t s, const int* row_map, const int* ga_flag,
-                          const uint8_t* tok_sf, int tok_rows) {
+                          const uint8_t* tok_sf, int tok_rows, int64_t tok_stride) {
   if (slots == 0) return 0;
   const int64_t max_tiles = slots / 128 + E + 1;
   swizzle_scales_kernel<<<(unsigned)max_tiles, 256, 0, s>>>(lin, tile_prefix, counts, eoff, E, H, sf, row_map,
-                                                            ga_flag, tok_sf, tok_rows);
+                                                            ga_flag, tok_sf, tok_rows,
+                                                            tok_stride > 0 ? tok_stride : (int64_t)(H / 16));
   return 0;
 }
 

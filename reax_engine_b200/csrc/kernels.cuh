@@ -30,7 +30,8 @@ int launch_permute_quant(const __nv_bfloat16* a, const float* a1_gscale, const i
                          uint8_t* lin_sf, int* c_map, cudaStream_t s, const GatherRows* ga = nullptr);
 int launch_swizzle_scales(const uint8_t* lin, const int* tile_prefix, const int* counts, const int* eoff, int E, int H,
                           int64_t slots, uint8_t* sf, cudaStream_t s, const int* row_map = nullptr,
-                          const int* ga_flag = nullptr, const uint8_t* tok_sf = nullptr, int tok_rows = 0);
+                          const int* ga_flag = nullptr, const uint8_t* tok_sf = nullptr, int tok_rows = 0,
+                          int64_t tok_stride = 0);
 int launch_combine(const __nv_bfloat16* c3, const int* c_map, const float* w, int m, int H, int k,
                    __nv_bfloat16* out, int num_sms, cudaStream_t s);
 int launch_quantize(const void* x, bool f32, int64_t rows, int cols, int group_rows, const float* gscale,
@@ -47,7 +48,8 @@ int launch_ep_pack(const __nv_bfloat16* a, const float* a1_gscale, const int* id
 int launch_ep_unpack_meta(const uint8_t* records, int n, int k, int H, int rec_bytes, int* lid, float* lw,
                           cudaStream_t s);
 int launch_ep_permute(const uint8_t* records, const int* lid, const int* seg_base, const int* eoff, int n, int H,
-                      int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, cudaStream_t s);
+                      int El, int k, int rec_bytes, uint8_t* rep_fp4, uint8_t* lin_sf, int* c_map, cudaStream_t s,
+                      const GatherRows* ga = nullptr);
 int launch_ep_combine(const __nv_bfloat16* ret, const int* map, int m, int H, int k, __nv_bfloat16* out, int num_sms,
                       cudaStream_t s);
 
@@ -117,6 +119,7 @@ struct GemmLaunch {
   const int* row_token;
   const int* ga_flag;
   int64_t tokens;
+  int64_t tok_stride;   // bytes between consecutive rows of a_tok (0: K/2, packed rows)
   // mode 0, expert-parallel receiver: slot rows whose direct_dst is non-zero are written as the record's finished
   // row, bf16(bf16(alpha * acc) * bf16(direct_w)) (+0 normalised when topk > 1, as the combine's sum does), at
   // direct_dst (a peer's return buffer over NVLink) instead of c3
