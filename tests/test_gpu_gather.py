@@ -95,3 +95,19 @@ def test_forward_uses_gather_layout_and_matches_stages():
                     c["w2s"], c["w2_alphas"], w, ids, "gelu_tanh")
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+def test_forward_falls_back_when_input_scales_differ():
+    """reaxmoe_forward with experts whose input scales differ: the per-slot fallback inside the workspace gives the
+    staged per-slot chain's output exactly."""
+    import reax_engine_b200 as R
+    T, H, E, k, inter = 1500, 2816, 32, 4, 704
+    c = make_case(T, H, E, k, inter, "gelu_tanh", seed=15)
+    a1 = c["a1_gscale"] * torch.linspace(0.5, 2.0, E, device="cuda")
+    w, ids = R.route(None, c["logits"], k)
+    _, ref = _chain(R, c, w, ids, a1, False)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    R.run_moe_nvfp4(out, c["x"], a1, c["w1q"], c["w1s"], c["w1_alphas"], c["a2_gscale"], c["w2q"], c["w2s"],
+                    c["w2_alphas"], w, ids, "gelu_tanh")
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
