@@ -175,3 +175,19 @@ def test_p2p_entry_points_reject_bad_args():
                                             None) == L.ERR_MISALIGNED
     assert L.lib().reaxmoe_ipc_alloc(0, ctypes.byref(ctypes.c_void_p()), None) == L.ERR_NULL
     assert L.lib().reaxmoe_ep_signal_bytes() >= 512 + 4 * 64 * 64
+
+
+def test_gather_layout_staged_calls_still_need_scale_atoms():
+    """The staged gather layout (rep_fp4 == NULL) keeps the A-scale atoms: rep_sf stays required in both calls."""
+    lib = L.lib()
+    prob = L.problem(16, 256, 256, 8, 2, 0)
+    n = lib.reaxmoe_workspace_size(ctypes.byref(prob))
+    buf = ctypes.create_string_buffer(n + 256)
+    ws = (ctypes.addressof(buf) + 255) & ~255
+    dummy = ctypes.create_string_buffer(4096 + 16)
+    d = (ctypes.addressof(dummy) + 15) & ~15
+    # a, a1_gscale, topk_ids, workspace, bytes, rep_fp4 = NULL, rep_sf = NULL, c_map, stream
+    assert lib.reaxmoe_permute_quant(ctypes.byref(prob), d, d, d, ws, n, None, None, d, None) == L.ERR_NULL
+    # rep_fp4 = NULL (gather layout), rep_sf = NULL
+    assert lib.reaxmoe_gemm_w13(ctypes.byref(prob), None, None, d, d, d, d, ws, n, d, d, None) == L.ERR_NULL
+    assert "NULL" in L.last_error()
